@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Benchmark: one OrthoCache decode layer (score -> compact -> attend) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (N = 1): configuration 1 of the baseline — GQA decode, batch 1,
+32 query heads / 8 KV heads, head_dim 128, bf16, 65,536-token KV cache
+(128 blocks of 512), 75 % union eviction, synthetic seeded keys (smooth /
+noise block mixture), values N(0,1), queries N(0, 1/sqrt(128)).  τ is
+calibrated per layer for the eviction target, ζ_max = 5.
+
+A step is one decode layer: the fused scorer reads all keys, the compaction
+emits the retained block list, the split-KV attention reads the retained K
+and V blocks.  The KV caches of 4 layers (1.07 GB) rotate across steps, so
+every step reads data that left L2 three steps earlier.
+
+N > 1 (torchrun, one rank per GPU, NCCL): sequence-parallel decode with a
+65,536-token shard per GPU (weak scaling; configuration 3 at N = 8).  Each
+rank scores, compacts and attends over its own shard, producing partial
+(max, sum, output) per query head; the partials (32 x 130 floats per rank)
+are all-gathered over NVLink and merged in log-sum-exp form.  No KV block
+crosses NVLink.
+
+Prints one JSON line (rank 0).  The value is µs per decode layer for the
+whole job (lower is better).
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode attn µs/layer @64K ctx 75% evict (incl. scoring); scorer HBM GB/s vs peak"
+UNIT = "us/layer"
+S_SHARD, HQ, HKV, D = 65536, 32, 8, 128
+ZETA_MAX = 5.0
+LAYERS = 4
+FALLBACK_HBM = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--evict", type=float, default=0.75)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+class Clocks:
+    """Sample SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+class Layer:
+    pass
+
+
+def make_layers(rank, evict, device):
+    import torch
+    from orthocache_b200 import synthetic as syn, score_blocks
+    nb = S_SHARD // 512
+    layers = []
+    for l in range(LAYERS):
+        seed = 1000 * rank + l
+        L = Layer()
+        L.kinds = syn.block_kinds(nb, evict, seed=seed)
+        L.k = syn.make_keys(nb, HKV, D, L.kinds, seed=seed, device=device)
+        L.v = syn.make_values(S_SHARD, HKV, D, seed=seed, device=device)
+        L.q = syn.make_queries(1, HQ, D, seed=seed, device=device)
+        sc = score_blocks(L.k, L.q, want=("zeta", "bound_max"))
+        L.tau, L.kept = syn.calibrate_tau(sc["zeta"], sc["bound_max"], ZETA_MAX, evict)
+        layers.append(L)
+    torch.cuda.synchronize()
+    return layers
+
+
+class Engine:
+    """Device buffers and the three C-ABI calls of one decode layer."""
+
+    def __init__(self, layers, device, world):
+        import torch
+        from orthocache_b200 import _lib
+        self.torch, self.lib, self.layers, self.world = torch, _lib, layers, world
+        nb = S_SHARD // 512
+        self.nb = nb
+        self.keep = torch.empty((nb, HKV), dtype=torch.uint8, device=device)
+        self.perm = torch.empty((nb,), dtype=torch.int32, device=device)
+        self.count = torch.empty((1,), dtype=torch.int32, device=device)
+        self.out = torch.empty((1, HQ, D), dtype=torch.bfloat16, device=device)
+        self.ws_bytes = _lib.query("oc_indirect_attention_workspace_bytes", 1, 1, HQ, HKV, D, 512, nb)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
+        rows = HQ
+        self.m = torch.empty((rows,), dtype=torch.float32, device=device)
+        self.l = torch.empty((rows,), dtype=torch.float32, device=device)
+        self.o = torch.empty((rows, D), dtype=torch.float32, device=device)
+        self.gm = torch.empty((world, rows), dtype=torch.float32, device=device)
+        self.gl = torch.empty((world, rows), dtype=torch.float32, device=device)
+        self.go = torch.empty((world, rows, D), dtype=torch.float32, device=device)
+        self.stream = torch.cuda.current_stream().cuda_stream
+        self.launches_per_step = 4 if world == 1 else 5
+
+    def score(self, L, q=None):
+        _l = self.lib
+        q = L.q if q is None else q
+        _l.call("oc_score_blocks", _l.ptr(L.k), _l.ptr(q), 1, 1, S_SHARD, HKV, D, 1, HQ,
+                1, 64, 64, 256, 256, 512, L.tau, ZETA_MAX,
+                None, None, None, None, None, None, None, _l.ptr(self.keep), 0, self.stream)
+
+    def compact(self):
+        _l = self.lib
+        _l.call("oc_stream_compact", _l.ptr(self.keep), 1, self.nb, HKV, _l.ptr(self.perm), _l.ptr(self.count),
+                self.stream)
+
+    def attend(self, L, q=None):
+        _l = self.lib
+        q = L.q if q is None else q
+        if self.world == 1:
+            _l.call("oc_indirect_attention", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, _l.ptr(self.perm), self.nb, 0,
+                    _l.ptr(self.count), 1, 0, 1, 1, HQ, HKV, D, S_SHARD, 512, self.nb, _l.ptr(self.out), 1,
+                    _l.ptr(self.ws), self.ws_bytes, self.stream)
+            return
+        import torch.distributed as dist
+        _l.call("oc_partial_attention", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, _l.ptr(self.perm), self.nb, 0,
+                _l.ptr(self.count), 1, 0, 1, 1, HQ, HKV, D, S_SHARD, 512, self.nb, _l.ptr(self.m), _l.ptr(self.l),
+                _l.ptr(self.o), _l.ptr(self.ws), self.ws_bytes, self.stream)
+        dist.all_gather_into_tensor(self.gm, self.m)
+        dist.all_gather_into_tensor(self.gl, self.l)
+        dist.all_gather_into_tensor(self.go, self.o)
+        _l.call("oc_merge_partials", _l.ptr(self.gm), _l.ptr(self.gl), _l.ptr(self.go), self.world, HQ, D,
+                _l.ptr(self.out), 1, self.stream)
+
+    def step(self, L, ev=None):
+        if ev is not None:
+            ev[0].record()
+        self.score(L)
+        if ev is not None:
+            ev[1].record()
+        self.compact()
+        if ev is not None:
+            ev[2].record()
+        self.attend(L)
+        if ev is not None:
+            ev[3].record()
+
+
+# ---------------------------------------------------------------------------
+# CPU port of the reference path (baseline leg and --impl reference)
+# ---------------------------------------------------------------------------
+def cpu_port_time(L, min_seconds=10.0, max_reps=20):
+    """Time the reference's decode layer on the host cores (oracle/oc_port.c,
+    OpenMP on all cores) on a full layer; returns (median µs, threads, reps)."""
+    import numpy as np
+    import torch
+    from oracle import port
+    bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+    kb, vb, qb = bits(L.k), bits(L.v), bits(L.q)
+    port.decode(kb, vb, qb, L.tau, ZETA_MAX)  # warm-up
+    ts = []
+    t_end = time.perf_counter() + min_seconds
+    while len(ts) < 3 or (time.perf_counter() < t_end and len(ts) < max_reps):
+        t0 = time.perf_counter()
+        port.decode(kb, vb, qb, L.tau, ZETA_MAX)
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts) * 1e6, port.threads(), len(ts)
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path (the C port, all host threads), rank 0 only."""
+    if rank != 0:
+        return
+    import torch
+    from orthocache_b200 import synthetic as syn
+    from oracle import oc_oracle as O, port
+    import numpy as np
+    nb = S_SHARD // 512
+    torch.manual_seed(0)
+    kinds = syn.block_kinds(nb, args.evict, seed=0)
+    L = Layer()
+    L.k = syn.make_keys(nb, HKV, D, kinds, seed=0, device="cpu")
+    L.v = syn.make_values(S_SHARD, HKV, D, seed=0, device="cpu")
+    L.q = syn.make_queries(1, HQ, D, seed=0, device="cpu")
+    sc = O.score_blocks(L.q.float().numpy(), L.k.float().numpy(), -1e30, ZETA_MAX)
+    L.tau, _ = syn.calibrate_tau(torch.tensor(sc["zeta"]), torch.tensor(sc["bound_max"]), ZETA_MAX, args.evict)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    kb, vb, qb = bits(L.k), bits(L.v), bits(L.q)
+    steps = max(1, min(args.steps, 200))
+    for _ in range(max(1, min(args.warmup, 5))):
+        port.decode(kb, vb, qb, L.tau, ZETA_MAX)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        port.decode(kb, vb, qb, L.tau, ZETA_MAX)
+    us = (time.perf_counter() - t0) / steps * 1e6
+    cores = port.threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(us, 2), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config1: GQA decode B=1, Hq=32/Hkv=8, D=128, S=65536, evict=%.2f" % args.evict,
+                   "layers": 1, "l2": "host run"},
+        "cpu_baseline": {"value": round(us, 2), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "full layer (65536 tokens) per step; reference JAX CPU path unavailable "
+                                   "(jax not installed), C/OpenMP port of its algorithm timed instead"},
+        "e2e": {"value": round(us, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    layers = make_layers(rank, args.evict, device)
+    eng = Engine(layers, device, world)
+    nb = S_SHARD // 512
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up: at least W steps and at least 0.5 s so clocks settle
+    t_w = time.perf_counter()
+    i = 0
+    while i < args.warmup or time.perf_counter() - t_w < 0.5:
+        eng.step(layers[i % LAYERS])
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local_rank) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for s in range(K):
+            eng.step(layers[s % LAYERS], evs[s])
+        stop.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(stop) / K
+    t_score = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    t_comp = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    t_attn = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # ---- end to end through the public API, host buffers ----
+    from orthocache_b200 import _lib  # noqa: F401
+    q_host = [L.q.cpu().pin_memory() for L in layers]
+    q_dev = torch.empty_like(layers[0].q)
+    out_host = torch.empty((1, HQ, D), dtype=torch.bfloat16).pin_memory()
+    cnt_host = torch.empty((1,), dtype=torch.int32).pin_memory()
+    Ke = max(8, min(K, 2000))
+    for s in range(4):
+        q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
+        eng.score(layers[s % LAYERS], q_dev); eng.compact(); eng.attend(layers[s % LAYERS], q_dev)
+        out_host.copy_(eng.out, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(Ke):
+        L = layers[s % LAYERS]
+        q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
+        eng.score(L, q_dev)
+        eng.compact()
+        eng.attend(L, q_dev)
+        out_host.copy_(eng.out, non_blocking=True)
+        cnt_host.copy_(eng.count, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / Ke
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    # correctness guard on the last step: retained count matches the calibration
+    assert int(cnt_host[0]) == layers[(Ke - 1) % LAYERS].kept, "retained block count changed"
+
+    if rank != 0:
+        return
+    hbm, peak_kind = peaks()
+    k_bytes = S_SHARD * HKV * D * 2
+    kept = statistics.mean(L.kept for L in layers)
+    alg_bytes = k_bytes + kept / nb * 2 * k_bytes + HQ * D * 2 * 2
+    score_gbs = k_bytes / (t_score * 1e-3) / 1e9
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        us_cpu, cores, reps = cpu_port_time(layers[0])
+        cpu = {"value": round(us_cpu, 2), "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"one full layer of this workload (layer 0), median of {reps} runs; C/OpenMP port of "
+                         "the reference's compute_multiband_mask + compaction + online-softmax loop"}
+    line = {
+        "metric": METRIC, "value": round(ms * 1e3, 3), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config1: GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens per GPU "
+                               "(%d total), evict=%.2f, zeta_max=5" % (S_SHARD, S_SHARD * world, args.evict),
+                   "l2": "inputs > L2: 4 layers of KV (1.07 GB) rotate per step",
+                   "parallelism": "single GPU" if world == 1 else f"sequence-parallel x{world}, LSE merge"},
+        "roofline": {"bound": "hbm", "kernel": "score_partial_kernel (fused scorer)",
+                     "achieved": round(score_gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(score_gbs / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+                     "bytes_per_launch": k_bytes},
+        "step_roofline": {"alg_bytes": int(alg_bytes), "achieved_gbs": round(alg_bytes / (ms * 1e-3) / 1e9, 1),
+                          "frac": round(alg_bytes / (ms * 1e-3) / 1e9 / hbm, 4)},
+        "kernel_us": {"score": round(t_score * 1e3, 2), "compact": round(t_comp * 1e3, 2),
+                      "attention": round(t_attn * 1e3, 2)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": UNIT, "h2d_bytes_per_step": HQ * D * 2,
+                "d2h_bytes_per_step": HQ * D * 2 + 4,
+                "note": "public C-ABI calls per step; q copied from pinned host, output + count read back; "
+                        "KV cache resident in HBM as in decode"},
+        "gpu_launches": K * eng.launches_per_step,
+        "clocks": clk.summary(),
+        "retained_blocks": kept,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,252 @@
+/*
+ * orthocache_b200 — C ABI of the B200 (sm_100a) OrthoCache eviction +
+ * attention hot path.
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers and sizes; the caller owns every buffer.  Tensors
+ *     are dense row-major.  Keys / values / queries are float32 (OC_F32) or
+ *     bfloat16 (OC_BF16); all arithmetic is float32.
+ *   - Layouts follow the reference's (seq, heads, dim) convention with an
+ *     optional leading batch dimension: keys/values (B, S, Hkv, D), queries
+ *     (B, Sq, Hq, D), per-block outputs (B, nb, Hkv[, D]) with nb = S / 512.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) and is asynchronous.  Counts stay on the device.
+ *   - Return 0 on success or a negative OC_ERR_* code.  Arguments are checked
+ *     on the host before anything is launched; oc_last_error() returns a
+ *     message for the calling thread's last failure.
+ *   - Functions that need scratch memory take (workspace, workspace_bytes);
+ *     the matching *_workspace_bytes() query gives the size.  No entry point
+ *     allocates device memory.
+ *
+ * Reference interfaces cited as file:line of the reference project
+ * (j-arndt/orthocache v0.3.0).
+ */
+#ifndef ORTHOCACHE_B200_H
+#define ORTHOCACHE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* oc_stream_t; /* == cudaStream_t */
+
+enum oc_dtype { OC_F32 = 0, OC_BF16 = 1 };
+
+enum oc_status {
+  OC_OK = 0,
+  OC_ERR_NULL = -1,        /* a required pointer is NULL */
+  OC_ERR_SHAPE = -2,       /* inconsistent or unsupported shape */
+  OC_ERR_ALIGN = -3,       /* pointer not 16-byte aligned */
+  OC_ERR_CAPACITY = -4,    /* workspace too small / size above a limit */
+  OC_ERR_DTYPE = -5,       /* unsupported dtype */
+  OC_ERR_CUDA = -6,        /* CUDA runtime error (message has details) */
+  OC_ERR_UNSUPPORTED = -7  /* valid request this build does not implement */
+};
+
+/* Library version (major*10000 + minor*100 + patch). */
+int oc_version(void);
+/* Static description of an OC_ERR_* code. */
+const char* oc_status_string(int status);
+/* Message of the calling thread's last failure ("" if none). */
+const char* oc_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * fwht_512 — replaces `fwht_512(x)` (src/orthocache/fwht.py:4-65).
+ * x: (512, ncols) row-major, dtype `x_dtype`; y: (512, ncols) float32.
+ * Natural (Hadamard) order, 9 butterfly stages h = 1..256 in the reference's
+ * order, then an IEEE float32 division by 22.627416997969522 (fwht.py:61):
+ * bit-identical to the reference's float32 butterfly.
+ */
+int oc_fwht512(const void* x, int x_dtype, int64_t ncols, float* y, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused block scorer — replaces, in one pass over the keys,
+ *   compute_spectral_bands        (src/orthocache/spectral_energy.py:69-106)
+ *   compute_spectral_decay_ratio  (spectral_energy.py:109-138)
+ *   compute_query_aware_bounds    (spectral_energy.py:141-177), max over rows
+ *   compute_query_aware_mask      (spectral_energy.py:180-196)
+ *   compute_multiband_mask        (spectral_energy.py:199-234)
+ *
+ * keys: (B, S, Hkv, D), S % 512 == 0, D in {64, 128, 256}.
+ * q: (B, Sq, Hq, D) of the same dtype, Hq % Hkv == 0; may be NULL (then no
+ *    bound is computed and the logit gate passes every block).
+ * Bands are half-open coefficient-index ranges [lo, hi) of the natural-order
+ * WHT (reference defaults (1,64), (64,256), (256,512)).  ζ = E_high /
+ * (E_low + 1e-6).  bound_max[b,j,h] = max over the Sq*G query rows of KV
+ * head h of  q·mean_j/√D + ‖q‖·√E_AC/√D  (GQA: query head hq reads KV head
+ * hq / G, G = Hq / Hkv).  keep = (bound_max >= tau) && (zeta <= zeta_max).
+ *
+ * Outputs, each nullable: dc (B, nb, Hkv, D) = WHT coefficient 0;
+ * e_low / e_mid / e_high / zeta / bound_max (B, nb, Hkv) float32;
+ * bounds (B, Sq, nb, Hq) float32 = the bound of every query row before the
+ * max (the (seq_len_q, num_blocks, num_heads) array of
+ * compute_query_aware_bounds); keep (B, nb, Hkv) uint8 0/1.
+ *
+ * mode: 0 = automatic; 1 = the partial-transform scorer (band edges must be
+ * 0, 1 or multiples of 64); 2 = the full 9-stage butterfly scorer (any bands).
+ */
+int oc_score_blocks(const void* keys, const void* q, int dtype,
+                    int batch, int seq_len, int kv_heads, int head_dim,
+                    int q_len, int q_heads,
+                    int band_low0, int band_low1, int band_mid0, int band_mid1,
+                    int band_high0, int band_high1,
+                    float tau, float zeta_max,
+                    float* dc, float* e_low, float* e_mid, float* e_high,
+                    float* zeta, float* bound_max, float* bounds, uint8_t* keep,
+                    int mode, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Sum of squared keys per (block, head) — replaces compute_block_energy_jax
+ * (spectral_energy.py:21-35).  energy: (B, nb, H) float32.  block_size any
+ * divisor of S.
+ */
+int oc_block_energy(const void* keys, int dtype, int batch, int seq_len, int heads,
+                    int head_dim, int block_size, float* energy, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Stream compaction — replaces the index part of
+ *   compaction.stream_compact           (src/orthocache/compaction.py:28-100)
+ *   alltoallv.stream_compact            (src/orthocache/alltoallv.py:44-75)
+ *   distributed_attention.stream_compact (distributed_attention.py:31-46)
+ *   adaptive_attention.stream_compact   (adaptive_attention.py:29-40)
+ * keep: (B, nb, heads) uint8; a block is active if any head keeps it
+ * (compaction.py:65).  perm: (B, nb) int32, the stable permutation with the
+ * active blocks first in ascending order, then the inactive blocks ascending
+ * (compaction.py:76-82).  count: (B) int32 number of active blocks.
+ */
+int oc_stream_compact(const uint8_t* keep, int batch, int num_blocks, int heads,
+                      int32_t* perm, int32_t* count, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Block gather — replaces the K/V gather of compaction.stream_compact
+ * (compaction.py:85-98), alltoallv.pack_active_blocks (alltoallv.py:150-212)
+ * and distributed_attention._pack_active_blocks (distributed_attention.py:49-75).
+ * src: (B, nb_src, block_elems) elements of `dtype`; dst: (B, nb_dst,
+ * block_elems).  For i < min(count[b], nb_dst): dst[b,i] = src[b, perm[b*perm_stride+i]];
+ * for i >= count[b]: zero if zero_tail, untouched otherwise.  count may be
+ * NULL (= nb_dst).  block_elems * sizeof(dtype) must be a multiple of 16.
+ */
+int oc_gather_blocks(const void* src, int dtype, int batch, int nb_src, int64_t block_elems,
+                     const int32_t* perm, int perm_stride, const int32_t* count,
+                     void* dst, int nb_dst, int zero_tail, oc_stream_t stream);
+
+/* Inverse of oc_gather_blocks — replaces compaction.stream_decompact
+ * (compaction.py:103-154): dst is zeroed, then dst[b, perm[b*perm_stride+i]]
+ * = src[b, i] for i < count[b] (count NULL = nb_src). */
+int oc_scatter_blocks(const void* src, int dtype, int batch, int nb_src, int64_t block_elems,
+                      const int32_t* perm, int perm_stride, const int32_t* count,
+                      void* dst, int nb_dst, oc_stream_t stream);
+
+/* Bucketed block count of indirect_attention (indirect_attention.py:20-26,
+ * 150-157): out[i] = the smallest of 1, 2, 4, ..., 512 that is >= count[i]
+ * (a count above 512 is kept; 0 stays 0), clamped to cap.  The reference's
+ * Pallas kernel attends to exactly that many leading entries of the
+ * permutation, i.e. to the active blocks plus the first inactive ones up to
+ * the bucket. */
+int oc_bucket_count(const int32_t* count, int n, int cap, int32_t* out, oc_stream_t stream);
+
+/* The two gates on precomputed scores (spectral_energy.py:196, 231-234):
+ * keep[i] = (bound_max[i] >= tau) && (zeta[i] <= zeta_max).  bound_max or
+ * zeta may be NULL (that gate passes); tau_dev (nullable) is a device float
+ * that overrides tau, so a threshold computed on the device needs no host
+ * round trip. */
+int oc_apply_gates(const float* bound_max, const float* zeta, int64_t cells, const float* tau_dev,
+                   float tau, float zeta_max, uint8_t* keep, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Indirect block attention — replaces
+ *   indirect_attention.indirect_attention (src/orthocache/indirect_attention.py:127-170)
+ *   adaptive_attention._multihead_loop    (adaptive_attention.py:90-120)
+ *   distributed_attention._online_softmax_indirect_attention
+ *                                         (distributed_attention.py:78-128)
+ * Every query head attends to the tokens of blocks idx[b*idx_stride + i],
+ * i < count[b]; logits = q·k/√D in float32, softmax over all those tokens,
+ * output o / l cast to out_dtype.  count[b] == 0 gives zeros
+ * (indirect_attention.py:150-151).
+ * q (B, Sq, Hq, D); k, v (B, S, Hkv, D); out (B, Sq, Hq, D).
+ * block_size % 64 == 0 and S % block_size == 0; D in {64, 128, 256}
+ * (float32 inputs: D <= 128).  max_blocks bounds count (the number of index
+ * slots scanned).
+ * Index addressing: the index list of (batch b, kv head h) starts at
+ * idx[b*idx_stride + h*idx_head_stride] and its length is
+ * count[b*count_stride + h*count_head_stride].  The union form of the
+ * reference (one list per batch row shared by all heads) is
+ * idx_head_stride = count_head_stride = 0, count_stride = 1; per-head lists
+ * (the predicated per-head mask of sparse_attention.py:46-49) use nonzero
+ * head strides.
+ */
+size_t oc_indirect_attention_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
+                                             int head_dim, int block_size, int max_blocks);
+int oc_indirect_attention(const void* q, const void* k, const void* v, int dtype,
+                          const int32_t* idx, int idx_stride, int idx_head_stride,
+                          const int32_t* count, int count_stride, int count_head_stride,
+                          int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                          int seq_len, int block_size, int max_blocks,
+                          void* out, int out_dtype,
+                          void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * One decode step of the OrthoCache pipeline on the device: score (two-gate
+ * keep mask), compact (perm, count) and attend over the retained blocks —
+ * the path of pipeline.orthocache_forward(mode='compact')
+ * (src/orthocache/pipeline.py:33-157) with compute_multiband_mask
+ * (spectral_energy.py:199-234) feeding indirect attention instead of the K/V
+ * copy of compact_and_attend (compaction.py:157-222).
+ * Shapes as above; keep (B, nb, Hkv) uint8, perm (B, nb), count (B) are
+ * outputs; out (B, Sq, Hq, D) in out_dtype.
+ */
+size_t oc_decode_step_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
+                                      int head_dim, int seq_len);
+int oc_decode_step(const void* q, const void* k, const void* v, int dtype,
+                   int batch, int q_len, int q_heads, int kv_heads, int head_dim, int seq_len,
+                   float tau, float zeta_max,
+                   uint8_t* keep, int32_t* perm, int32_t* count,
+                   void* out, int out_dtype,
+                   void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Sequence-parallel exchange helpers (the device-side index math of
+ * distributed_attention.py:179-191, alltoallv.py:113-145 and
+ * benchmarks/phase_e_stratified.py:182-197,242-265).
+ *
+ * oc_exchange_index: all_counts (P) int32 per-device active counts; slots =
+ * blocks each device contributed to the gathered buffer.  order (P*slots)
+ * int32 = slots j with j % slots < counts[j / slots] first (ascending), then
+ * the rest; total (1) int32 = sum of counts; offsets (P) int32 (nullable) =
+ * exclusive prefix sum of counts.
+ */
+int oc_exchange_index(const int32_t* all_counts, int num_devices, int slots,
+                      int32_t* order, int32_t* total, int32_t* offsets, oc_stream_t stream);
+
+/* Stratified capacity bucket of build_stratified (phase_e_stratified.py:182-197,
+ * 262-265), computed on the host: the smallest of the four buckets
+ * max(1,nb/4), max(1,nb/2), max(1,3nb/4), nb that is >= gmax. */
+int oc_stratified_bucket(int nb_per_device, int gmax);
+
+/* Merge of per-shard partial attention (m, l, o): the log-sum-exp combine of
+ * the online softmax in distributed_attention.py:95-128 applied across
+ * shards.  m, l: (P, rows), o: (P, rows, D) float32 as written by
+ * oc_partial_attention; out (rows, D) in out_dtype; rows = B*Sq*Hq. */
+int oc_merge_partials(const float* m, const float* l, const float* o, int parts, int rows,
+                      int head_dim, void* out, int out_dtype, oc_stream_t stream);
+
+/* Partial (unnormalised) attention of one shard for the LSE merge: same
+ * arguments as oc_indirect_attention but writes m (rows), l (rows) and
+ * o (rows, D) float32, rows = B*Sq*Hq in output order; m is in log2 units of
+ * the scaled logits.  A shard with count 0 writes m = -inf, l = 0, o = 0. */
+int oc_partial_attention(const void* q, const void* k, const void* v, int dtype,
+                         const int32_t* idx, int idx_stride, int idx_head_stride,
+                         const int32_t* count, int count_stride, int count_head_stride,
+                         int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                         int seq_len, int block_size, int max_blocks,
+                         float* m, float* l, float* o,
+                         void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ORTHOCACHE_B200_H */

@@ -1,0 +1,504 @@
+// Indirect block attention over the retained blocks (decode / short query),
+// split across CTAs by (retained block, 128-token chunk, kv head) with a
+// log-sum-exp merge; and the one-call decode step (score -> compact -> attend).
+//
+// Reference semantics (j-arndt/orthocache v0.3.0):
+//   indirect_attention.indirect_attention     src/orthocache/indirect_attention.py:127-170
+//   adaptive_attention._multihead_loop        src/orthocache/adaptive_attention.py:90-120
+//   distributed_attention._online_softmax_indirect_attention
+//                                             src/orthocache/distributed_attention.py:78-128
+//   pipeline.orthocache_forward (compact)     src/orthocache/pipeline.py:33-157
+//
+// The reference walks the retained blocks one after the other with an online
+// softmax (running max m, sum l, output o).  The same algebra is split here:
+// each work item (one chunk of one retained block for one kv head and a tile
+// of query rows) produces its own (m, l, o) in a workspace, and a merge
+// kernel combines them in log-sum-exp form, o / l.  Work items are taken by a
+// persistent grid, so evicted blocks cost nothing and the number of retained
+// blocks (device-side count) never leaves the GPU.
+//
+// Logits are kept in log2 units: s = (q.k) * log2(e) / sqrt(D), p = 2^(s - m).
+#include "oc_common.cuh"
+
+#include <math.h>
+
+namespace oc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxChunk = 128;  // tokens per work item
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* idx;
+  const int32_t* count;
+  int idx_stride, idx_hstride;      // list of (b, h) starts at b*idx_stride + h*idx_hstride
+  int cnt_stride, cnt_hstride;      // its length is count[b*cnt_stride + h*cnt_hstride]
+  int B, Sq, Hq, Hkv, G, D, S, bs;
+  int R;            // query rows per kv head = Sq * G
+  int n_rt;         // row tiles
+  int chunk;        // tokens per item
+  int chunks;       // items per block
+  int max_items;    // max_blocks * chunks
+  float scale_log2; // log2(e) / sqrt(D)
+  float* ws_m;      // [B][max_items][Hkv][R]
+  float* ws_l;
+  float* ws_o;      // [B][max_items][Hkv][R][D]
+};
+
+__device__ __forceinline__ int list_len(const AttnArgs& a, int b, int h) {
+  const int n = a.count[(size_t)b * a.cnt_stride + (size_t)h * a.cnt_hstride];
+  return max(0, min(n, a.max_items / a.chunks));
+}
+
+// Work item w -> (b, item, h, rt); false when past the end.  Items are
+// ordered by (batch, item, head, row tile) for union lists (consecutive CTAs
+// read the same token rows of neighbouring heads) and by (batch, head, item,
+// row tile) for per-head lists.
+__device__ __forceinline__ bool decode_item(const AttnArgs& a, int w, int& b, int& item, int& h, int& rt) {
+  if (a.idx_hstride == 0 && a.cnt_hstride == 0) {
+    const int per_item = a.Hkv * a.n_rt;
+    for (b = 0; b < a.B; ++b) {
+      const int n = list_len(a, b, 0) * a.chunks * per_item;
+      if (w < n) {
+        item = w / per_item;
+        const int rem = w - item * per_item;
+        h = rem / a.n_rt;
+        rt = rem - h * a.n_rt;
+        return true;
+      }
+      w -= n;
+    }
+    return false;
+  }
+  for (b = 0; b < a.B; ++b)
+    for (h = 0; h < a.Hkv; ++h) {
+      const int n = list_len(a, b, h) * a.chunks * a.n_rt;
+      if (w < n) {
+        item = w / a.n_rt;
+        rt = w - item * a.n_rt;
+        return true;
+      }
+      w -= n;
+    }
+  return false;
+}
+
+template <typename T, int D, int RT>
+__global__ void __launch_bounds__(kThreads, 2)
+attn_partial_kernel(AttnArgs a) {
+  constexpr int VEC = Elem<T>::kVec;
+  constexpr int LPR = D / VEC;           // lanes per key row (one 16-byte vector each)
+  constexpr int RPW = 32 / LPR;          // rows per warp instruction
+  constexpr int ROWS_PER_WARP = kMaxChunk / kWarps;
+  constexpr int ITERS = ROWS_PER_WARP / RPW;
+  static_assert(32 % LPR == 0 && ROWS_PER_WARP % RPW == 0, "mapping");
+
+  __shared__ float s_p[RT][kMaxChunk];
+  __shared__ float s_m[RT];
+  __shared__ float s_l[RT];
+  __shared__ float s_o[kWarps][RT][D];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int sub = lane / LPR;            // which row of the warp instruction
+  const int vl = lane % LPR;             // which 16-byte vector of the row
+  const int d0 = vl * VEC;
+
+  for (int w = blockIdx.x;; w += gridDim.x) {
+    int b, item, h, rt;
+    if (!decode_item(a, w, b, item, h, rt)) break;
+    const int slot = item / a.chunks;
+    const int c = item - slot * a.chunks;
+    const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
+    const int tok0 = blk * a.bs + c * a.chunk;
+    const int r0 = rt * RT;
+    const int nr = min(RT, a.R - r0);
+    if (blk < 0 || blk >= a.S / a.bs) {
+      // Out-of-range index: this item contributes nothing (no memory access).
+      const size_t part = (((size_t)b * a.max_items + item) * a.Hkv + h) * a.R + r0;
+      for (int x = tid; x < nr * D; x += kThreads) a.ws_o[part * D + x] = 0.f;
+      if (tid < nr) { a.ws_m[part + tid] = -INFINITY; a.ws_l[part + tid] = 0.f; }
+      continue;
+    }
+
+    // Query rows of this tile in registers (this thread's VEC dims).
+    float qv[RT][VEC];
+    const T* qb = reinterpret_cast<const T*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      if (r < nr) {
+        const int row = r0 + r, s = row / a.G, g = row - s * a.G;
+        const T* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + g) * D + d0;
+        uint4 raw = *reinterpret_cast<const uint4*>(qr);
+        unpack16<T>(raw, qv[r]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) qv[r][e] *= a.scale_log2;
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) qv[r][e] = 0.f;
+      }
+    }
+
+    const size_t tok_stride = (size_t)a.Hkv * D;
+    const T* kbase = reinterpret_cast<const T*>(a.k) +
+                     (((size_t)b * a.S + tok0) * a.Hkv + h) * D + d0;
+    const T* vbase = reinterpret_cast<const T*>(a.v) +
+                     (((size_t)b * a.S + tok0) * a.Hkv + h) * D + d0;
+    const int trow0 = warp * ROWS_PER_WARP + sub;
+
+    // ---- logits: s[r][t] = q_r . k_t (scaled) ----
+    uint4 kr[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int t = trow0 + i * RPW;
+      kr[i] = t < a.chunk ? ldg_stream(kbase + (size_t)t * tok_stride) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int t = trow0 + i * RPW;
+      float kf[VEC];
+      unpack16<T>(kr[i], kf);
+#pragma unroll
+      for (int r = 0; r < RT; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc = fmaf(qv[r][e], kf[e], acc);
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (vl == 0 && t < a.chunk) s_p[r][t] = acc;
+      }
+    }
+    __syncthreads();
+
+    // ---- softmax statistics per row (one warp per row) ----
+    for (int r = warp; r < RT; r += kWarps) {
+      float m = -INFINITY;
+      for (int t = lane; t < a.chunk; t += 32) m = fmaxf(m, s_p[r][t]);
+      m = warp_max(m);
+      float l = 0.f;
+      for (int t = lane; t < a.chunk; t += 32) {
+        const float p = exp2f(s_p[r][t] - m);
+        s_p[r][t] = p;
+        l += p;
+      }
+      l = warp_sum(l);
+      if (lane == 0) { s_m[r] = m; s_l[r] = l; }
+    }
+    __syncthreads();
+
+    // ---- o[r][d] = sum_t p[r][t] v[t][d] ----
+    uint4 vr[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int t = trow0 + i * RPW;
+      vr[i] = t < a.chunk ? ldg_stream(vbase + (size_t)t * tok_stride) : make_uint4(0, 0, 0, 0);
+    }
+    float acc[RT][VEC];
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[r][e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int t = trow0 + i * RPW;
+      if (t < a.chunk) {
+        float vf[VEC];
+        unpack16<T>(vr[i], vf);
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          const float p = s_p[r][t];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[r][e] = fmaf(p, vf[e], acc[r][e]);
+        }
+      }
+    }
+    // lanes with the same vl but different sub hold the same dims
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        float x = acc[r][e];
+#pragma unroll
+        for (int o = LPR; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        acc[r][e] = x;
+      }
+    if (sub == 0) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) s_o[warp][r][d0 + e] = acc[r][e];
+    }
+    __syncthreads();
+    const size_t part = (((size_t)b * a.max_items + item) * a.Hkv + h) * a.R + r0;
+    for (int x = tid; x < nr * D; x += kThreads) {
+      const int r = x / D, d = x - r * D;
+      float s = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kWarps; ++ww) s += s_o[ww][r][d];
+      a.ws_o[(part + r) * D + d] = s;
+    }
+    if (tid < nr) {
+      a.ws_m[part + tid] = s_m[tid];
+      a.ws_l[part + tid] = s_l[tid];
+    }
+    __syncthreads();  // shared buffers are reused by the next item
+  }
+}
+
+// Combine the items of one (batch, kv head, row): M = max m_i,
+// L = sum l_i 2^(m_i - M), O = sum o_i 2^(m_i - M).  mode 0 writes O / L in
+// the output dtype at the reference's (Sq, Hq, D) position (zeros when the
+// batch row has no retained block); mode 1 writes (M, L, O) float32 for a
+// later cross-shard merge.
+template <typename TO>
+__global__ void __launch_bounds__(128)
+attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode) {
+  const int r = blockIdx.x % a.R;
+  const int h = (blockIdx.x / a.R) % a.Hkv;
+  const int b = blockIdx.x / (a.R * a.Hkv);
+  const int n = list_len(a, b, h) * a.chunks;
+  const int s = r / a.G, g = r - s * a.G;
+  const size_t orow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + g;
+  const size_t stride = (size_t)a.Hkv * a.R;
+  const size_t p0 = ((size_t)b * a.max_items * a.Hkv + h) * a.R + r;
+  float M = -INFINITY;
+  for (int i = 0; i < n; ++i) M = fmaxf(M, a.ws_m[p0 + (size_t)i * stride]);
+  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    for (int i = 0; i < n && M != -INFINITY; ++i) {
+      const size_t p = p0 + (size_t)i * stride;
+      if (a.ws_m[p] == -INFINITY) continue;
+      const float f = exp2f(a.ws_m[p] - M);
+      L = fmaf(a.ws_l[p], f, L);
+      O = fmaf(a.ws_o[p * a.D + d], f, O);
+    }
+    if (mode == 0) {
+      out[orow * a.D + d] = from_f32<TO>(L > 0.f ? O / L : 0.f);
+    } else {
+      po[orow * a.D + d] = L > 0.f ? O : 0.f;
+      if (d == 0) { pm[orow] = M; pl[orow] = L; }
+    }
+  }
+}
+
+// Cross-shard merge of (m, l, o) triples (P parts of `rows` rows).
+template <typename TO>
+__global__ void __launch_bounds__(128)
+merge_parts_kernel(const float* m, const float* l, const float* o, int P, int rows, int D, TO* out) {
+  const int r = blockIdx.x;
+  float M = -INFINITY;
+  for (int p = 0; p < P; ++p) M = fmaxf(M, m[(size_t)p * rows + r]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int p = 0; p < P; ++p) {
+        const float mp = m[(size_t)p * rows + r];
+        if (mp == -INFINITY) continue;
+        const float f = exp2f(mp - M);
+        L = fmaf(l[(size_t)p * rows + r], f, L);
+        O = fmaf(o[((size_t)p * rows + r) * D + d], f, O);
+      }
+    }
+    out[(size_t)r * D + d] = from_f32<TO>(L > 0.f ? O / L : 0.f);
+  }
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Row-tile size: query rows handled per work item (8 at most; 4 at D = 256 so
+// the per-warp reduction buffer stays within static shared memory).
+int pick_rt(int R, int D) {
+  const int rt = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
+  return D == 256 && rt > 4 ? 4 : rt;
+}
+
+int chunk_for(int bs) { return bs % 128 == 0 ? 128 : 64; }
+
+size_t attn_ws_bytes(int B, int Sq, int Hq, int Hkv, int D, int bs, int max_blocks) {
+  const int G = Hq / Hkv;
+  const size_t R = (size_t)Sq * G;
+  const size_t items = (size_t)max_blocks * (bs / chunk_for(bs));
+  const size_t parts = (size_t)B * items * Hkv * R;
+  return 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float));
+}
+
+int validate_attn(const void* q, const void* k, const void* v, int dtype, const int32_t* idx,
+                  int idx_stride, int idx_hstride, const int32_t* count, int B, int Sq, int Hq, int Hkv, int D,
+                  int S, int bs, int max_blocks) {
+  OC_REQUIRE(q && k && v && idx && count, OC_ERR_NULL, "attention: null pointer");
+  OC_REQUIRE(dtype == OC_F32 || dtype == OC_BF16, OC_ERR_DTYPE, "attention: dtype %d", dtype);
+  OC_REQUIRE(D == 64 || D == 128 || D == 256, OC_ERR_SHAPE, "attention: head_dim %d not in {64,128,256}", D);
+  OC_REQUIRE(B >= 1 && Sq >= 1 && Hkv >= 1 && Hq >= Hkv && Hq % Hkv == 0, OC_ERR_SHAPE,
+             "attention: batch %d, q_len %d, q_heads %d, kv_heads %d", B, Sq, Hq, Hkv);
+  OC_REQUIRE(bs >= 64 && bs % 64 == 0 && S % bs == 0, OC_ERR_SHAPE,
+             "attention: block_size %d must be a multiple of 64 dividing seq_len %d", bs, S);
+  OC_REQUIRE(max_blocks >= 0 && max_blocks <= S / bs, OC_ERR_SHAPE,
+             "attention: max_blocks %d > nb %d", max_blocks, S / bs);
+  OC_REQUIRE(idx_stride >= 0 && idx_hstride >= 0, OC_ERR_SHAPE, "attention: negative index stride");
+  OC_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v), OC_ERR_ALIGN, "attention: q/k/v not 16-byte aligned");
+  return OC_OK;
+}
+
+template <typename T, int D>
+int launch_partials_d(const AttnArgs& a, int rt, int grid, cudaStream_t st) {
+  if constexpr (Elem<T>::kVec * 32 < D) {
+    return set_error(OC_ERR_UNSUPPORTED, "attention: float32 inputs support head_dim <= 128");
+  } else {
+  switch (rt) {
+    case 1: attn_partial_kernel<T, D, 1><<<grid, kThreads, 0, st>>>(a); break;
+    case 2: attn_partial_kernel<T, D, 2><<<grid, kThreads, 0, st>>>(a); break;
+    case 4: attn_partial_kernel<T, D, 4><<<grid, kThreads, 0, st>>>(a); break;
+    default:
+      if constexpr (D == 256) attn_partial_kernel<T, D, 4><<<grid, kThreads, 0, st>>>(a);
+      else attn_partial_kernel<T, D, 8><<<grid, kThreads, 0, st>>>(a);
+      break;
+  }
+  return check_launch("attn_partial_kernel");
+  }
+}
+
+template <typename T>
+int launch_partials(const AttnArgs& a, int rt, int grid, cudaStream_t st) {
+  switch (a.D) {
+    case 64: return launch_partials_d<T, 64>(a, rt, grid, st);
+    case 128: return launch_partials_d<T, 128>(a, rt, grid, st);
+    default: return launch_partials_d<T, 256>(a, rt, grid, st);
+  }
+}
+
+// Enqueue the partial + merge kernels.  mode 0: final output; mode 1: (m,l,o).
+int run_attention(const void* q, const void* k, const void* v, int dtype, const int32_t* idx,
+                  int idx_stride, int idx_hstride, const int32_t* count, int cnt_stride, int cnt_hstride,
+                  int B, int Sq, int Hq, int Hkv, int D,
+                  int S, int bs, int max_blocks, void* out, int out_dtype, float* pm, float* pl,
+                  float* po, void* ws, size_t ws_bytes, int mode, cudaStream_t st) {
+  int rc = validate_attn(q, k, v, dtype, idx, idx_stride, idx_hstride, count, B, Sq, Hq, Hkv, D, S, bs,
+                         max_blocks);
+  if (rc) return rc;
+  const size_t need = attn_ws_bytes(B, Sq, Hq, Hkv, D, bs, max_blocks);
+  OC_REQUIRE(ws || need == 0, OC_ERR_NULL, "attention: workspace is NULL");
+  OC_REQUIRE(ws_bytes >= need, OC_ERR_CAPACITY, "attention: workspace %zu bytes < %zu needed", ws_bytes, need);
+  OC_REQUIRE(mode == 1 || out_dtype == OC_F32 || out_dtype == OC_BF16, OC_ERR_DTYPE,
+             "attention: out_dtype %d", out_dtype);
+  AttnArgs a;
+  a.q = q; a.k = k; a.v = v; a.idx = idx; a.count = count;
+  a.idx_stride = idx_stride; a.idx_hstride = idx_hstride;
+  a.cnt_stride = cnt_stride; a.cnt_hstride = cnt_hstride;
+  a.B = B; a.Sq = Sq; a.Hq = Hq; a.Hkv = Hkv; a.G = Hq / Hkv; a.D = D; a.S = S; a.bs = bs;
+  a.R = Sq * a.G;
+  const int rt = pick_rt(a.R, D);
+  a.n_rt = (a.R + rt - 1) / rt;
+  a.chunk = chunk_for(bs);
+  a.chunks = bs / a.chunk;
+  a.max_items = max_blocks * a.chunks;
+  a.scale_log2 = kLog2e / sqrtf((float)D);
+  const size_t parts = (size_t)B * a.max_items * Hkv * a.R;
+  char* w = static_cast<char*>(ws);
+  a.ws_m = reinterpret_cast<float*>(w);
+  a.ws_l = reinterpret_cast<float*>(w + align256(parts * sizeof(float)));
+  a.ws_o = reinterpret_cast<float*>(w + 2 * align256(parts * sizeof(float)));
+  const int64_t rows = (int64_t)B * Hkv * a.R;
+  OC_REQUIRE(rows < (1ll << 31), OC_ERR_CAPACITY, "attention: too many rows");
+
+  if (max_blocks > 0) {
+    const int grid = device_sm_count() * 2;
+    rc = dtype == OC_F32 ? launch_partials<float>(a, rt, grid, st)
+                         : launch_partials<__nv_bfloat16>(a, rt, grid, st);
+    if (rc) return rc;
+  }
+  if (mode == 0) {
+    if (out_dtype == OC_F32)
+      attn_merge_kernel<float><<<(unsigned)rows, 128, 0, st>>>(a, (float*)out, nullptr, nullptr, nullptr, 0);
+    else
+      attn_merge_kernel<__nv_bfloat16><<<(unsigned)rows, 128, 0, st>>>(a, (__nv_bfloat16*)out, nullptr,
+                                                                        nullptr, nullptr, 0);
+  } else {
+    attn_merge_kernel<float><<<(unsigned)rows, 128, 0, st>>>(a, nullptr, pm, pl, po, 1);
+  }
+  return check_launch("attn_merge_kernel");
+}
+
+}  // namespace
+}  // namespace oc
+
+using namespace oc;
+
+extern "C" size_t oc_indirect_attention_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
+                                                        int head_dim, int block_size, int max_blocks) {
+  if (batch < 1 || q_len < 1 || kv_heads < 1 || q_heads % kv_heads || block_size < 64 || block_size % 64)
+    return 0;
+  return attn_ws_bytes(batch, q_len, q_heads, kv_heads, head_dim, block_size, max_blocks);
+}
+
+extern "C" int oc_indirect_attention(const void* q, const void* k, const void* v, int dtype,
+                                     const int32_t* idx, int idx_stride, int idx_head_stride,
+                                     const int32_t* count, int count_stride, int count_head_stride,
+                                     int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                     int seq_len, int block_size, int max_blocks,
+                                     void* out, int out_dtype,
+                                     void* workspace, size_t workspace_bytes, oc_stream_t stream) {
+  OC_REQUIRE(out, OC_ERR_NULL, "oc_indirect_attention: out is NULL");
+  return run_attention(q, k, v, dtype, idx, idx_stride, idx_head_stride, count, count_stride,
+                       count_head_stride, batch, q_len, q_heads, kv_heads, head_dim,
+                       seq_len, block_size, max_blocks, out, out_dtype, nullptr, nullptr, nullptr, workspace,
+                       workspace_bytes, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int oc_partial_attention(const void* q, const void* k, const void* v, int dtype,
+                                    const int32_t* idx, int idx_stride, int idx_head_stride,
+                                    const int32_t* count, int count_stride, int count_head_stride,
+                                    int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                    int seq_len, int block_size, int max_blocks,
+                                    float* m, float* l, float* o,
+                                    void* workspace, size_t workspace_bytes, oc_stream_t stream) {
+  OC_REQUIRE(m && l && o, OC_ERR_NULL, "oc_partial_attention: m/l/o is NULL");
+  return run_attention(q, k, v, dtype, idx, idx_stride, idx_head_stride, count, count_stride,
+                       count_head_stride, batch, q_len, q_heads, kv_heads, head_dim,
+                       seq_len, block_size, max_blocks, nullptr, OC_F32, m, l, o, workspace, workspace_bytes, 1,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int oc_merge_partials(const float* m, const float* l, const float* o, int parts, int rows,
+                                 int head_dim, void* out, int out_dtype, oc_stream_t stream) {
+  OC_REQUIRE(m && l && o && out, OC_ERR_NULL, "oc_merge_partials: null pointer");
+  OC_REQUIRE(parts >= 1 && rows >= 0 && head_dim >= 1, OC_ERR_SHAPE, "oc_merge_partials: bad shape");
+  if (rows == 0) return OC_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (out_dtype == OC_F32)
+    merge_parts_kernel<float><<<rows, 128, 0, st>>>(m, l, o, parts, rows, head_dim, (float*)out);
+  else if (out_dtype == OC_BF16)
+    merge_parts_kernel<__nv_bfloat16><<<rows, 128, 0, st>>>(m, l, o, parts, rows, head_dim,
+                                                             (__nv_bfloat16*)out);
+  else
+    return set_error(OC_ERR_DTYPE, "oc_merge_partials: out_dtype %d", out_dtype);
+  return check_launch("merge_parts_kernel");
+}
+
+extern "C" size_t oc_decode_step_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
+                                                 int head_dim, int seq_len) {
+  if (seq_len % 512) return 0;
+  return oc_indirect_attention_workspace_bytes(batch, q_len, q_heads, kv_heads, head_dim, 512, seq_len / 512);
+}
+
+extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int dtype,
+                              int batch, int q_len, int q_heads, int kv_heads, int head_dim, int seq_len,
+                              float tau, float zeta_max,
+                              uint8_t* keep, int32_t* perm, int32_t* count,
+                              void* out, int out_dtype,
+                              void* workspace, size_t workspace_bytes, oc_stream_t stream) {
+  OC_REQUIRE(keep && perm && count && out, OC_ERR_NULL, "oc_decode_step: null output pointer");
+  OC_REQUIRE(seq_len % 512 == 0, OC_ERR_SHAPE, "oc_decode_step: seq_len %d not a multiple of 512", seq_len);
+  const int nb = seq_len / 512;
+  int rc = oc_score_blocks(k, q, dtype, batch, seq_len, kv_heads, head_dim, q_len, q_heads, 1, 64, 64, 256,
+                           256, 512, tau, zeta_max, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                           keep, 0, stream);
+  if (rc) return rc;
+  rc = oc_stream_compact(keep, batch, nb, kv_heads, perm, count, stream);
+  if (rc) return rc;
+  return oc_indirect_attention(q, k, v, dtype, perm, nb, 0, count, 1, 0, batch, q_len, q_heads, kv_heads, head_dim,
+                               seq_len, 512, nb, out, out_dtype, workspace, workspace_bytes, stream);
+}

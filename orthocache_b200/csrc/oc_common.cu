@@ -1,0 +1,66 @@
+// Error state, status strings and small host utilities shared by all entry points.
+#include "oc_common.cuh"
+
+#include <stdarg.h>
+#include <stdio.h>
+
+namespace oc {
+
+static thread_local char g_msg[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return set_error(OC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return OC_OK;
+}
+
+int device_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n > 0 ? n : 148;
+}
+
+}  // namespace oc
+
+extern "C" {
+
+int oc_version(void) { return 100; /* 0.1.0 */ }
+
+const char* oc_status_string(int s) {
+  switch (s) {
+    case OC_OK: return "ok";
+    case OC_ERR_NULL: return "null pointer";
+    case OC_ERR_SHAPE: return "bad shape";
+    case OC_ERR_ALIGN: return "misaligned pointer";
+    case OC_ERR_CAPACITY: return "capacity exceeded";
+    case OC_ERR_DTYPE: return "unsupported dtype";
+    case OC_ERR_CUDA: return "CUDA error";
+    case OC_ERR_UNSUPPORTED: return "unsupported";
+    default: return "unknown status";
+  }
+}
+
+const char* oc_last_error(void) { return oc::g_msg; }
+
+int oc_stratified_bucket(int nb, int gmax) {
+  if (nb <= 0) return oc::set_error(OC_ERR_SHAPE, "nb_per_device must be > 0");
+  // Buckets of build_stratified: nb/4, nb/2, 3nb/4, nb (each at least 1),
+  // deduplicated; the first that holds the global max count is chosen.
+  int b[4] = {nb / 4 > 1 ? nb / 4 : 1, nb / 2 > 1 ? nb / 2 : 1,
+              (3 * nb) / 4 > 1 ? (3 * nb) / 4 : 1, nb};
+  for (int i = 0; i < 3; ++i)
+    if (gmax <= b[i]) return b[i];
+  return b[3];
+}
+
+}  // extern "C"

@@ -1,0 +1,93 @@
+// Shared helpers for the OrthoCache sm_100a kernels: error reporting,
+// element conversion and 16-byte vector access.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/orthocache_b200.h"
+
+namespace oc {
+
+// ---------------------------------------------------------------------------
+// Error state.  Every entry point validates its arguments on the host before
+// any launch, returns an OC_ERR_* code and leaves a message retrievable with
+// oc_last_error() (thread-local, so concurrent callers do not clobber it).
+// ---------------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+int device_sm_count();
+
+#define OC_REQUIRE(cond, code, ...)                                   \
+  do {                                                                \
+    if (!(cond)) return ::oc::set_error((code), __VA_ARGS__);         \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// Element types.  Keys, values and queries arrive as float32 or bfloat16; all
+// arithmetic is float32.
+// ---------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static constexpr int kVec = 4;  // elements per 16-byte vector
+  static constexpr int kCode = OC_F32;
+};
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  static constexpr int kCode = OC_BF16;
+};
+
+// bfloat16 is the upper half of an IEEE float32: widening is a shift.
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Read-only, L1-bypassing 16-byte load for data streamed once.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Unpack one 16-byte vector into float32 lanes.
+template <typename T> __device__ __forceinline__ void unpack16(const uint4& v, float* out);
+template <> __device__ __forceinline__ void unpack16<float>(const uint4& v, float* out) {
+  out[0] = __uint_as_float(v.x); out[1] = __uint_as_float(v.y);
+  out[2] = __uint_as_float(v.z); out[3] = __uint_as_float(v.w);
+}
+template <> __device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& v, float* out) {
+  out[0] = bf16lo(v.x); out[1] = bf16hi(v.x);
+  out[2] = bf16lo(v.y); out[3] = bf16hi(v.y);
+  out[4] = bf16lo(v.z); out[5] = bf16hi(v.z);
+  out[6] = bf16lo(v.w); out[7] = bf16hi(v.w);
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace oc

@@ -1,0 +1,473 @@
+// Block scorer: Walsh–Hadamard spectral bands, ζ, query-aware logit bound and
+// the two-gate keep mask, in one pass over the keys; plus the stand-alone
+// 512-point FWHT.
+//
+// Reference semantics (j-arndt/orthocache v0.3.0):
+//   fwht_512                     src/orthocache/fwht.py:4-65
+//   _run_fwht_on_blocks          src/orthocache/spectral_energy.py:38-66
+//   compute_spectral_bands       spectral_energy.py:69-106
+//   compute_spectral_decay_ratio spectral_energy.py:109-138
+//   compute_query_aware_bounds   spectral_energy.py:141-177
+//   compute_query_aware_mask     spectral_energy.py:180-196
+//   compute_multiband_mask       spectral_energy.py:199-234
+//
+// Two scorers share one epilogue:
+//
+//  * Partial-transform scorer (mode 1; default when every band edge is 0, 1 or
+//    a multiple of 64).  Write the token index of a 512-block as
+//    i = 64*i_hi + i_lo and the coefficient index as k = 64*k_hi + k_lo.  The
+//    natural-order WHT factors as  c[k] = sum_{i_lo} (-1)^{k_lo.i_lo} y[k_hi,i_lo]
+//    with  y[k_hi, i_lo] = sum_{i_hi} (-1)^{k_hi.i_hi} x[64 i_hi + i_lo]  — the
+//    last three butterfly stages (h = 64, 128, 256) applied first.  By
+//    Parseval over the 64-point inner transform, the energy of coefficient
+//    group k_hi (indices 64 k_hi .. 64 k_hi + 63) is sum_{i_lo} y[k_hi,i_lo]^2 / 8
+//    after the reference's 1/sqrt(512) normalisation, and the energy of
+//    indices 1..63 is the centred sum  sum (y[0,i_lo] - mean)^2 / 8 (two-pass,
+//    so no cancellation against a large DC term).  DC = sum_{i_lo} y[0,i_lo]
+//    / sqrt(512).  Every band of the reference (1-63, 64-255, 256-511) is a
+//    union of these groups, so the band energies need 3 butterfly stages per
+//    element instead of 9; the results equal the reference's up to float32
+//    summation order.
+//
+//  * Full-butterfly scorer (mode 2; any bands).  All 9 stages in the
+//    reference's order in shared memory, coefficient by coefficient, then band
+//    sums of coef^2.  Coefficients are bit-identical to fwht_512.
+//
+// One CTA scores one (batch, block, kv-head) tile of 512 x D keys.
+#include "oc_common.cuh"
+
+#include <math.h>
+
+namespace oc {
+namespace {
+
+constexpr int kBlock = 512;
+constexpr int kThreads = 256;
+constexpr float kNorm = 22.627416997969522f;  // fwht.py:61, rounded to float32
+
+struct Bands {
+  int lo[3], hi[3];  // low, mid, high: [lo, hi) in natural coefficient order
+};
+
+struct ScoreArgs {
+  const void* keys;
+  const void* q;
+  int S, H, D, nb;
+  int Sq, Hq, G;
+  Bands bands;
+  float tau, zeta_max;
+  float* dc;
+  float* e_low;
+  float* e_mid;
+  float* e_high;
+  float* zeta;
+  float* bound_max;
+  float* bounds;  // (B, Sq, nb, Hq) or null
+  uint8_t* keep;
+};
+
+// ---------------------------------------------------------------------------
+// Epilogue shared by both scorers.  Inputs in shared memory: dc_coef[D]
+// (normalised WHT coefficient 0 per column) and band[4] = {E_low, E_mid,
+// E_high, E_AC}.  Computes the bound over the Sq*G query rows of this KV head
+// (spectral_energy.py:150-177), its max (:195), ζ (:138) and the keep bit
+// (:196, :231-234).
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ void score_epilogue(const ScoreArgs& a, int b, int j, int h,
+                               const float* dc_coef, const float* band, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int D = a.D;
+  const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
+  if (a.dc)
+    for (int c = tid; c < D; c += kThreads) a.dc[cell * D + c] = dc_coef[c];
+
+  float bmax = -INFINITY;
+  if (a.q) {
+    const float e_ac = band[3];
+    const float sqrt_d = sqrtf((float)D);
+    const float resid_scale = sqrtf(e_ac);
+    const int rows = a.Sq * a.G;
+    const T* qb = reinterpret_cast<const T*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+    for (int r = warp; r < rows; r += kThreads / 32) {
+      const int s = r / a.G, g = r - s * a.G;
+      const T* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + g) * D;
+      float dot = 0.f, nrm = 0.f;
+      for (int c = lane; c < D; c += 32) {
+        const float qv = to_f32<T>(qr[c]);
+        const float mean = dc_coef[c] / kNorm;  // block mean = DC / sqrt(512)  (:166)
+        dot = fmaf(qv, mean, dot);
+        nrm = fmaf(qv, qv, nrm);
+      }
+      dot = warp_sum(dot);
+      nrm = warp_sum(nrm);
+      const float align = dot / sqrt_d;                        // (:169)
+      const float resid = (sqrtf(nrm) * resid_scale) / sqrt_d;  // (:172-175)
+      const float bound = align + resid;
+      if (a.bounds && lane == 0)
+        a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + g] = bound;
+      bmax = fmaxf(bmax, bound);
+    }
+    if (lane == 0) red[warp] = bmax;
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < kThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
+      red[0] = bmax;
+    }
+    __syncthreads();
+    bmax = red[0];
+  }
+  if (tid == 0) {
+    const float z = band[2] / (band[0] + 1e-6f);  // (:138)
+    if (a.e_low) a.e_low[cell] = band[0];
+    if (a.e_mid) a.e_mid[cell] = band[1];
+    if (a.e_high) a.e_high[cell] = band[2];
+    if (a.zeta) a.zeta[cell] = z;
+    if (a.q && a.bound_max) a.bound_max[cell] = bmax;
+    if (a.keep) {
+      const bool gate1 = a.q ? (bmax >= a.tau) : true;
+      a.keep[cell] = (gate1 && (z <= a.zeta_max)) ? 1 : 0;
+    }
+  }
+}
+
+// Energy of band [lo, hi) from the 8 coefficient-group energies of the
+// partial transform (grp[0] excludes the DC coefficient) and the DC energy.
+__device__ __forceinline__ float band_from_groups(int lo, int hi, const float* grp, float e_dc) {
+  float e = 0.f;
+  if (lo == 0 && hi >= 1) e += e_dc;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int glo = k == 0 ? 1 : 64 * k;
+    if (lo <= glo && hi >= 64 * (k + 1)) e += grp[k];
+  }
+  return e;
+}
+
+// ---------------------------------------------------------------------------
+// Partial-transform scorer.
+// Thread t owns column group cg = t % CG (VEC consecutive columns, one 16-byte
+// vector) and the inner token offsets i_lo = t / CG + n * (256 / CG).  For
+// each i_lo it loads the 8 tokens i_lo + 64 * i_hi, runs the butterfly
+// stages h = 64, 128, 256 across them and accumulates the squared results
+// per coefficient group.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads)
+score_partial_kernel(ScoreArgs a) {
+  constexpr int VEC = Elem<T>::kVec;
+  constexpr int CG = D / VEC;
+  constexpr int STEP = kThreads / CG;  // i_lo stride between a thread's items
+  constexpr int ITEMS = 64 / STEP;
+  static_assert(kThreads % CG == 0 && 64 % STEP == 0, "tile mapping");
+
+  __shared__ float s_part[STEP][D];  // per-thread-row column sums of y0
+  __shared__ float s_dc[D];
+  __shared__ float s_mean[D];
+  __shared__ float s_grp[kThreads / 32][8];
+  __shared__ float s_band[4];
+  __shared__ float s_red[kThreads / 32];
+
+  const int tid = threadIdx.x;
+  const int h = blockIdx.x % a.H;
+  const int j = (blockIdx.x / a.H) % a.nb;
+  const int b = blockIdx.x / (a.H * a.nb);
+  const int cg = tid % CG;
+  const int row0 = tid / CG;
+
+  const T* base = reinterpret_cast<const T*>(a.keys) +
+                  (((size_t)b * a.S + (size_t)j * kBlock) * a.H + h) * D + cg * VEC;
+  const size_t tok_stride = (size_t)a.H * D;  // elements between consecutive tokens
+
+  float y0[ITEMS][VEC];
+  float grp[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) grp[k] = 0.f;
+  float colsum[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) colsum[v] = 0.f;
+
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int ilo = row0 + it * STEP;
+    uint4 raw[8];
+#pragma unroll
+    for (int ih = 0; ih < 8; ++ih)
+      raw[ih] = ldg_stream(base + (size_t)(ih * 64 + ilo) * tok_stride);
+    {
+      float x[8][VEC];
+#pragma unroll
+      for (int ih = 0; ih < 8; ++ih) unpack16<T>(raw[ih], x[ih]);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        // stage h = 64 (token bit 6)
+        float a0 = x[0][v] + x[1][v], a1 = x[0][v] - x[1][v];
+        float a2 = x[2][v] + x[3][v], a3 = x[2][v] - x[3][v];
+        float a4 = x[4][v] + x[5][v], a5 = x[4][v] - x[5][v];
+        float a6 = x[6][v] + x[7][v], a7 = x[6][v] - x[7][v];
+        // stage h = 128 (bit 7)
+        float b0 = a0 + a2, b2 = a0 - a2, b1 = a1 + a3, b3 = a1 - a3;
+        float b4 = a4 + a6, b6 = a4 - a6, b5 = a5 + a7, b7 = a5 - a7;
+        // stage h = 256 (bit 8)
+        float c0 = b0 + b4, c4 = b0 - b4, c1 = b1 + b5, c5 = b1 - b5;
+        float c2 = b2 + b6, c6 = b2 - b6, c3 = b3 + b7, c7 = b3 - b7;
+        y0[it][v] = c0;
+        colsum[v] += c0;
+        grp[1] = fmaf(c1, c1, grp[1]);
+        grp[2] = fmaf(c2, c2, grp[2]);
+        grp[3] = fmaf(c3, c3, grp[3]);
+        grp[4] = fmaf(c4, c4, grp[4]);
+        grp[5] = fmaf(c5, c5, grp[5]);
+        grp[6] = fmaf(c6, c6, grp[6]);
+        grp[7] = fmaf(c7, c7, grp[7]);
+      }
+    }
+  }
+
+  // Column sums of y0 over the 64 inner offsets -> DC (deterministic order).
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) s_part[row0][cg * VEC + v] = colsum[v];
+  __syncthreads();
+  for (int c = tid; c < D; c += kThreads) {
+    float s = 0.f;
+    for (int r = 0; r < STEP; ++r) s += s_part[r][c];
+    s_mean[c] = s * (1.0f / 64.0f);
+    s_dc[c] = s / kNorm;
+  }
+  __syncthreads();
+
+  // Second pass: centred energy of group 0 (coefficients 1..63).
+  float g0 = 0.f;
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      const float d = y0[it][v] - s_mean[cg * VEC + v];
+      g0 = fmaf(d, d, g0);
+    }
+  grp[0] = g0;
+
+  const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float s = warp_sum(grp[k]);
+    if (lane == 0) s_grp[warp][k] = s;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float g[8];
+    for (int k = 0; k < 8; ++k) {
+      float s = 0.f;
+      for (int w = 0; w < kThreads / 32; ++w) s += s_grp[w][k];
+      g[k] = s * 0.125f;  // (64 / 512) Parseval factor of the inner transform
+    }
+    float e_dc = 0.f;
+    for (int c = 0; c < D; ++c) e_dc = fmaf(s_dc[c], s_dc[c], e_dc);
+    float e_ac = 0.f;
+    for (int k = 0; k < 8; ++k) e_ac += g[k];
+    s_band[0] = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
+    s_band[1] = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
+    s_band[2] = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
+    s_band[3] = e_ac;
+  }
+  __syncthreads();
+  score_epilogue<T>(a, b, j, h, s_dc, s_band, s_red);
+}
+
+// ---------------------------------------------------------------------------
+// Full 9-stage butterfly on a shared-memory slab of 512 x 32 float32,
+// stage order h = 1, 2, ..., 256 and "a + b" to the lower / "a - b" to the
+// upper row exactly as fwht.py:25-58 (bit-identical float32 results).
+// ---------------------------------------------------------------------------
+constexpr int kSlab = 32;
+
+__device__ __forceinline__ void slab_fwht(float (*s)[kSlab]) {
+  const int c = threadIdx.x & 31;
+  const int p0 = threadIdx.x >> 5;  // 8 pair rows per pass
+#pragma unroll 1
+  for (int hs = 1; hs < kBlock; hs <<= 1) {
+    __syncthreads();
+#pragma unroll 8
+    for (int p = p0; p < kBlock / 2; p += kThreads / 32) {
+      const int lo = (p / hs) * (2 * hs) + (p % hs);
+      const int hi = lo + hs;
+      const float x = s[lo][c], y = s[hi][c];
+      s[lo][c] = x + y;
+      s[hi][c] = x - y;
+    }
+  }
+  __syncthreads();
+}
+
+template <typename T>
+__device__ __forceinline__ void load_slab(float (*s)[kSlab], const T* src, size_t row_stride,
+                                          int ncols_valid) {
+  for (int i = threadIdx.x; i < kBlock * kSlab; i += kThreads) {
+    const int r = i / kSlab, c = i % kSlab;
+    s[r][c] = c < ncols_valid ? to_f32<T>(src[(size_t)r * row_stride + c]) : 0.f;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+score_full_kernel(ScoreArgs a) {
+  extern __shared__ float dyn[];
+  float (*s)[kSlab] = reinterpret_cast<float (*)[kSlab]>(dyn);
+  float* s_dc = dyn + kBlock * kSlab;           // [D]
+  __shared__ float s_acc[kThreads / 32][4];
+  __shared__ float s_band[4];
+  __shared__ float s_red[kThreads / 32];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int D = a.D;
+  const int h = blockIdx.x % a.H;
+  const int j = (blockIdx.x / a.H) % a.nb;
+  const int b = blockIdx.x / (a.H * a.nb);
+  const T* base = reinterpret_cast<const T*>(a.keys) +
+                  (((size_t)b * a.S + (size_t)j * kBlock) * a.H + h) * D;
+  const size_t tok_stride = (size_t)a.H * D;
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};  // low, mid, high, AC
+  for (int c0 = 0; c0 < D; c0 += kSlab) {
+    __syncthreads();
+    load_slab<T>(s, base + c0, tok_stride, min(kSlab, D - c0));
+    slab_fwht(s);
+    for (int i = tid; i < kBlock * kSlab; i += kThreads) {
+      const int k = i / kSlab, c = i % kSlab;
+      if (c0 + c >= D) continue;
+      const float coef = s[k][c] / kNorm;
+      if (k == 0) { s_dc[c0 + c] = coef; }
+      const float e = coef * coef;
+      if (k >= 1) acc[3] += e;
+#pragma unroll
+      for (int bnd = 0; bnd < 3; ++bnd)
+        if (k >= a.bands.lo[bnd] && k < a.bands.hi[bnd]) acc[bnd] += e;
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float v = warp_sum(acc[q]);
+    if (lane == 0) s_acc[warp][q] = v;
+  }
+  __syncthreads();
+  if (tid < 4) {
+    float v = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) v += s_acc[w][tid];
+    s_band[tid] = v;
+  }
+  __syncthreads();
+  score_epilogue<T>(a, b, j, h, s_dc, s_band, s_red);
+}
+
+// Stand-alone fwht_512 over (512, N): one CTA per 32-column slab.
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+fwht512_kernel(const T* x, float* y, int64_t n) {
+  extern __shared__ float dyn[];
+  float (*s)[kSlab] = reinterpret_cast<float (*)[kSlab]>(dyn);
+  const int64_t c0 = (int64_t)blockIdx.x * kSlab;
+  const int valid = (int)((n - c0) < kSlab ? (n - c0) : kSlab);
+  load_slab<T>(s, x + c0, (size_t)n, valid);
+  slab_fwht(s);
+  for (int i = threadIdx.x; i < kBlock * kSlab; i += kThreads) {
+    const int r = i / kSlab, c = i % kSlab;
+    if (c < valid) y[(size_t)r * n + c0 + c] = s[r][c] / kNorm;
+  }
+}
+
+constexpr size_t kSlabBytes = (size_t)kBlock * kSlab * sizeof(float);
+
+bool bands_partial_ok(const Bands& bd) {
+  for (int i = 0; i < 3; ++i) {
+    const int e[2] = {bd.lo[i], bd.hi[i]};
+    for (int q = 0; q < 2; ++q)
+      if (!(e[q] == 0 || e[q] == 1 || e[q] % 64 == 0)) return false;
+  }
+  return true;
+}
+
+template <typename T>
+int launch_score(const ScoreArgs& a, int mode, int ncta, cudaStream_t st) {
+  if (mode == 1) {
+    switch (a.D) {
+      case 64: score_partial_kernel<T, 64><<<ncta, kThreads, 0, st>>>(a); break;
+      case 128: score_partial_kernel<T, 128><<<ncta, kThreads, 0, st>>>(a); break;
+      case 256: score_partial_kernel<T, 256><<<ncta, kThreads, 0, st>>>(a); break;
+      default: return set_error(OC_ERR_SHAPE, "head_dim %d not in {64,128,256}", a.D);
+    }
+    return check_launch("score_partial_kernel");
+  }
+  const size_t smem = kSlabBytes + (size_t)a.D * sizeof(float);
+  // Per call: the attribute is per device, and one process may drive several.
+  cudaFuncSetAttribute(score_full_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  score_full_kernel<T><<<ncta, kThreads, smem, st>>>(a);
+  return check_launch("score_full_kernel");
+}
+
+}  // namespace
+}  // namespace oc
+
+using namespace oc;
+
+extern "C" int oc_fwht512(const void* x, int x_dtype, int64_t ncols, float* y, oc_stream_t stream) {
+  OC_REQUIRE(x && y, OC_ERR_NULL, "oc_fwht512: null pointer");
+  OC_REQUIRE(ncols >= 0, OC_ERR_SHAPE, "oc_fwht512: ncols < 0");
+  if (ncols == 0) return OC_OK;
+  const int64_t grid = (ncols + kSlab - 1) / kSlab;
+  OC_REQUIRE(grid < (1ll << 31), OC_ERR_CAPACITY, "oc_fwht512: too many columns");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaFuncSetAttribute(fwht512_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSlabBytes);
+  cudaFuncSetAttribute(fwht512_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSlabBytes);
+  if (x_dtype == OC_F32)
+    fwht512_kernel<float><<<(unsigned)grid, kThreads, kSlabBytes, st>>>((const float*)x, y, ncols);
+  else if (x_dtype == OC_BF16)
+    fwht512_kernel<__nv_bfloat16><<<(unsigned)grid, kThreads, kSlabBytes, st>>>(
+        (const __nv_bfloat16*)x, y, ncols);
+  else
+    return set_error(OC_ERR_DTYPE, "oc_fwht512: dtype %d", x_dtype);
+  return check_launch("fwht512_kernel");
+}
+
+extern "C" int oc_score_blocks(const void* keys, const void* q, int dtype,
+                               int batch, int seq_len, int kv_heads, int head_dim,
+                               int q_len, int q_heads,
+                               int bl0, int bl1, int bm0, int bm1, int bh0, int bh1,
+                               float tau, float zeta_max,
+                               float* dc, float* e_low, float* e_mid, float* e_high,
+                               float* zeta, float* bound_max, float* bounds, uint8_t* keep,
+                               int mode, oc_stream_t stream) {
+  OC_REQUIRE(keys, OC_ERR_NULL, "oc_score_blocks: keys is NULL");
+  OC_REQUIRE(batch >= 1 && kv_heads >= 1, OC_ERR_SHAPE, "oc_score_blocks: batch/kv_heads < 1");
+  OC_REQUIRE(seq_len >= 0 && seq_len % kBlock == 0, OC_ERR_SHAPE,
+             "oc_score_blocks: seq_len %d is not a multiple of 512", seq_len);
+  OC_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, OC_ERR_SHAPE,
+             "oc_score_blocks: head_dim %d not in {64,128,256}", head_dim);
+  OC_REQUIRE(dtype == OC_F32 || dtype == OC_BF16, OC_ERR_DTYPE, "oc_score_blocks: dtype %d", dtype);
+  OC_REQUIRE(aligned16(keys), OC_ERR_ALIGN, "oc_score_blocks: keys not 16-byte aligned");
+  if (q) {
+    OC_REQUIRE(q_len >= 1 && q_heads >= 1 && q_heads % kv_heads == 0, OC_ERR_SHAPE,
+               "oc_score_blocks: q_heads %d must be a positive multiple of kv_heads %d (q_len %d)",
+               q_heads, kv_heads, q_len);
+  }
+  Bands bd{{bl0, bm0, bh0}, {bl1, bm1, bh1}};
+  for (int i = 0; i < 3; ++i)
+    OC_REQUIRE(bd.lo[i] >= 0 && bd.hi[i] <= kBlock && bd.lo[i] <= bd.hi[i], OC_ERR_SHAPE,
+               "oc_score_blocks: band %d = [%d, %d) outside [0, 512)", i, bd.lo[i], bd.hi[i]);
+  if (mode == 0) mode = bands_partial_ok(bd) ? 1 : 2;
+  OC_REQUIRE(mode == 1 || mode == 2, OC_ERR_SHAPE, "oc_score_blocks: mode %d", mode);
+  OC_REQUIRE(mode == 2 || bands_partial_ok(bd), OC_ERR_SHAPE,
+             "oc_score_blocks: mode 1 needs band edges in {0, 1, 64k}");
+  const int nb = seq_len / kBlock;
+  const int64_t ncta = (int64_t)batch * nb * kv_heads;
+  if (ncta == 0) return OC_OK;
+  OC_REQUIRE(ncta < (1ll << 31), OC_ERR_CAPACITY, "oc_score_blocks: too many blocks");
+  ScoreArgs a;
+  a.keys = keys; a.q = q; a.S = seq_len; a.H = kv_heads; a.D = head_dim; a.nb = nb;
+  a.Sq = q ? q_len : 0; a.Hq = q ? q_heads : 0; a.G = q ? q_heads / kv_heads : 1;
+  a.bands = bd; a.tau = tau; a.zeta_max = zeta_max;
+  a.dc = dc; a.e_low = e_low; a.e_mid = e_mid; a.e_high = e_high; a.zeta = zeta;
+  a.bound_max = bound_max; a.bounds = q ? bounds : nullptr; a.keep = keep;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == OC_F32) return launch_score<float>(a, mode, (int)ncta, st);
+  return launch_score<__nv_bfloat16>(a, mode, (int)ncta, st);
+}

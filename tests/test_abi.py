@@ -1,0 +1,57 @@
+"""The C-ABI library loads on a machine without a GPU and exports every entry
+point declared in include/orthocache_b200.h; the ctypes table covers them all.
+No compute calls (those need a GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "orthocache_b200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(oc_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for n in ("oc_fwht512", "oc_score_blocks", "oc_stream_compact", "oc_indirect_attention", "oc_decode_step"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from orthocache_b200 import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        from orthocache_b200 import build
+        build.build()
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_ctypes_table_matches_header():
+    from orthocache_b200 import _lib
+    assert sorted(_lib.SIGNATURES) == declared()
+    lib = _lib.load()
+    assert lib.oc_version() >= 100
+    assert lib.oc_status_string(-2) == b"bad shape"
+
+
+def test_host_side_validation_without_gpu():
+    """Argument checks run on the host before any launch: bad shapes fail with
+    a status code and a message, without touching the device."""
+    from orthocache_b200 import _lib
+    lib = _lib.load()
+    rc = lib.oc_score_blocks(ctypes.c_void_p(16), None, 1, 1, 1000, 8, 128, 0, 0, 1, 64, 64, 256, 256, 512,
+                             0.0, 5.0, None, None, None, None, None, None, None, None, 0, None)
+    assert rc == -2 and b"multiple of 512" in lib.oc_last_error()
+    rc = lib.oc_stream_compact(None, 1, 4, 1, None, None, None)
+    assert rc == -1
+    assert lib.oc_stratified_bucket(16, 5) == 8
+    assert lib.oc_stratified_bucket(16, 0) == 4
+    assert lib.oc_stratified_bucket(1, 1) == 1
+    assert lib.oc_indirect_attention_workspace_bytes(1, 1, 32, 8, 128, 512, 128) > 0
