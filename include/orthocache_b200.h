@@ -53,6 +53,12 @@ const char* oc_status_string(int status);
 /* Message of the calling thread's last failure ("" if none). */
 const char* oc_last_error(void);
 
+/* Device-side status of the pipelined kernels: nonzero if a bounded wait on
+ * an asynchronous copy gave up (the kernel then skipped its remaining work
+ * instead of hanging).  Synchronises the current device; reset != 0 clears it.
+ * Returns the status (>= 0) or an OC_ERR_* code. */
+int oc_device_status(int reset);
+
 /* ---------------------------------------------------------------------------
  * fwht_512 — replaces `fwht_512(x)` (src/orthocache/fwht.py:4-65).
  * x: (512, ncols) row-major, dtype `x_dtype`; y: (512, ncols) float32.
@@ -86,7 +92,10 @@ int oc_fwht512(const void* x, int x_dtype, int64_t ncols, float* y, oc_stream_t 
  * compute_query_aware_bounds); keep (B, nb, Hkv) uint8 0/1.
  *
  * mode: 0 = automatic; 1 = the partial-transform scorer (band edges must be
- * 0, 1 or multiples of 64); 2 = the full 9-stage butterfly scorer (any bands).
+ * 0, 1 or multiples of 64; bfloat16 keys stream through a bulk-tensor (TMA)
+ * shared-memory pipeline); 2 = the full 9-stage butterfly scorer (any
+ * bands); 3 = the partial-transform scorer with per-thread vector loads
+ * (same results as 1, kept as a cross-check).
  */
 int oc_score_blocks(const void* keys, const void* q, int dtype,
                     int batch, int seq_len, int kv_heads, int head_dim,
@@ -187,6 +196,16 @@ int oc_indirect_attention(const void* q, const void* k, const void* v, int dtype
                           int seq_len, int block_size, int max_blocks,
                           void* out, int out_dtype,
                           void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
+/* Predicated-attention semantics for a head with no kept block
+ * (sparse_attention.py:49-57: every logit masked to -1e9, so the softmax is
+ * uniform): for each (b, h) with count[b*count_stride + h*count_head_stride]
+ * == 0, write the mean over all S value rows of head h to the G query heads
+ * of that group in out (B, Sq, Hq, D).  Other rows are untouched; run it after
+ * oc_indirect_attention with per-head lists. */
+int oc_empty_heads_mean(const void* v, int dtype, const int32_t* count, int count_stride,
+                        int count_head_stride, int batch, int q_len, int q_heads, int kv_heads,
+                        int head_dim, int seq_len, void* out, int out_dtype, oc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * One decode step of the OrthoCache pipeline on the device: score (two-gate

@@ -165,3 +165,13 @@ def count_tensor(n, device, batch=1):
         return n.to(device=device, dtype=torch.int32).reshape(-1).expand(batch).contiguous() \
             if n.numel() == 1 else n.to(device=device, dtype=torch.int32).contiguous()
     return torch.full((batch,), int(n), dtype=torch.int32, device=device)
+
+
+def fill_empty_heads(out, v, count, count_stride, count_head_stride):
+    """Rows of heads whose list is empty get mean(V) (reference -1e9 predication)."""
+    B, Sq, Hq, D = out.shape
+    S, Hkv = v.shape[1], v.shape[2]
+    _lib.call("oc_empty_heads_mean", _lib.ptr(v), _lib.dtype_code(v), _lib.ptr(count), int(count_stride),
+              int(count_head_stride), B, Sq, Hq, Hkv, D, S, _lib.ptr(out), _lib.dtype_code(out),
+              _lib.stream_ptr(v.device))
+    return out

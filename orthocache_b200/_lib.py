@@ -30,6 +30,7 @@ SIGNATURES = {
     "oc_version": (_i, []),
     "oc_status_string": (C.c_char_p, [_i]),
     "oc_last_error": (C.c_char_p, []),
+    "oc_device_status": (_i, [_i]),
     "oc_fwht512": (_i, [_p, _i, _i64, _p, _p]),
     "oc_score_blocks": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _f,
                              _p, _p, _p, _p, _p, _p, _p, _p, _i, _p]),
@@ -44,6 +45,7 @@ SIGNATURES = {
                                    _i, _p, _i, _p, _sz, _p]),
     "oc_partial_attention": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
                                   _i, _p, _p, _p, _p, _sz, _p]),
+    "oc_empty_heads_mean": (_i, [_p, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p]),
     "oc_merge_partials": (_i, [_p, _p, _p, _i, _i, _i, _p, _i, _p]),
     "oc_decode_step_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "oc_decode_step": (_i, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p, _p, _p, _i, _p, _sz,

@@ -19,6 +19,7 @@
 //
 // Logits are kept in log2 units: s = (q.k) * log2(e) / sqrt(D), p = 2^(s - m).
 #include "oc_common.cuh"
+#include "oc_tma.cuh"
 
 #include <math.h>
 
@@ -157,6 +158,13 @@ attn_partial_kernel(AttnArgs a) {
       const int t = trow0 + i * RPW;
       kr[i] = t < a.chunk ? ldg_stream(kbase + (size_t)t * tok_stride) : make_uint4(0, 0, 0, 0);
     }
+    // V of the same rows is requested now, so its latency hides behind the softmax.
+    uint4 vr[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int t = trow0 + i * RPW;
+      vr[i] = t < a.chunk ? ldg_stream(vbase + (size_t)t * tok_stride) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
     for (int i = 0; i < ITERS; ++i) {
       const int t = trow0 + i * RPW;
@@ -191,12 +199,6 @@ attn_partial_kernel(AttnArgs a) {
     __syncthreads();
 
     // ---- o[r][d] = sum_t p[r][t] v[t][d] ----
-    uint4 vr[ITERS];
-#pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-      const int t = trow0 + i * RPW;
-      vr[i] = t < a.chunk ? ldg_stream(vbase + (size_t)t * tok_stride) : make_uint4(0, 0, 0, 0);
-    }
     float acc[RT][VEC];
 #pragma unroll
     for (int r = 0; r < RT; ++r)
@@ -249,14 +251,235 @@ attn_partial_kernel(AttnArgs a) {
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// bfloat16 path: the same work items, with K and V chunks streamed by 2-D
+// bulk-tensor loads into a ring of shared-memory stages (persistent grid, one
+// CTA per SM, thread 0 keeps kAStages chunks in flight).  A stage holds the
+// CH x D keys and the CH x D values of one item; it is refilled with the item
+// kAStages ahead as soon as the softmax-weighted sum has read it.
+// ---------------------------------------------------------------------------
+constexpr int kAStages = 3;
+constexpr int kAStageBytes = 65536;  // 2 * CH * D * 2 with CH * D = 16384
+
+__device__ int g_attn_status = 0;
+
+struct GroupSync {
+  int id;  // named barrier 1 or 2 for a 256-thread consumer group
+  __device__ void operator()() const { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
+};
+
+template <int D, int RT>
+__global__ void __launch_bounds__(2 * kThreads, 1)
+attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+  constexpr int CH = 16384 / D;          // tokens per item (128 at D = 128)
+  constexpr int VEC = 8;
+  constexpr int LPR = D / VEC;
+  constexpr int RPW = 32 / LPR;
+  constexpr int ROWS_PER_WARP = CH / kWarps;
+  constexpr int ITERS = ROWS_PER_WARP / RPW;
+  constexpr int ROWB = D * 2;            // bytes per token row in shared memory
+  static_assert(ROWS_PER_WARP % RPW == 0, "mapping");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kAStages];
+  __shared__ float s_p[2][RT][CH];
+  __shared__ float s_m[2][RT], s_l[2][RT];
+  __shared__ float s_o[2][kWarps / 2][RT][D];
+  __shared__ int s_abort[2];
+
+  const int gid = threadIdx.x / kThreads;
+  const int tid = threadIdx.x % kThreads, lane = tid & 31, warp = tid >> 5;
+  const GroupSync gsync{1 + gid};
+  const int sub = lane / LPR, vl = lane % LPR, d0 = vl * VEC;
+
+  auto issue = [&](int k) -> bool {
+    int b, item, h, rt;
+    if (!decode_item(a, blockIdx.x + k * gridDim.x, b, item, h, rt)) return false;
+    const int slot = item / a.chunks, c = item - slot * a.chunks;
+    const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
+    uint64_t* bar = &full[k % kAStages];
+    uint8_t* dst = smem + (size_t)(k % kAStages) * kAStageBytes;
+    mbar_expect_tx(bar, kAStageBytes);
+    // An out-of-range index is never dereferenced: block 0 is loaded instead
+    // and the item contributes nothing.
+    const int y = (blk < 0 || blk >= a.S / a.bs) ? b * a.S : b * a.S + blk * a.bs + c * CH;
+    tma_load_2d(dst, &kmap, bar, h * D, y);
+    tma_load_2d(dst + kAStageBytes / 2, &vmap, bar, h * D, y);
+    return true;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kAStages; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    for (int k = 0; k < kAStages; ++k)
+      if (!issue(k)) break;
+  }
+  if (tid == 0) s_abort[gid] = 0;
+  __syncthreads();
+
+  // Group g takes this CTA's items k with k % 2 == g.
+  for (int k = gid;; k += 2) {
+    int b, item, h, rt;
+    if (!decode_item(a, blockIdx.x + k * gridDim.x, b, item, h, rt)) break;
+    const int stage = k % kAStages;
+    if (!mbar_wait(&full[stage], (k / kAStages) & 1)) s_abort[gid] = 1;
+    gsync();
+    if (s_abort[gid]) {
+      if (tid == 0) atomicExch(&g_attn_status, 1);
+      return;
+    }
+    const int slot = item / a.chunks;
+    const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
+    const int r0 = rt * RT;
+    const int nr = min(RT, a.R - r0);
+    const size_t part = (((size_t)b * a.max_items + item) * a.Hkv + h) * a.R + r0;
+    const uint8_t* ks = smem + (size_t)stage * kAStageBytes;
+    const uint8_t* vs = ks + kAStageBytes / 2;
+    const bool valid = blk >= 0 && blk < a.S / a.bs;
+
+    float qv[RT][VEC];
+    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      if (r < nr) {
+        const int row = r0 + r, s = row / a.G, g = row - s * a.G;
+        const uint4 raw = *reinterpret_cast<const uint4*>(qb + ((size_t)s * a.Hq + (size_t)h * a.G + g) * D + d0);
+        unpack16<__nv_bfloat16>(raw, qv[r]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) qv[r][e] *= a.scale_log2;
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) qv[r][e] = 0.f;
+      }
+    }
+    const int trow0 = warp * ROWS_PER_WARP + sub;
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int t = trow0 + i * RPW;
+      float kf[VEC];
+      unpack16<__nv_bfloat16>(*reinterpret_cast<const uint4*>(ks + (size_t)t * ROWB + d0 * 2), kf);
+#pragma unroll
+      for (int r = 0; r < RT; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc = fmaf(qv[r][e], kf[e], acc);
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (vl == 0) s_p[gid][r][t] = acc;
+      }
+    }
+    gsync();
+    for (int r = warp; r < RT; r += kWarps) {
+      float m = -INFINITY;
+      for (int t = lane; t < CH; t += 32) m = fmaxf(m, s_p[gid][r][t]);
+      m = warp_max(m);
+      float l = 0.f;
+      for (int t = lane; t < CH; t += 32) {
+        const float p = exp2f(s_p[gid][r][t] - m);
+        s_p[gid][r][t] = p;
+        l += p;
+      }
+      l = warp_sum(l);
+      if (lane == 0) { s_m[gid][r] = m; s_l[gid][r] = l; }
+    }
+    gsync();
+    float acc[RT][VEC];
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[r][e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < ITERS; ++i) {
+      const int t = trow0 + i * RPW;
+      float vf[VEC];
+      unpack16<__nv_bfloat16>(*reinterpret_cast<const uint4*>(vs + (size_t)t * ROWB + d0 * 2), vf);
+#pragma unroll
+      for (int r = 0; r < RT; ++r) {
+        const float p = s_p[gid][r][t];
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[r][e] = fmaf(p, vf[e], acc[r][e]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        float x = acc[r][e];
+#pragma unroll
+        for (int o = LPR; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        acc[r][e] = x;
+      }
+    // Cross-warp sum in two rounds through half-size scratch.
+    if (sub == 0 && warp >= kWarps / 2) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) s_o[gid][warp - kWarps / 2][r][d0 + e] = acc[r][e];
+    }
+    gsync();  // stage fully read; upper warps' sums visible
+    if (tid == 0) {
+      fence_proxy_async();
+      issue(k + kAStages);
+    }
+    if (sub == 0 && warp < kWarps / 2) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) s_o[gid][warp][r][d0 + e] += acc[r][e];
+    }
+    gsync();
+    for (int x = tid; x < nr * D; x += kThreads) {
+      const int r = x / D, d = x - r * D;
+      float sum = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kWarps / 2; ++ww) sum += s_o[gid][ww][r][d];
+      a.ws_o[(part + r) * D + d] = valid ? sum : 0.f;
+    }
+    if (tid < nr) {
+      a.ws_m[part + tid] = valid ? s_m[gid][tid] : -INFINITY;
+      a.ws_l[part + tid] = valid ? s_l[gid][tid] : 0.f;
+    }
+    gsync();
+  }
+}
+
+template <int D>
+int launch_attn_tma(const AttnArgs& a, int rt, cudaStream_t st) {
+  constexpr int CH = 16384 / D;
+  CUtensorMap km, vm;
+  const uint64_t cols = (uint64_t)a.Hkv * D, rows = (uint64_t)a.B * a.S;
+  int rc = encode_map_2d(&km, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, D, CH);
+  if (!rc) rc = encode_map_2d(&vm, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, D, CH);
+  if (rc) return set_error(OC_ERR_CUDA, "attention: tensor map encode failed (%d)", rc);
+  const int smem = kAStages * kAStageBytes;
+  const int grid = device_sm_count();
+#define OC_ATMA(RTV)                                                                                   \
+  do {                                                                                                 \
+    cudaFuncSetAttribute(attn_tma_kernel<D, RTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    attn_tma_kernel<D, RTV><<<grid, 2 * kThreads, smem, st>>>(km, vm, a);                                  \
+  } while (0)
+  if (rt == 1) OC_ATMA(1);
+  else if (rt == 2) OC_ATMA(2);
+  else if constexpr (D <= 128) {
+    if (rt == 4) OC_ATMA(4);
+    else return set_error(OC_ERR_SHAPE, "attention: row tile %d", rt);
+  } else
+    return set_error(OC_ERR_SHAPE, "attention: row tile %d", rt);
+#undef OC_ATMA
+  return check_launch("attn_tma_kernel");
+}
+
 // Combine the items of one (batch, kv head, row): M = max m_i,
 // L = sum l_i 2^(m_i - M), O = sum o_i 2^(m_i - M).  mode 0 writes O / L in
 // the output dtype at the reference's (Sq, Hq, D) position (zeros when the
 // batch row has no retained block); mode 1 writes (M, L, O) float32 for a
 // later cross-shard merge.
 template <typename TO>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode) {
+  __shared__ float s_f[256];
+  __shared__ float s_red[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r = blockIdx.x % a.R;
   const int h = (blockIdx.x / a.R) % a.Hkv;
   const int b = blockIdx.x / (a.R * a.Hkv);
@@ -265,17 +488,47 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
   const size_t orow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + g;
   const size_t stride = (size_t)a.Hkv * a.R;
   const size_t p0 = ((size_t)b * a.max_items * a.Hkv + h) * a.R + r;
+
+  // M = max_i m_i (all items in parallel)
   float M = -INFINITY;
-  for (int i = 0; i < n; ++i) M = fmaxf(M, a.ws_m[p0 + (size_t)i * stride]);
-  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
-    float L = 0.f, O = 0.f;
-    for (int i = 0; i < n && M != -INFINITY; ++i) {
+  for (int i = tid; i < n; i += 256) M = fmaxf(M, a.ws_m[p0 + (size_t)i * stride]);
+  M = warp_max(M);
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  M = s_red[0];
+  for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
+  __syncthreads();
+
+  // Weights f_i = 2^(m_i - M) staged 256 at a time; thread d accumulates O[d].
+  float lpart = 0.f, O = 0.f;
+  const int d = tid;
+  for (int c0 = 0; c0 < n; c0 += 256) {
+    const int i = c0 + tid;
+    float f = 0.f;
+    if (i < n) {
       const size_t p = p0 + (size_t)i * stride;
-      if (a.ws_m[p] == -INFINITY) continue;
-      const float f = exp2f(a.ws_m[p] - M);
-      L = fmaf(a.ws_l[p], f, L);
-      O = fmaf(a.ws_o[p * a.D + d], f, O);
+      const float mi = a.ws_m[p];
+      if (mi != -INFINITY) {
+        f = exp2f(mi - M);
+        lpart = fmaf(a.ws_l[p], f, lpart);
+      }
     }
+    s_f[tid] = f;
+    __syncthreads();
+    if (d < a.D) {
+      const int cn = min(256, n - c0);
+      const float* ob = a.ws_o + (p0 + (size_t)c0 * stride) * a.D + d;
+#pragma unroll 8
+      for (int j = 0; j < cn; ++j) O = fmaf(s_f[j], ob[(size_t)j * stride * a.D], O);
+    }
+    __syncthreads();
+  }
+  lpart = warp_sum(lpart);
+  if (lane == 0) s_red[warp] = lpart;
+  __syncthreads();
+  float L = 0.f;
+  for (int w = 0; w < 8; ++w) L += s_red[w];
+  if (d < a.D) {
     if (mode == 0) {
       out[orow * a.D + d] = from_f32<TO>(L > 0.f ? O / L : 0.f);
     } else {
@@ -307,6 +560,34 @@ merge_parts_kernel(const float* m, const float* l, const float* o, int P, int ro
   }
 }
 
+// Rows of (batch, kv head) pairs whose index list is empty get the mean of
+// all value rows of that head: the reference's predicated attention masks
+// every logit of such a head with -1e9, and its softmax is then uniform over
+// all tokens (sparse_attention.py:49-57).
+template <typename T, typename TO>
+__global__ void __launch_bounds__(256)
+empty_heads_mean_kernel(const T* __restrict__ v, const int32_t* __restrict__ count, int cnt_stride,
+                        int cnt_hstride, int Sq, int Hq, int Hkv, int D, int S, TO* __restrict__ out) {
+  __shared__ float s_acc[256];
+  const int h = blockIdx.x % Hkv, b = blockIdx.x / Hkv;
+  if (count[(size_t)b * cnt_stride + (size_t)h * cnt_hstride] != 0) return;
+  const int G = Hq / Hkv;
+  const int lanes_per_d = 256 / D;  // D in {64, 128, 256}
+  const int d = threadIdx.x % D, part = threadIdx.x / D;
+  float acc = 0.f;
+  for (int t = part; t < S; t += lanes_per_d)
+    acc += to_f32<T>(v[(((size_t)b * S + t) * Hkv + h) * D + d]);
+  s_acc[threadIdx.x] = acc;
+  __syncthreads();
+  if (part == 0) {
+    for (int p2 = 1; p2 < lanes_per_d; ++p2) acc += s_acc[p2 * D + d];
+    const float mean = acc / (float)S;
+    for (int sq = 0; sq < Sq; ++sq)
+      for (int g = 0; g < G; ++g)
+        out[(((size_t)b * Sq + sq) * Hq + (size_t)h * G + g) * D + d] = from_f32<TO>(mean);
+  }
+}
+
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Row-tile size: query rows handled per work item (8 at most; 4 at D = 256 so
@@ -316,12 +597,19 @@ int pick_rt(int R, int D) {
   return D == 256 && rt > 4 ? 4 : rt;
 }
 
-int chunk_for(int bs) { return bs % 128 == 0 ? 128 : 64; }
+// Tokens per work item: 128 (64 when the block size is not a multiple of
+// 128, or at D = 256 so that a K + V chunk stays within one 64 KB stage).
+int chunk_for(int bs, int D) { return (bs % 128 == 0 && D <= 128) ? 128 : 64; }
+
+// The bulk-tensor path streams CH = 16384 / D tokens per item.
+bool use_tma_path(int dtype, int bs, int D) {
+  return dtype == OC_BF16 && chunk_for(bs, D) == 16384 / D;
+}
 
 size_t attn_ws_bytes(int B, int Sq, int Hq, int Hkv, int D, int bs, int max_blocks) {
   const int G = Hq / Hkv;
   const size_t R = (size_t)Sq * G;
-  const size_t items = (size_t)max_blocks * (bs / chunk_for(bs));
+  const size_t items = (size_t)max_blocks * (bs / chunk_for(bs, D));
   const size_t parts = (size_t)B * items * Hkv * R;
   return 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float));
 }
@@ -390,9 +678,12 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.cnt_stride = cnt_stride; a.cnt_hstride = cnt_hstride;
   a.B = B; a.Sq = Sq; a.Hq = Hq; a.Hkv = Hkv; a.G = Hq / Hkv; a.D = D; a.S = S; a.bs = bs;
   a.R = Sq * a.G;
-  const int rt = pick_rt(a.R, D);
+  const bool tma = use_tma_path(dtype, bs, D);
+  int rt = pick_rt(a.R, D);
+  if (tma && rt * D > 512) rt = 512 / D;
+  if (tma && rt > 4) rt = 4;
   a.n_rt = (a.R + rt - 1) / rt;
-  a.chunk = chunk_for(bs);
+  a.chunk = chunk_for(bs, D);
   a.chunks = bs / a.chunk;
   a.max_items = max_blocks * a.chunks;
   a.scale_log2 = kLog2e / sqrtf((float)D);
@@ -406,18 +697,22 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
 
   if (max_blocks > 0) {
     const int grid = device_sm_count() * 2;
-    rc = dtype == OC_F32 ? launch_partials<float>(a, rt, grid, st)
-                         : launch_partials<__nv_bfloat16>(a, rt, grid, st);
+    if (tma)
+      rc = D == 64 ? launch_attn_tma<64>(a, rt, st) : D == 128 ? launch_attn_tma<128>(a, rt, st)
+                                                     : launch_attn_tma<256>(a, rt, st);
+    else
+      rc = dtype == OC_F32 ? launch_partials<float>(a, rt, grid, st)
+                           : launch_partials<__nv_bfloat16>(a, rt, grid, st);
     if (rc) return rc;
   }
   if (mode == 0) {
     if (out_dtype == OC_F32)
-      attn_merge_kernel<float><<<(unsigned)rows, 128, 0, st>>>(a, (float*)out, nullptr, nullptr, nullptr, 0);
+      attn_merge_kernel<float><<<(unsigned)rows, 256, 0, st>>>(a, (float*)out, nullptr, nullptr, nullptr, 0);
     else
-      attn_merge_kernel<__nv_bfloat16><<<(unsigned)rows, 128, 0, st>>>(a, (__nv_bfloat16*)out, nullptr,
+      attn_merge_kernel<__nv_bfloat16><<<(unsigned)rows, 256, 0, st>>>(a, (__nv_bfloat16*)out, nullptr,
                                                                         nullptr, nullptr, 0);
   } else {
-    attn_merge_kernel<float><<<(unsigned)rows, 128, 0, st>>>(a, nullptr, pm, pl, po, 1);
+    attn_merge_kernel<float><<<(unsigned)rows, 256, 0, st>>>(a, nullptr, pm, pl, po, 1);
   }
   return check_launch("attn_merge_kernel");
 }
@@ -502,3 +797,36 @@ extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int d
   return oc_indirect_attention(q, k, v, dtype, perm, nb, 0, count, 1, 0, batch, q_len, q_heads, kv_heads, head_dim,
                                seq_len, 512, nb, out, out_dtype, workspace, workspace_bytes, stream);
 }
+
+extern "C" int oc_empty_heads_mean(const void* v, int dtype, const int32_t* count, int count_stride,
+                                   int count_head_stride, int batch, int q_len, int q_heads, int kv_heads,
+                                   int head_dim, int seq_len, void* out, int out_dtype, oc_stream_t stream) {
+  OC_REQUIRE(v && count && out, OC_ERR_NULL, "oc_empty_heads_mean: null pointer");
+  OC_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, OC_ERR_SHAPE, "oc_empty_heads_mean: head_dim");
+  OC_REQUIRE(batch >= 1 && kv_heads >= 1 && q_heads % kv_heads == 0 && seq_len >= 1, OC_ERR_SHAPE,
+             "oc_empty_heads_mean: bad shape");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = batch * kv_heads;
+#define OC_EHM(T, TO) empty_heads_mean_kernel<T, TO><<<grid, 256, 0, st>>>((const T*)v, count, count_stride, \
+      count_head_stride, q_len, q_heads, kv_heads, head_dim, seq_len, (TO*)out)
+  if (dtype == OC_F32 && out_dtype == OC_F32) OC_EHM(float, float);
+  else if (dtype == OC_F32 && out_dtype == OC_BF16) OC_EHM(float, __nv_bfloat16);
+  else if (dtype == OC_BF16 && out_dtype == OC_F32) OC_EHM(__nv_bfloat16, float);
+  else if (dtype == OC_BF16 && out_dtype == OC_BF16) OC_EHM(__nv_bfloat16, __nv_bfloat16);
+  else return set_error(OC_ERR_DTYPE, "oc_empty_heads_mean: dtype %d / %d", dtype, out_dtype);
+#undef OC_EHM
+  return check_launch("empty_heads_mean_kernel");
+}
+
+namespace oc {
+int attn_status(int* status, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_attn_status, sizeof(int));
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  }
+  return OC_OK;
+}
+}  // namespace oc

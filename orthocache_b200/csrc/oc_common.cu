@@ -64,3 +64,46 @@ int oc_stratified_bucket(int nb, int gmax) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Tensor-map encoding through the driver entry point.
+// ---------------------------------------------------------------------------
+#include "oc_tma.cuh"
+
+namespace oc {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
+                  uint64_t rows, uint32_t box_cols, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
+}  // namespace oc
+
+extern "C" int oc_device_status(int reset) {
+  int s1 = 0, s2 = 0;
+  int rc = oc::score_status(&s1, reset);
+  if (rc) return rc;
+  rc = oc::attn_status(&s2, reset);
+  if (rc) return rc;
+  return s1 | (s2 << 1);
+}

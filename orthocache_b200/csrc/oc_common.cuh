@@ -19,6 +19,10 @@ namespace oc {
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 int device_sm_count();
+// Device-side error status of the pipelined kernels (a bounded wait gave up):
+// copies it to *status (0 = none) and clears it if reset.  Synchronous.
+int score_status(int* status, int reset);
+int attn_status(int* status, int reset);
 
 #define OC_REQUIRE(cond, code, ...)                                   \
   do {                                                                \

@@ -35,6 +35,7 @@
 //
 // One CTA scores one (batch, block, kv-head) tile of 512 x D keys.
 #include "oc_common.cuh"
+#include "oc_tma.cuh"
 
 #include <math.h>
 
@@ -73,10 +74,20 @@ struct ScoreArgs {
 // (spectral_energy.py:150-177), its max (:195), ζ (:138) and the keep bit
 // (:196, :231-234).
 // ---------------------------------------------------------------------------
-template <typename T>
+// Synchronisation of a 256-thread group: the whole CTA, or one named barrier.
+struct CtaSync {
+  __device__ void operator()() const { __syncthreads(); }
+};
+struct GroupSync {
+  int id;  // named barrier 1 or 2
+  __device__ void operator()() const { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
+};
+
+template <typename T, typename Sync = CtaSync>
 __device__ void score_epilogue(const ScoreArgs& a, int b, int j, int h,
-                               const float* dc_coef, const float* band, float* red) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+                               const float* dc_coef, const float* band, float* red,
+                               int tid = threadIdx.x, Sync sync = Sync()) {
+  const int lane = tid & 31, warp = tid >> 5;
   const int D = a.D;
   const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
   if (a.dc)
@@ -109,13 +120,11 @@ __device__ void score_epilogue(const ScoreArgs& a, int b, int j, int h,
       bmax = fmaxf(bmax, bound);
     }
     if (lane == 0) red[warp] = bmax;
-    __syncthreads();
-    if (tid == 0) {
-      for (int w = 1; w < kThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
-      red[0] = bmax;
-    }
-    __syncthreads();
+    sync();
     bmax = red[0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
+    sync();  // red is reused by the caller
   }
   if (tid == 0) {
     const float z = band[2] / (band[0] + 1e-6f);  // (:138)
@@ -187,13 +196,18 @@ score_partial_kernel(ScoreArgs a) {
 #pragma unroll
   for (int v = 0; v < VEC; ++v) colsum[v] = 0.f;
 
+  // Software pipeline: the 8 loads of item it+1 are in flight while item it
+  // is transformed.
+  uint4 raw[8], nxt[8];
+#pragma unroll
+  for (int ih = 0; ih < 8; ++ih) raw[ih] = ldg_stream(base + (size_t)(ih * 64 + row0) * tok_stride);
 #pragma unroll
   for (int it = 0; it < ITEMS; ++it) {
-    const int ilo = row0 + it * STEP;
-    uint4 raw[8];
+    if (it + 1 < ITEMS) {
+      const int ilo_n = row0 + (it + 1) * STEP;
 #pragma unroll
-    for (int ih = 0; ih < 8; ++ih)
-      raw[ih] = ldg_stream(base + (size_t)(ih * 64 + ilo) * tok_stride);
+      for (int ih = 0; ih < 8; ++ih) nxt[ih] = ldg_stream(base + (size_t)(ih * 64 + ilo_n) * tok_stride);
+    }
     {
       float x[8][VEC];
 #pragma unroll
@@ -221,6 +235,10 @@ score_partial_kernel(ScoreArgs a) {
         grp[6] = fmaf(c6, c6, grp[6]);
         grp[7] = fmaf(c7, c7, grp[7]);
       }
+    }
+    if (it + 1 < ITEMS) {
+#pragma unroll
+      for (int ih = 0; ih < 8; ++ih) raw[ih] = nxt[ih];
     }
   }
 
@@ -272,6 +290,198 @@ score_partial_kernel(ScoreArgs a) {
   }
   __syncthreads();
   score_epilogue<T>(a, b, j, h, s_dc, s_band, s_red);
+}
+
+
+// ---------------------------------------------------------------------------
+// Partial-transform scorer, bfloat16 keys, bulk-tensor pipeline.
+//
+// Persistent grid, one CTA per SM.  The unit of work is a slab of 512 tokens
+// x 64 channels of one (batch, block, kv head) tile (64 KB); a tile of D
+// channels is D / 64 consecutive slabs.  Thread 0 keeps kStages slabs in
+// flight with 2-D tensor loads (two 256-row boxes per slab) into a ring of
+// shared-memory stages, each completed on its own mbarrier.  The 256 threads
+// transform a slab straight out of shared memory (thread = 8 channels x 2
+// inner offsets), then the stage is refilled with the slab kStages ahead.
+// Band sums and the DC column sums accumulate across the slabs of a tile; the
+// tile's epilogue (bound, ζ, keep) runs after its last slab.
+// ---------------------------------------------------------------------------
+constexpr int kStages = 3;
+constexpr int kSlabC = 64;                                  // channels per slab
+constexpr int kSlabB = kBlock * kSlabC * 2;                 // bytes per slab (bf16)
+
+__device__ int g_score_status = 0;
+
+template <int D>
+__global__ void __launch_bounds__(2 * kThreads, 1)
+score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_tiles) {
+  constexpr int PARTS = D / kSlabC;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kStages];
+  // per consumer group scratch
+  __shared__ float s_part[2][kThreads / 32][kSlabC];
+  __shared__ float s_mean[2][kSlabC];
+  __shared__ float s_dc[2][D];
+  __shared__ float s_grp[2][kThreads / 32][9];
+  __shared__ float s_band[2][4];
+  __shared__ float s_red[2][kThreads / 32];
+  __shared__ int s_abort[2];
+
+  const int grp_id = threadIdx.x / kThreads;      // consumer group 0 / 1
+  const int tid = threadIdx.x % kThreads;         // thread within the group
+  const int lane = tid & 31, warp = tid >> 5;
+  const GroupSync gsync{1 + grp_id};
+  const int cg = tid & 7;      // 8 bf16 channels
+  const int row0 = tid >> 3;   // inner offsets row0 and row0 + 32
+  const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int n_units = my_tiles * PARTS;
+
+  // Unit k of this CTA = slab (k % PARTS) of its tile (k / PARTS); stage k % kStages.
+  auto issue = [&](int k) {
+    const int t = blockIdx.x + (k / PARTS) * gridDim.x;
+    const int part = k % PARTS;
+    const int h = t % a.H;
+    const int j = (t / a.H) % a.nb;
+    const int b = t / (a.H * a.nb);
+    uint8_t* dst = smem + (size_t)(k % kStages) * kSlabB;
+    uint64_t* bar = &full[k % kStages];
+    const int x = h * D + part * kSlabC;
+    const int y = b * a.S + j * kBlock;
+    mbar_expect_tx(bar, kSlabB);
+    tma_load_2d(dst, &kmap, bar, x, y);
+    tma_load_2d(dst + kSlabB / 2, &kmap, bar, x, y + kBlock / 2);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
+  }
+  if (tid == 0) s_abort[grp_id] = 0;
+  __syncthreads();
+
+  // Group g owns the tiles with (tile index within the CTA) % 2 == g.
+  for (int tile = grp_id; tile < my_tiles; tile += 2) {
+    const int t = blockIdx.x + tile * gridDim.x;
+    const int h = t % a.H;
+    const int j = (t / a.H) % a.nb;
+    const int b = t / (a.H * a.nb);
+    float grp[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) grp[q] = 0.f;
+    float edc = 0.f;  // DC energy of this thread's channels (tid < 64)
+    for (int part = 0; part < PARTS; ++part) {
+      const int k = tile * PARTS + part;
+      const int stage = k % kStages;
+      if (!mbar_wait(&full[stage], (k / kStages) & 1)) s_abort[grp_id] = 1;
+      gsync();
+      if (s_abort[grp_id]) {  // a copy never completed: record it and stop (no spin)
+        if (tid == 0) atomicExch(&g_score_status, 1);
+        return;
+      }
+      const uint8_t* slab = smem + (size_t)stage * kSlabB;
+      float y0[2][8];
+      float colsum[8];
+#pragma unroll
+      for (int v = 0; v < 8; ++v) colsum[v] = 0.f;
+#pragma unroll
+      for (int it = 0; it < 2; ++it) {
+        const int ilo = row0 + 32 * it;
+        float x[8][8];
+#pragma unroll
+        for (int ih = 0; ih < 8; ++ih) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * (kSlabC * 2) + cg * 16);
+          unpack16<__nv_bfloat16>(raw, x[ih]);
+        }
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          float a0 = x[0][v] + x[1][v], a1 = x[0][v] - x[1][v];  // h = 64
+          float a2 = x[2][v] + x[3][v], a3 = x[2][v] - x[3][v];
+          float a4 = x[4][v] + x[5][v], a5 = x[4][v] - x[5][v];
+          float a6 = x[6][v] + x[7][v], a7 = x[6][v] - x[7][v];
+          float b0 = a0 + a2, b2 = a0 - a2, b1 = a1 + a3, b3 = a1 - a3;  // h = 128
+          float b4 = a4 + a6, b6 = a4 - a6, b5 = a5 + a7, b7 = a5 - a7;
+          float c0 = b0 + b4, c4 = b0 - b4, c1 = b1 + b5, c5 = b1 - b5;  // h = 256
+          float c2 = b2 + b6, c6 = b2 - b6, c3 = b3 + b7, c7 = b3 - b7;
+          y0[it][v] = c0;
+          colsum[v] += c0;
+          grp[1] = fmaf(c1, c1, grp[1]);
+          grp[2] = fmaf(c2, c2, grp[2]);
+          grp[3] = fmaf(c3, c3, grp[3]);
+          grp[4] = fmaf(c4, c4, grp[4]);
+          grp[5] = fmaf(c5, c5, grp[5]);
+          grp[6] = fmaf(c6, c6, grp[6]);
+          grp[7] = fmaf(c7, c7, grp[7]);
+        }
+      }
+      // Column sums: the 4 lanes of a warp with the same cg, then 8 warps.
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        float cs = colsum[v];
+        cs += __shfl_xor_sync(0xffffffffu, cs, 8);
+        cs += __shfl_xor_sync(0xffffffffu, cs, 16);
+        colsum[v] = cs;
+      }
+      if (lane < 8) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) s_part[grp_id][warp][cg * 8 + v] = colsum[v];
+      }
+      gsync();  // the stage has been read by every thread of the group
+      if (tid == 0 && k + kStages < n_units) {
+        fence_proxy_async();
+        issue(k + kStages);
+      }
+      if (tid < kSlabC) {
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) sum += s_part[grp_id][w][tid];
+        s_mean[grp_id][tid] = sum * (1.0f / 64.0f);
+        const float dcv = sum / kNorm;
+        s_dc[grp_id][part * kSlabC + tid] = dcv;
+        edc = fmaf(dcv, dcv, edc);
+      }
+      gsync();
+#pragma unroll
+      for (int it = 0; it < 2; ++it)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float dlt = y0[it][v] - s_mean[grp_id][cg * 8 + v];
+          grp[0] = fmaf(dlt, dlt, grp[0]);
+        }
+    }
+    // Tile epilogue: group energies (8) and the DC energy, reduced over the group.
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float sq = warp_sum(grp[q]);
+      if (lane == 0) s_grp[grp_id][warp][q] = sq;
+    }
+    {
+      const float sq = warp_sum(edc);
+      if (lane == 0) s_grp[grp_id][warp][8] = sq;
+    }
+    gsync();
+    if (warp == 0) {
+      // lane q < 9 sums column q over the 8 warps
+      float v = 0.f;
+      if (lane < 9)
+        for (int w = 0; w < kThreads / 32; ++w) v += s_grp[grp_id][w][lane];
+      float g[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, v, q) * 0.125f;
+      const float e_dc = __shfl_sync(0xffffffffu, v, 8);
+      if (lane == 0) {
+        float e_ac = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) e_ac += g[q];
+        s_band[grp_id][0] = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
+        s_band[grp_id][1] = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
+        s_band[grp_id][2] = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
+        s_band[grp_id][3] = e_ac;
+      }
+    }
+    gsync();
+    score_epilogue<__nv_bfloat16, GroupSync>(a, b, j, h, s_dc[grp_id], s_band[grp_id], s_red[grp_id], tid, gsync);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -386,9 +596,32 @@ bool bands_partial_ok(const Bands& bd) {
   return true;
 }
 
+template <int D>
+int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
+  CUtensorMap map;
+  const uint64_t cols = (uint64_t)a.H * D;
+  const uint64_t rows = (uint64_t)ntiles / ((uint64_t)a.H * a.nb) * a.S;  // B * S
+  int rc = encode_map_2d(&map, a.keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, kSlabC, kBlock / 2);
+  if (rc) return set_error(OC_ERR_CUDA, "oc_score_blocks: tensor map encode failed (%d)", rc);
+  const int smem = kStages * kSlabB;
+  cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
+  score_tma_kernel<D><<<grid, 2 * kThreads, smem, st>>>(map, a, ntiles);
+  return check_launch("score_tma_kernel");
+}
+
 template <typename T>
 int launch_score(const ScoreArgs& a, int mode, int ncta, cudaStream_t st) {
-  if (mode == 1) {
+  if constexpr (Elem<T>::kCode == OC_BF16) {
+    if (mode == 1) {
+      switch (a.D) {
+        case 64: return launch_tma<64>(a, ncta, st);
+        case 128: return launch_tma<128>(a, ncta, st);
+        case 256: return launch_tma<256>(a, ncta, st);
+      }
+    }
+  }
+  if (mode == 1 || mode == 3) {
     switch (a.D) {
       case 64: score_partial_kernel<T, 64><<<ncta, kThreads, 0, st>>>(a); break;
       case 128: score_partial_kernel<T, 128><<<ncta, kThreads, 0, st>>>(a); break;
@@ -454,9 +687,9 @@ extern "C" int oc_score_blocks(const void* keys, const void* q, int dtype,
     OC_REQUIRE(bd.lo[i] >= 0 && bd.hi[i] <= kBlock && bd.lo[i] <= bd.hi[i], OC_ERR_SHAPE,
                "oc_score_blocks: band %d = [%d, %d) outside [0, 512)", i, bd.lo[i], bd.hi[i]);
   if (mode == 0) mode = bands_partial_ok(bd) ? 1 : 2;
-  OC_REQUIRE(mode == 1 || mode == 2, OC_ERR_SHAPE, "oc_score_blocks: mode %d", mode);
+  OC_REQUIRE(mode >= 1 && mode <= 3, OC_ERR_SHAPE, "oc_score_blocks: mode %d", mode);
   OC_REQUIRE(mode == 2 || bands_partial_ok(bd), OC_ERR_SHAPE,
-             "oc_score_blocks: mode 1 needs band edges in {0, 1, 64k}");
+             "oc_score_blocks: modes 1 and 3 need band edges in {0, 1, 64k}");
   const int nb = seq_len / kBlock;
   const int64_t ncta = (int64_t)batch * nb * kv_heads;
   if (ncta == 0) return OC_OK;
@@ -471,3 +704,16 @@ extern "C" int oc_score_blocks(const void* keys, const void* q, int dtype,
   if (dtype == OC_F32) return launch_score<float>(a, mode, (int)ncta, st);
   return launch_score<__nv_bfloat16>(a, mode, (int)ncta, st);
 }
+
+namespace oc {
+int score_status(int* status, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_score_status, sizeof(int));
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_score_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  }
+  return OC_OK;
+}
+}  // namespace oc

@@ -100,6 +100,7 @@ def orthocache_forward(q, keys, values, block_size: int = 512, zeta_max: float =
         perm, count = _core.compact_per_head(keep)
         out = _core.attend(qq, k, v, perm, count, block_size, idx_stride=H * num_blocks,
                            idx_head_stride=num_blocks, count_stride=H, count_head_stride=1)
+        _core.fill_empty_heads(out, v, count, H, 1)
         un, uc = _core.compact(keep, batched=True)
         retained = int(uc.sum().item()) if batched else int(uc[0].item())
     _sync()

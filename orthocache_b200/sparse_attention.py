@@ -4,9 +4,8 @@ The reference masks evicted logits with -1e9 per (block, head) and takes a
 softmax over all tokens (``sparse_attention.py:5-64``).  Here each head's
 kept blocks are compacted into their own index list and only those blocks are
 read (per-head indirect attention); the softmax over the kept tokens is the
-same.  One divergence, by construction: a head whose mask keeps no block gets
-zeros, where the reference's all -1e9 row degenerates to the uniform average
-of every value row.
+same.  A head whose mask keeps no block gets the uniform average of all its
+value rows, which is what the reference's all -1e9 logit row gives.
 """
 from __future__ import annotations
 
@@ -28,6 +27,7 @@ def jax_block_sparse_attention(q, keys, values, block_mask, block_size: int = 51
     perm, count = _core.compact_per_head(m)
     out = _core.attend(qq, k, v, perm, count, block_size, idx_stride=Hkv * nb, idx_head_stride=nb,
                        count_stride=Hkv, count_head_stride=1)
+    _core.fill_empty_heads(out, v, count, Hkv, 1)
     return out if batched else out[0]
 
 

@@ -79,6 +79,10 @@ def score_blocks(keys, q=None, tau=-math.inf, zeta_max=math.inf, block_size=BLOC
             raise ValueError("bounds need q")
         out["bounds"] = torch.empty((B, Sq, nb, Hq), **f32)
     keep = torch.empty((B, nb, H), dtype=torch.uint8, device=dev) if "keep" in want else None
+    if B * nb * H == 0:
+        if keep is not None:
+            out["keep"] = keep.bool()
+        return out if batched else {n: t[0] for n, t in out.items()}
     _lib.call("oc_score_blocks", _lib.ptr(k), _lib.ptr(qq), _lib.dtype_code(k),
               B, S, H, D, Sq, Hq,
               int(band_low[0]), int(band_low[1]), int(band_mid[0]), int(band_mid[1]),

@@ -202,3 +202,14 @@ def test_decode_step_cabi_vs_oracle(nb, hq, hkv, evict):
     assert np.array_equal(host(perm), rp)
     ref = O.indirect_attention(qf, kf, vf, rp, rn)
     np.testing.assert_allclose(host(out), ref, rtol=ATT_RTOL, atol=ATT_ATOL)
+
+
+def test_sparse_head_with_no_kept_block_is_uniform():
+    """sparse_attention.py:49-57: a head whose blocks are all masked gets the
+    uniform softmax over all tokens, i.e. the mean of its value rows."""
+    import orthocache_b200 as oc
+    rs = np.random.RandomState(8)
+    q, k, v = rand_qkv(rs, 2, 4, 2, 64, 4)
+    m = np.array([[1, 0], [0, 0], [1, 0], [0, 0]], bool)  # head 1 keeps nothing
+    sp = oc.jax_block_sparse_attention(dev(q), dev(k), dev(v), dev(m), 512)
+    np.testing.assert_allclose(host(sp), O.block_sparse_attention(q, k, v, m), rtol=2e-4, atol=2e-4)

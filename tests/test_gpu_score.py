@@ -95,7 +95,7 @@ CASES = [  # (nb, Hkv, Hq, Sq, D, dtype, smooth_frac, mid_frac)
 
 
 @pytest.mark.parametrize("case", CASES)
-@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("mode", [1, 2, 3])
 def test_scorer_vs_oracle(case, mode):
     from orthocache_b200 import synthetic as syn, score_blocks
     nb, hkv, hq, sq, d, dt, fs, fm = case
@@ -152,3 +152,23 @@ def test_scorer_edge_errors():
         score_blocks(torch.zeros(512, 2, 64, device="cuda"), torch.zeros(1, 3, 64, device="cuda"))
     r = score_blocks(torch.zeros(0, 2, 64, device="cuda"), want=("zeta",))
     assert r["zeta"].shape == (0, 2)
+
+
+def test_tma_scorer_status_clean_and_matches_register_path():
+    """The bulk-tensor pipeline and the per-thread-load scorer agree bit for bit
+    on a multi-tile, multi-batch input, and no bounded wait gave up."""
+    from orthocache_b200 import synthetic as syn, score_blocks, _lib
+    nb = 300  # > SM count: several tiles per CTA, uneven split
+    k = syn.make_keys(nb, 4, 128, syn.block_kinds(nb, 0.5, seed=9), seed=9, device="cuda")
+    q = syn.make_queries(1, 16, 128, seed=9, device="cuda")
+    kb = torch.stack([k, k.flip(0)])
+    qb = torch.stack([q, -q])
+    want = ("dc", "e_low", "e_mid", "e_high", "zeta", "bound_max", "keep")
+    r1 = score_blocks(kb, qb, tau=0.0, zeta_max=5.0, want=want, mode=1)
+    r3 = score_blocks(kb, qb, tau=0.0, zeta_max=5.0, want=want, mode=3)
+    for n in want:
+        if n in ("keep",):
+            assert torch.equal(r1[n], r3[n])
+        else:
+            torch.testing.assert_close(r1[n], r3[n], rtol=2e-6, atol=1e-5)
+    assert _lib.load().oc_device_status(1) == 0
