@@ -85,7 +85,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
-                  uint64_t rows, uint32_t box_cols, uint32_t box_rows) {
+                  uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
   auto fn = encode_fn();
   if (!fn) return -1;
   cuuint64_t dims[2] = {cols, rows};
@@ -93,7 +93,8 @@ int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, in
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return (int)r;
 }
 

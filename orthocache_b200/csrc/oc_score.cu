@@ -316,27 +316,24 @@ template <int D>
 __global__ void __launch_bounds__(2 * kThreads, 1)
 score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_tiles) {
   constexpr int PARTS = D / kSlabC;
-  extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr int kW = kThreads / 32;  // warps per consumer group
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 128-byte swizzled stages must start on a 1024-byte boundary.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full[kStages];
-  // per consumer group scratch
-  __shared__ float s_part[2][kThreads / 32][kSlabC];
-  __shared__ float s_mean[2][kSlabC];
-  __shared__ float s_dc[2][D];
-  __shared__ float s_grp[2][kThreads / 32][9];
+  __shared__ int s_rel[kStages];                 // warps done with a stage
+  __shared__ float s_dc[2][2][D];                // [group][tile parity][channel]
+  __shared__ float s_grp[2][2][kW][9];           // per-warp group energies + DC energy
   __shared__ float s_band[2][4];
-  __shared__ float s_red[2][kThreads / 32];
-  __shared__ int s_abort[2];
+  __shared__ float s_red[2][kW];
 
-  const int grp_id = threadIdx.x / kThreads;      // consumer group 0 / 1
-  const int tid = threadIdx.x % kThreads;         // thread within the group
-  const int lane = tid & 31, warp = tid >> 5;
-  const GroupSync gsync{1 + grp_id};
-  const int cg = tid & 7;      // 8 bf16 channels
-  const int row0 = tid >> 3;   // inner offsets row0 and row0 + 32
+  const int gid = threadIdx.x / kThreads;        // consumer group 0 / 1
+  const int tid = threadIdx.x % kThreads;
+  const int lane = tid & 31, warp = tid >> 5;    // warp w owns channels 8w .. 8w+7 of a slab
+  const GroupSync gsync{1 + gid};
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int n_units = my_tiles * PARTS;
 
-  // Unit k of this CTA = slab (k % PARTS) of its tile (k / PARTS); stage k % kStages.
   auto issue = [&](int k) {
     const int t = blockIdx.x + (k / PARTS) * gridDim.x;
     const int part = k % PARTS;
@@ -353,15 +350,15 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
     fence_mbar_init();
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
   }
-  if (tid == 0) s_abort[grp_id] = 0;
   __syncthreads();
 
-  // Group g owns the tiles with (tile index within the CTA) % 2 == g.
-  for (int tile = grp_id; tile < my_tiles; tile += 2) {
+  int tl = 0;  // tiles done by this group (buffer parity)
+  for (int tile = gid; tile < my_tiles; tile += 2, ++tl) {
+    const int buf = tl & 1;
     const int t = blockIdx.x + tile * gridDim.x;
     const int h = t % a.H;
     const int j = (t / a.H) % a.nb;
@@ -369,14 +366,12 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     float grp[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) grp[q] = 0.f;
-    float edc = 0.f;  // DC energy of this thread's channels (tid < 64)
+    float edc = 0.f;
     for (int part = 0; part < PARTS; ++part) {
       const int k = tile * PARTS + part;
       const int stage = k % kStages;
-      if (!mbar_wait(&full[stage], (k / kStages) & 1)) s_abort[grp_id] = 1;
-      gsync();
-      if (s_abort[grp_id]) {  // a copy never completed: record it and stop (no spin)
-        if (tid == 0) atomicExch(&g_score_status, 1);
+      if (!mbar_wait(&full[stage], (k / kStages) & 1)) {  // a copy never completed: record, stop
+        atomicExch(&g_score_status, 1);
         return;
       }
       const uint8_t* slab = smem + (size_t)stage * kSlabB;
@@ -386,11 +381,12 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       for (int v = 0; v < 8; ++v) colsum[v] = 0.f;
 #pragma unroll
       for (int it = 0; it < 2; ++it) {
-        const int ilo = row0 + 32 * it;
+        const int ilo = lane + 32 * it;
+        const int chunk = (warp ^ (ilo & 7)) * 16;  // 128-byte swizzle of the tensor load
         float x[8][8];
 #pragma unroll
         for (int ih = 0; ih < 8; ++ih) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * (kSlabC * 2) + cg * 16);
+          const uint4 raw = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * 128 + chunk);
           unpack16<__nv_bfloat16>(raw, x[ih]);
         }
 #pragma unroll
@@ -414,73 +410,114 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
           grp[7] = fmaf(c7, c7, grp[7]);
         }
       }
-      // Column sums: the 4 lanes of a warp with the same cg, then 8 warps.
+      // This warp is done with the stage; the last of the group's 8 warps refills it.
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&s_rel[stage], 1) == kW - 1) {
+          s_rel[stage] = 0;
+          if (k + kStages < n_units) {
+            fence_proxy_async();
+            issue(k + kStages);
+          }
+        }
+      }
+      // Column sums over the 64 inner offsets (2 per lane): warp shuffles only.
 #pragma unroll
       for (int v = 0; v < 8; ++v) {
         float cs = colsum[v];
-        cs += __shfl_xor_sync(0xffffffffu, cs, 8);
-        cs += __shfl_xor_sync(0xffffffffu, cs, 16);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
         colsum[v] = cs;
       }
-      if (lane < 8) {
 #pragma unroll
-        for (int v = 0; v < 8; ++v) s_part[grp_id][warp][cg * 8 + v] = colsum[v];
-      }
-      gsync();  // the stage has been read by every thread of the group
-      if (tid == 0 && k + kStages < n_units) {
-        fence_proxy_async();
-        issue(k + kStages);
-      }
-      if (tid < kSlabC) {
-        float sum = 0.f;
-#pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) sum += s_part[grp_id][w][tid];
-        s_mean[grp_id][tid] = sum * (1.0f / 64.0f);
-        const float dcv = sum / kNorm;
-        s_dc[grp_id][part * kSlabC + tid] = dcv;
-        edc = fmaf(dcv, dcv, edc);
-      }
-      gsync();
-#pragma unroll
-      for (int it = 0; it < 2; ++it)
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const float dlt = y0[it][v] - s_mean[grp_id][cg * 8 + v];
-          grp[0] = fmaf(dlt, dlt, grp[0]);
+      for (int v = 0; v < 8; ++v) {
+        const float mean = colsum[v] * (1.0f / 64.0f);
+        const float d0 = y0[0][v] - mean, d1 = y0[1][v] - mean;
+        grp[0] = fmaf(d0, d0, grp[0]);
+        grp[0] = fmaf(d1, d1, grp[0]);
+        if (lane == v) {
+          const float dcv = colsum[v] / kNorm;
+          s_dc[gid][buf][part * kSlabC + warp * 8 + v] = dcv;
+          edc = fmaf(dcv, dcv, edc);
         }
+      }
     }
-    // Tile epilogue: group energies (8) and the DC energy, reduced over the group.
+    // Tile epilogue.
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const float sq = warp_sum(grp[q]);
-      if (lane == 0) s_grp[grp_id][warp][q] = sq;
+      if (lane == 0) s_grp[gid][buf][warp][q] = sq;
     }
     {
       const float sq = warp_sum(edc);
-      if (lane == 0) s_grp[grp_id][warp][8] = sq;
+      if (lane == 0) s_grp[gid][buf][warp][8] = sq;
     }
     gsync();
+    const int rows = a.q ? a.Sq * a.G : 0;
     if (warp == 0) {
-      // lane q < 9 sums column q over the 8 warps
       float v = 0.f;
       if (lane < 9)
-        for (int w = 0; w < kThreads / 32; ++w) v += s_grp[grp_id][w][lane];
+        for (int w = 0; w < kW; ++w) v += s_grp[gid][buf][w][lane];
       float g[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, v, q) * 0.125f;
       const float e_dc = __shfl_sync(0xffffffffu, v, 8);
-      if (lane == 0) {
-        float e_ac = 0.f;
+      float e_ac = 0.f;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) e_ac += g[q];
-        s_band[grp_id][0] = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
-        s_band[grp_id][1] = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
-        s_band[grp_id][2] = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
-        s_band[grp_id][3] = e_ac;
+      for (int q = 0; q < 8; ++q) e_ac += g[q];
+      const float e_lo = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
+      const float e_mi = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
+      const float e_hi = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
+      if (rows <= 8) {
+        // Small query tile: warp 0 finishes the tile alone; the other warps go on.
+        const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
+        const float* dcp = s_dc[gid][buf];
+        if (a.dc)
+          for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
+        float bmax = -INFINITY;
+        if (a.q) {
+          const float sqrt_d = sqrtf((float)D);
+          const float resid_scale = sqrtf(e_ac);
+          const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+          for (int r = 0; r < rows; ++r) {
+            const int s = r / a.G, gq = r - s * a.G;
+            const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D;
+            float dot = 0.f, nrm = 0.f;
+#pragma unroll
+            for (int c = lane; c < D; c += 32) {
+              const float qv = __bfloat162float(qr[c]);
+              dot = fmaf(qv, dcp[c] / kNorm, dot);  // block mean = DC / sqrt(512)
+              nrm = fmaf(qv, qv, nrm);
+            }
+            dot = warp_sum(dot);
+            nrm = warp_sum(nrm);
+            const float bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
+            if (a.bounds && lane == 0)
+              a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + gq] = bound;
+            bmax = fmaxf(bmax, bound);
+          }
+        }
+        if (lane == 0) {
+          const float z = e_hi / (e_lo + 1e-6f);
+          if (a.e_low) a.e_low[cell] = e_lo;
+          if (a.e_mid) a.e_mid[cell] = e_mi;
+          if (a.e_high) a.e_high[cell] = e_hi;
+          if (a.zeta) a.zeta[cell] = z;
+          if (a.q && a.bound_max) a.bound_max[cell] = bmax;
+          if (a.keep) a.keep[cell] = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
+        }
+      } else if (lane == 0) {
+        s_band[gid][0] = e_lo;
+        s_band[gid][1] = e_mi;
+        s_band[gid][2] = e_hi;
+        s_band[gid][3] = e_ac;
       }
     }
-    gsync();
-    score_epilogue<__nv_bfloat16, GroupSync>(a, b, j, h, s_dc[grp_id], s_band[grp_id], s_red[grp_id], tid, gsync);
+    if (rows > 8) {  // many query rows: the whole group computes the bound
+      gsync();
+      score_epilogue<__nv_bfloat16, GroupSync>(a, b, j, h, s_dc[gid][buf], s_band[gid], s_red[gid], tid, gsync);
+    }
   }
 }
 
@@ -601,9 +638,9 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   CUtensorMap map;
   const uint64_t cols = (uint64_t)a.H * D;
   const uint64_t rows = (uint64_t)ntiles / ((uint64_t)a.H * a.nb) * a.S;  // B * S
-  int rc = encode_map_2d(&map, a.keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, kSlabC, kBlock / 2);
+  int rc = encode_map_2d(&map, a.keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, kSlabC, kBlock / 2, true);
   if (rc) return set_error(OC_ERR_CUDA, "oc_score_blocks: tensor map encode failed (%d)", rc);
-  const int smem = kStages * kSlabB;
+  const int smem = kStages * kSlabB + 1024;
   cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
   score_tma_kernel<D><<<grid, 2 * kThreads, smem, st>>>(map, a, ntiles);

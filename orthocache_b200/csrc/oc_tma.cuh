@@ -76,7 +76,9 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 
 // Host: encode a row-major 2-D tensor map (cols innermost).  Returns 0 or a
 // CUresult code.
+// swizzle128: 16-byte chunk c of box row r lands at chunk c ^ (r % 8) within
+// each 1024-byte group of 8 rows (needs box_cols * elem_bytes == 128).
 int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
-                  uint64_t rows, uint32_t box_cols, uint32_t box_rows);
+                  uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128 = false);
 
 }  // namespace oc
