@@ -261,6 +261,12 @@ attn_partial_kernel(AttnArgs a) {
 // ---------------------------------------------------------------------------
 constexpr int kAStages = 3;
 constexpr int kAStageBytes = 65536;  // 2 * CH * D * 2 with CH * D = 16384
+constexpr int kAThreads = 512;
+constexpr int kAWarps = kAThreads / 32;
+
+struct CtaBarrier {
+  __device__ void operator()() const { __syncthreads(); }
+};
 
 __device__ int g_attn_status = 0;
 
@@ -270,26 +276,29 @@ struct GroupSync {
 };
 
 template <int D, int RT>
-__global__ void __launch_bounds__(2 * kThreads, 1)
+__global__ void __launch_bounds__(kAThreads, 1)
 attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
   constexpr int CH = 16384 / D;          // tokens per item (128 at D = 128)
   constexpr int VEC = 8;
   constexpr int LPR = D / VEC;
   constexpr int RPW = 32 / LPR;
-  constexpr int ROWS_PER_WARP = CH / kWarps;
+  constexpr int ROWS_PER_WARP = CH / kAWarps;
   constexpr int ITERS = ROWS_PER_WARP / RPW;
   constexpr int ROWB = D * 2;            // bytes per token row in shared memory
   static_assert(ROWS_PER_WARP % RPW == 0, "mapping");
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kAStages];
-  __shared__ float s_p[2][RT][CH];
-  __shared__ float s_m[2][RT], s_l[2][RT];
-  __shared__ float s_o[2][kWarps / 2][RT][D];
-  __shared__ int s_abort[2];
+  __shared__ float s_p[1][RT][CH];
+  __shared__ float s_m[1][RT], s_l[1][RT];
+  __shared__ float s_o[1][kAWarps / 2][RT][D];
+  __shared__ int s_abort[1];
 
-  const int gid = threadIdx.x / kThreads;
-  const int tid = threadIdx.x % kThreads, lane = tid & 31, warp = tid >> 5;
-  const GroupSync gsync{1 + gid};
+  // One group of 16 warps consumes every stage in ring order, so a wait on a
+  // stage always follows this CTA's own consumption of the stage's previous
+  // phase (no parity aliasing between independent consumers).
+  const int gid = 0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const CtaBarrier gsync;
   const int sub = lane / LPR, vl = lane % LPR, d0 = vl * VEC;
 
   auto issue = [&](int k) -> bool {
@@ -317,8 +326,7 @@ attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   if (tid == 0) s_abort[gid] = 0;
   __syncthreads();
 
-  // Group g takes this CTA's items k with k % 2 == g.
-  for (int k = gid;; k += 2) {
+  for (int k = 0;; ++k) {
     int b, item, h, rt;
     if (!decode_item(a, blockIdx.x + k * gridDim.x, b, item, h, rt)) break;
     const int stage = k % kAStages;
@@ -369,7 +377,7 @@ attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
       }
     }
     gsync();
-    for (int r = warp; r < RT; r += kWarps) {
+    for (int r = warp; r < RT; r += kAWarps) {
       float m = -INFINITY;
       for (int t = lane; t < CH; t += 32) m = fmaxf(m, s_p[gid][r][t]);
       m = warp_max(m);
@@ -410,29 +418,29 @@ attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         acc[r][e] = x;
       }
     // Cross-warp sum in two rounds through half-size scratch.
-    if (sub == 0 && warp >= kWarps / 2) {
+    if (sub == 0 && warp >= kAWarps / 2) {
 #pragma unroll
       for (int r = 0; r < RT; ++r)
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) s_o[gid][warp - kWarps / 2][r][d0 + e] = acc[r][e];
+        for (int e = 0; e < VEC; ++e) s_o[gid][warp - kAWarps / 2][r][d0 + e] = acc[r][e];
     }
     gsync();  // stage fully read; upper warps' sums visible
     if (tid == 0) {
       fence_proxy_async();
       issue(k + kAStages);
     }
-    if (sub == 0 && warp < kWarps / 2) {
+    if (sub == 0 && warp < kAWarps / 2) {
 #pragma unroll
       for (int r = 0; r < RT; ++r)
 #pragma unroll
         for (int e = 0; e < VEC; ++e) s_o[gid][warp][r][d0 + e] += acc[r][e];
     }
     gsync();
-    for (int x = tid; x < nr * D; x += kThreads) {
+    for (int x = tid; x < nr * D; x += kAThreads) {
       const int r = x / D, d = x - r * D;
       float sum = 0.f;
 #pragma unroll
-      for (int ww = 0; ww < kWarps / 2; ++ww) sum += s_o[gid][ww][r][d];
+      for (int ww = 0; ww < kAWarps / 2; ++ww) sum += s_o[gid][ww][r][d];
       a.ws_o[(part + r) * D + d] = valid ? sum : 0.f;
     }
     if (tid < nr) {
@@ -456,7 +464,7 @@ int launch_attn_tma(const AttnArgs& a, int rt, cudaStream_t st) {
 #define OC_ATMA(RTV)                                                                                   \
   do {                                                                                                 \
     cudaFuncSetAttribute(attn_tma_kernel<D, RTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    attn_tma_kernel<D, RTV><<<grid, 2 * kThreads, smem, st>>>(km, vm, a);                                  \
+    attn_tma_kernel<D, RTV><<<grid, kAThreads, smem, st>>>(km, vm, a);                                  \
   } while (0)
   if (rt == 1) OC_ATMA(1);
   else if (rt == 2) OC_ATMA(2);
@@ -830,3 +838,4 @@ int attn_status(int* status, int reset) {
   return OC_OK;
 }
 }  // namespace oc
+

@@ -307,30 +307,31 @@ score_partial_kernel(ScoreArgs a) {
 // tile's epilogue (bound, ζ, keep) runs after its last slab.
 // ---------------------------------------------------------------------------
 constexpr int kStages = 3;
+constexpr int kScoreThreads = 512;  // 16 warps consume every stage in order
 constexpr int kSlabC = 64;                                  // channels per slab
 constexpr int kSlabB = kBlock * kSlabC * 2;                 // bytes per slab (bf16)
 
 __device__ int g_score_status = 0;
 
 template <int D>
-__global__ void __launch_bounds__(2 * kThreads, 1)
+__global__ void __launch_bounds__(kScoreThreads, 1)
 score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_tiles) {
   constexpr int PARTS = D / kSlabC;
-  constexpr int kW = kThreads / 32;  // warps per consumer group
+  constexpr int kW = kScoreThreads / 32;  // 16 warps, each owns 4 channels of a slab
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte swizzled stages must start on a 1024-byte boundary.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full[kStages];
   __shared__ int s_rel[kStages];                 // warps done with a stage
-  __shared__ float s_dc[2][2][D];                // [group][tile parity][channel]
-  __shared__ float s_grp[2][2][kW][9];           // per-warp group energies + DC energy
-  __shared__ float s_band[2][4];
-  __shared__ float s_red[2][kW];
+  __shared__ float s_dc[2][D];                   // [tile parity][channel]
+  __shared__ float s_grp[2][kW][9];              // per-warp group energies + DC energy
+  __shared__ float s_band[4];
+  __shared__ float s_red[kThreads / 32];
+  __shared__ volatile int s_abort;
 
-  const int gid = threadIdx.x / kThreads;        // consumer group 0 / 1
-  const int tid = threadIdx.x % kThreads;
-  const int lane = tid & 31, warp = tid >> 5;    // warp w owns channels 8w .. 8w+7 of a slab
-  const GroupSync gsync{1 + gid};
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;    // warp w owns channels 4w .. 4w+3 of a slab
+  const GroupSync gsync{1};                      // warps 0-7 (the many-row epilogue)
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int n_units = my_tiles * PARTS;
 
@@ -352,12 +353,13 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
     fence_mbar_init();
+    s_abort = 0;
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
   }
   __syncthreads();
 
   int tl = 0;  // tiles done by this group (buffer parity)
-  for (int tile = gid; tile < my_tiles; tile += 2, ++tl) {
+  for (int tile = 0; tile < my_tiles; ++tile, ++tl) {
     const int buf = tl & 1;
     const int t = blockIdx.x + tile * gridDim.x;
     const int h = t % a.H;
@@ -370,27 +372,31 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     for (int part = 0; part < PARTS; ++part) {
       const int k = tile * PARTS + part;
       const int stage = k % kStages;
-      if (!mbar_wait(&full[stage], (k / kStages) & 1)) {  // a copy never completed: record, stop
-        atomicExch(&g_score_status, 1);
-        return;
+      // A copy that never completes sets the abort flag; every warp then skips
+      // ahead to the tile barrier and the CTA leaves together (no spin, no hang).
+      if (s_abort || !mbar_wait(&full[stage], (k / kStages) & 1)) {
+        s_abort = 1;
+        break;
       }
       const uint8_t* slab = smem + (size_t)stage * kSlabB;
-      float y0[2][8];
-      float colsum[8];
+      float y0[2][4];
+      float colsum[4];
 #pragma unroll
-      for (int v = 0; v < 8; ++v) colsum[v] = 0.f;
+      for (int v = 0; v < 4; ++v) colsum[v] = 0.f;
 #pragma unroll
       for (int it = 0; it < 2; ++it) {
         const int ilo = lane + 32 * it;
-        const int chunk = (warp ^ (ilo & 7)) * 16;  // 128-byte swizzle of the tensor load
-        float x[8][8];
+        // 128-byte swizzle of the tensor load: 16-byte chunk c of row r sits at c ^ (r % 8)
+        const int off = ((warp >> 1) ^ (ilo & 7)) * 16 + (warp & 1) * 8;
+        float x[8][4];
 #pragma unroll
         for (int ih = 0; ih < 8; ++ih) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * 128 + chunk);
-          unpack16<__nv_bfloat16>(raw, x[ih]);
+          const uint2 raw = *reinterpret_cast<const uint2*>(slab + (size_t)(ih * 64 + ilo) * 128 + off);
+          x[ih][0] = bf16lo(raw.x); x[ih][1] = bf16hi(raw.x);
+          x[ih][2] = bf16lo(raw.y); x[ih][3] = bf16hi(raw.y);
         }
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
+        for (int v = 0; v < 4; ++v) {
           float a0 = x[0][v] + x[1][v], a1 = x[0][v] - x[1][v];  // h = 64
           float a2 = x[2][v] + x[3][v], a3 = x[2][v] - x[3][v];
           float a4 = x[4][v] + x[5][v], a5 = x[4][v] - x[5][v];
@@ -410,13 +416,13 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
           grp[7] = fmaf(c7, c7, grp[7]);
         }
       }
-      // This warp is done with the stage; the last of the group's 8 warps refills it.
+      // This warp is done with the stage; the last of the 16 warps refills it.
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
         if (atomicAdd(&s_rel[stage], 1) == kW - 1) {
           s_rel[stage] = 0;
-          if (k + kStages < n_units) {
+          if (k + kStages < n_units && !s_abort) {
             fence_proxy_async();
             issue(k + kStages);
           }
@@ -424,21 +430,21 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       }
       // Column sums over the 64 inner offsets (2 per lane): warp shuffles only.
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
+      for (int v = 0; v < 4; ++v) {
         float cs = colsum[v];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
         colsum[v] = cs;
       }
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
+      for (int v = 0; v < 4; ++v) {
         const float mean = colsum[v] * (1.0f / 64.0f);
         const float d0 = y0[0][v] - mean, d1 = y0[1][v] - mean;
         grp[0] = fmaf(d0, d0, grp[0]);
         grp[0] = fmaf(d1, d1, grp[0]);
         if (lane == v) {
           const float dcv = colsum[v] / kNorm;
-          s_dc[gid][buf][part * kSlabC + warp * 8 + v] = dcv;
+          s_dc[buf][part * kSlabC + warp * 4 + v] = dcv;
           edc = fmaf(dcv, dcv, edc);
         }
       }
@@ -447,18 +453,22 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const float sq = warp_sum(grp[q]);
-      if (lane == 0) s_grp[gid][buf][warp][q] = sq;
+      if (lane == 0) s_grp[buf][warp][q] = sq;
     }
     {
       const float sq = warp_sum(edc);
-      if (lane == 0) s_grp[gid][buf][warp][8] = sq;
+      if (lane == 0) s_grp[buf][warp][8] = sq;
     }
-    gsync();
+    __syncthreads();
+    if (s_abort) {
+      if (tid == 0) atomicExch(&g_score_status, 1);
+      return;  // uniform: every thread passed the barrier above
+    }
     const int rows = a.q ? a.Sq * a.G : 0;
     if (warp == 0) {
       float v = 0.f;
       if (lane < 9)
-        for (int w = 0; w < kW; ++w) v += s_grp[gid][buf][w][lane];
+        for (int w = 0; w < kW; ++w) v += s_grp[buf][w][lane];
       float g[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, v, q) * 0.125f;
@@ -472,7 +482,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       if (rows <= 8) {
         // Small query tile: warp 0 finishes the tile alone; the other warps go on.
         const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
-        const float* dcp = s_dc[gid][buf];
+        const float* dcp = s_dc[buf];
         if (a.dc)
           for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
         float bmax = -INFINITY;
@@ -508,15 +518,15 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
           if (a.keep) a.keep[cell] = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
         }
       } else if (lane == 0) {
-        s_band[gid][0] = e_lo;
-        s_band[gid][1] = e_mi;
-        s_band[gid][2] = e_hi;
-        s_band[gid][3] = e_ac;
+        s_band[0] = e_lo;
+        s_band[1] = e_mi;
+        s_band[2] = e_hi;
+        s_band[3] = e_ac;
       }
     }
-    if (rows > 8) {  // many query rows: the whole group computes the bound
+    if (rows > 8 && tid < kThreads) {  // many query rows: warps 0-7 compute the bound
       gsync();
-      score_epilogue<__nv_bfloat16, GroupSync>(a, b, j, h, s_dc[gid][buf], s_band[gid], s_red[gid], tid, gsync);
+      score_epilogue<__nv_bfloat16, GroupSync>(a, b, j, h, s_dc[buf], s_band, s_red, tid, gsync);
     }
   }
 }
@@ -643,7 +653,7 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   const int smem = kStages * kSlabB + 1024;
   cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
-  score_tma_kernel<D><<<grid, 2 * kThreads, smem, st>>>(map, a, ntiles);
+  score_tma_kernel<D><<<grid, kScoreThreads, smem, st>>>(map, a, ntiles);
   return check_launch("score_tma_kernel");
 }
 
