@@ -208,6 +208,34 @@ int oc_empty_heads_mean(const void* v, int dtype, const int32_t* count, int coun
                         int head_dim, int seq_len, void* out, int out_dtype, oc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * oc_indirect_attention without a workspace argument.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when
+ * they run the attention (an allocator-free FFI host, a serving loop whose
+ * memory pool forbids allocations during a step, a process whose allocator
+ * is exhausted).  Same inputs, outputs and results as oc_indirect_attention;
+ * the scratch comes from a fixed 16 MiB device array that every GPU which
+ * loads this library holds until the process exits.  It never calls
+ * cudaMalloc or cudaFree.
+ *   - Shapes whose scratch need (oc_indirect_attention_workspace_bytes) is
+ *     above oc_indirect_attention_noalloc_max_scratch_bytes() are rejected
+ *     with OC_ERR_CAPACITY.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls on a device share the one array: calls whose kernels overlap
+ *     on the GPU (different streams, or other threads) race and corrupt each
+ *     other's results.  Serialise them.  Nothing in the array needs to start
+ *     at zero; it keeps the last call's contents.
+ */
+size_t oc_indirect_attention_noalloc_max_scratch_bytes(void);
+int oc_indirect_attention_noalloc(const void* q, const void* k, const void* v, int dtype,
+                                  const int32_t* idx, int idx_stride, int idx_head_stride,
+                                  const int32_t* count, int count_stride, int count_head_stride,
+                                  int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                  int seq_len, int block_size, int max_blocks,
+                                  void* out, int out_dtype, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * One decode step of the OrthoCache pipeline on the device: score (two-gate
  * keep mask), compact (perm, count) and attend over the retained blocks —
  * the path of pipeline.orthocache_forward(mode='compact')

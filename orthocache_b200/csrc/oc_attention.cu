@@ -23,6 +23,8 @@
 
 #include <math.h>
 
+#include <mutex>
+
 namespace oc {
 namespace {
 
@@ -839,3 +841,75 @@ int attn_status(int* status, int reset) {
 }
 }  // namespace oc
 
+// ---------------------------------------------------------------------------
+// Indirect attention without any allocation (no counterpart in the reference).
+//
+// Some callers cannot allocate device memory at the point where they run the
+// attention: code inside a custom memory pool or a framework that forbids
+// allocations during a decode step, an FFI host that has no CUDA allocator of
+// its own, or a process whose allocator is already exhausted.  For them this
+// entry point takes its scratch (the per-chunk (m, l, o) partials of the
+// split-KV attention) from a file-scope device array that exists on every GPU
+// that loads this library, for the life of the process.
+// ---------------------------------------------------------------------------
+namespace oc {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device.  Host code may
+// not use the symbol itself: on the host it names a stand-in, not GPU memory.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_indirect_attention_noalloc: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(OC_ERR_UNSUPPORTED, "oc_indirect_attention_noalloc: device %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(OC_ERR_CUDA, "oc_indirect_attention_noalloc: cudaGetSymbolAddress: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return OC_OK;
+}
+
+}  // namespace
+}  // namespace oc
+
+extern "C" size_t oc_indirect_attention_noalloc_max_scratch_bytes(void) { return oc::kNoAllocScratchBytes; }
+
+extern "C" int oc_indirect_attention_noalloc(const void* q, const void* k, const void* v, int dtype,
+                                             const int32_t* idx, int idx_stride, int idx_head_stride,
+                                             const int32_t* count, int count_stride, int count_head_stride,
+                                             int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                             int seq_len, int block_size, int max_blocks,
+                                             void* out, int out_dtype, oc_stream_t stream) {
+  OC_REQUIRE(out, OC_ERR_NULL, "oc_indirect_attention_noalloc: out is NULL");
+  OC_REQUIRE(batch >= 1 && q_len >= 1 && kv_heads >= 1 && q_heads >= kv_heads && q_heads % kv_heads == 0 &&
+                 block_size >= 64 && block_size % 64 == 0 && max_blocks >= 0,
+             OC_ERR_SHAPE, "oc_indirect_attention_noalloc: bad shape");
+  const size_t need = oc::attn_ws_bytes(batch, q_len, q_heads, kv_heads, head_dim, block_size, max_blocks);
+  OC_REQUIRE(need <= oc::kNoAllocScratchBytes, OC_ERR_CAPACITY,
+             "oc_indirect_attention_noalloc: this shape needs %zu bytes of scratch, above the fixed %zu-byte "
+             "limit; use oc_indirect_attention with a caller-provided workspace",
+             need, oc::kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int rc = oc::noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // Every partial the merge reads is written first by the partial kernel of
+  // the same call, so the scratch needs no clearing between calls.
+  return oc::run_attention(q, k, v, dtype, idx, idx_stride, idx_head_stride, count, count_stride,
+                           count_head_stride, batch, q_len, q_heads, kv_heads, head_dim, seq_len, block_size,
+                           max_blocks, out, out_dtype, nullptr, nullptr, nullptr, scratch, oc::kNoAllocScratchBytes,
+                           0, reinterpret_cast<cudaStream_t>(stream));
+}
