@@ -317,21 +317,24 @@ template <int D>
 __global__ void __launch_bounds__(kScoreThreads, 1)
 score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_tiles) {
   constexpr int PARTS = D / kSlabC;
-  constexpr int kW = kScoreThreads / 32;  // 16 warps, each owns 4 channels of a slab
+  constexpr int kW = kScoreThreads / 32;  // 16 warps
+  constexpr int NBUF = 4;                 // tile buffers in flight (see the note at the epilogue)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte swizzled stages must start on a 1024-byte boundary.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full[kStages];
-  __shared__ int s_rel[kStages];                 // warps done with a stage
-  __shared__ float s_dc[2][D];                   // [tile parity][channel]
-  __shared__ float s_grp[2][kW][9];              // per-warp group energies + DC energy
-  __shared__ float s_band[4];
-  __shared__ float s_red[kThreads / 32];
+  __shared__ int s_rel[kStages];             // warps done with a stage
+  __shared__ int s_cnt[NBUF];                // warps done with a tile
+  __shared__ float s_grp[NBUF][kW][8];       // per-warp coefficient-group energies
+  __shared__ float s_mu[NBUF][2][D];         // per-channel means of y0 over each half of the inner offsets
+  __shared__ float s_dcw[kW][D];             // the epilogue warp's DC coefficients
   __shared__ volatile int s_abort;
 
   const int tid = threadIdx.x;
-  const int lane = tid & 31, warp = tid >> 5;    // warp w owns channels 4w .. 4w+3 of a slab
-  const GroupSync gsync{1};                      // warps 0-7 (the many-row epilogue)
+  const int lane = tid & 31, warp = tid >> 5;
+  const int cg = warp & 7;    // channels 8cg .. 8cg+7 of a slab (one 16-byte chunk)
+  const int hf = warp >> 3;   // inner offsets 32hf .. 32hf+31, one per lane
+  const int ilo = 32 * hf + lane;
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int n_units = my_tiles * PARTS;
 
@@ -343,83 +346,50 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     const int b = t / (a.H * a.nb);
     uint8_t* dst = smem + (size_t)(k % kStages) * kSlabB;
     uint64_t* bar = &full[k % kStages];
-    const int x = h * D + part * kSlabC;
-    const int y = b * a.S + j * kBlock;
     mbar_expect_tx(bar, kSlabB);
-    tma_load_2d(dst, &kmap, bar, x, y);
-    tma_load_2d(dst + kSlabB / 2, &kmap, bar, x, y + kBlock / 2);
+    tma_load_2d(dst, &kmap, bar, h * D + part * kSlabC, b * a.S + j * kBlock);
+    tma_load_2d(dst + kSlabB / 2, &kmap, bar, h * D + part * kSlabC, b * a.S + j * kBlock + kBlock / 2);
   };
 
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
+    for (int i = 0; i < NBUF; ++i) s_cnt[i] = 0;
     fence_mbar_init();
     s_abort = 0;
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
   }
-  __syncthreads();
+  __syncthreads();  // the only CTA-wide barrier
 
-  int tl = 0;  // tiles done by this group (buffer parity)
-  for (int tile = 0; tile < my_tiles; ++tile, ++tl) {
-    const int buf = tl & 1;
-    const int t = blockIdx.x + tile * gridDim.x;
-    const int h = t % a.H;
-    const int j = (t / a.H) % a.nb;
-    const int b = t / (a.H * a.nb);
+  // 16-byte chunk cg of row r sits at chunk cg ^ (r % 8) (128-byte swizzle);
+  // rows ih*64 + ilo all have r % 8 == ilo % 8.
+  const int chunk_off = (cg ^ (ilo & 7)) * 16;
+  for (int tile = 0; tile < my_tiles; ++tile) {
+    const int tb = tile % NBUF;
     float grp[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) grp[q] = 0.f;
-    float edc = 0.f;
     for (int part = 0; part < PARTS; ++part) {
       const int k = tile * PARTS + part;
       const int stage = k % kStages;
-      // A copy that never completes sets the abort flag; every warp then skips
-      // ahead to the tile barrier and the CTA leaves together (no spin, no hang).
-      if (s_abort || !mbar_wait(&full[stage], (k / kStages) & 1)) {
+      // A copy that never completes sets the abort flag: every warp stops
+      // waiting and leaves (there is no barrier left to meet).
+      if (s_abort) return;
+      if (!mbar_wait(&full[stage], (k / kStages) & 1)) {
         s_abort = 1;
-        break;
+        if (lane == 0) atomicExch(&g_score_status, 1);
+        return;
       }
       const uint8_t* slab = smem + (size_t)stage * kSlabB;
-      float y0[2][4];
-      float colsum[4];
+      float x[8][8];
 #pragma unroll
-      for (int v = 0; v < 4; ++v) colsum[v] = 0.f;
-#pragma unroll
-      for (int it = 0; it < 2; ++it) {
-        const int ilo = lane + 32 * it;
-        // 128-byte swizzle of the tensor load: 16-byte chunk c of row r sits at c ^ (r % 8)
-        const int off = ((warp >> 1) ^ (ilo & 7)) * 16 + (warp & 1) * 8;
-        float x[8][4];
-#pragma unroll
-        for (int ih = 0; ih < 8; ++ih) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(slab + (size_t)(ih * 64 + ilo) * 128 + off);
-          x[ih][0] = bf16lo(raw.x); x[ih][1] = bf16hi(raw.x);
-          x[ih][2] = bf16lo(raw.y); x[ih][3] = bf16hi(raw.y);
-        }
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          float a0 = x[0][v] + x[1][v], a1 = x[0][v] - x[1][v];  // h = 64
-          float a2 = x[2][v] + x[3][v], a3 = x[2][v] - x[3][v];
-          float a4 = x[4][v] + x[5][v], a5 = x[4][v] - x[5][v];
-          float a6 = x[6][v] + x[7][v], a7 = x[6][v] - x[7][v];
-          float b0 = a0 + a2, b2 = a0 - a2, b1 = a1 + a3, b3 = a1 - a3;  // h = 128
-          float b4 = a4 + a6, b6 = a4 - a6, b5 = a5 + a7, b7 = a5 - a7;
-          float c0 = b0 + b4, c4 = b0 - b4, c1 = b1 + b5, c5 = b1 - b5;  // h = 256
-          float c2 = b2 + b6, c6 = b2 - b6, c3 = b3 + b7, c7 = b3 - b7;
-          y0[it][v] = c0;
-          colsum[v] += c0;
-          grp[1] = fmaf(c1, c1, grp[1]);
-          grp[2] = fmaf(c2, c2, grp[2]);
-          grp[3] = fmaf(c3, c3, grp[3]);
-          grp[4] = fmaf(c4, c4, grp[4]);
-          grp[5] = fmaf(c5, c5, grp[5]);
-          grp[6] = fmaf(c6, c6, grp[6]);
-          grp[7] = fmaf(c7, c7, grp[7]);
-        }
+      for (int ih = 0; ih < 8; ++ih) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * 128 + chunk_off);
+        unpack16<__nv_bfloat16>(raw, x[ih]);
       }
       // This warp is done with the stage; the last of the 16 warps refills it.
+      __threadfence_block();
       __syncwarp();
       if (lane == 0) {
-        __threadfence_block();
         if (atomicAdd(&s_rel[stage], 1) == kW - 1) {
           s_rel[stage] = 0;
           if (k + kStages < n_units && !s_abort) {
@@ -428,106 +398,130 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
           }
         }
       }
-      // Column sums over the 64 inner offsets (2 per lane): warp shuffles only.
+      float y0[8];
 #pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        float cs = colsum[v];
+      for (int v = 0; v < 8; ++v) {
+        float a0 = x[0][v] + x[1][v], a1 = x[0][v] - x[1][v];  // h = 64
+        float a2 = x[2][v] + x[3][v], a3 = x[2][v] - x[3][v];
+        float a4 = x[4][v] + x[5][v], a5 = x[4][v] - x[5][v];
+        float a6 = x[6][v] + x[7][v], a7 = x[6][v] - x[7][v];
+        float b0 = a0 + a2, b2 = a0 - a2, b1 = a1 + a3, b3 = a1 - a3;  // h = 128
+        float b4 = a4 + a6, b6 = a4 - a6, b5 = a5 + a7, b7 = a5 - a7;
+        float c0 = b0 + b4, c4 = b0 - b4, c1 = b1 + b5, c5 = b1 - b5;  // h = 256
+        float c2 = b2 + b6, c6 = b2 - b6, c3 = b3 + b7, c7 = b3 - b7;
+        y0[v] = c0;
+        grp[1] = fmaf(c1, c1, grp[1]);
+        grp[2] = fmaf(c2, c2, grp[2]);
+        grp[3] = fmaf(c3, c3, grp[3]);
+        grp[4] = fmaf(c4, c4, grp[4]);
+        grp[5] = fmaf(c5, c5, grp[5]);
+        grp[6] = fmaf(c6, c6, grp[6]);
+        grp[7] = fmaf(c7, c7, grp[7]);
+      }
+      // Mean of y0 over this warp's 32 inner offsets, per channel; centred
+      // squares against it (the halves are combined exactly at the epilogue).
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        float cs = y0[v];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-        colsum[v] = cs;
-      }
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        const float mean = colsum[v] * (1.0f / 64.0f);
-        const float d0 = y0[0][v] - mean, d1 = y0[1][v] - mean;
-        grp[0] = fmaf(d0, d0, grp[0]);
-        grp[0] = fmaf(d1, d1, grp[0]);
-        if (lane == v) {
-          const float dcv = colsum[v] / kNorm;
-          s_dc[buf][part * kSlabC + warp * 4 + v] = dcv;
-          edc = fmaf(dcv, dcv, edc);
-        }
+        const float mu = cs * (1.0f / 32.0f);
+        const float dl = y0[v] - mu;
+        grp[0] = fmaf(dl, dl, grp[0]);
+        if (lane == v) s_mu[tb][hf][part * kSlabC + cg * 8 + v] = mu;
       }
     }
-    // Tile epilogue.
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const float sq = warp_sum(grp[q]);
-      if (lane == 0) s_grp[buf][warp][q] = sq;
+      if (lane == 0) s_grp[tb][warp][q] = sq;
     }
-    {
-      const float sq = warp_sum(edc);
-      if (lane == 0) s_grp[buf][warp][8] = sq;
+    // The last warp to finish the tile runs its epilogue; nobody waits.  The
+    // buffer tb is reused NBUF tiles later: a warp can only get there after
+    // consuming a stage that the epilogue warp releases after finishing this
+    // epilogue (NBUF * PARTS >= kStages + 1), so the reads below are safe.
+    int last = 0;
+    __threadfence_block();
+    __syncwarp();
+    if (lane == 0) {
+      last = atomicAdd(&s_cnt[tb], 1) == kW - 1;
+      if (last) s_cnt[tb] = 0;
     }
-    __syncthreads();
-    if (s_abort) {
-      if (tid == 0) atomicExch(&g_score_status, 1);
-      return;  // uniform: every thread passed the barrier above
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) continue;
+    __threadfence_block();  // see every warp's s_grp / s_mu of this tile
+
+    const int t = blockIdx.x + tile * gridDim.x;
+    const int h = t % a.H;
+    const int j = (t / a.H) % a.nb;
+    const int b = t / (a.H * a.nb);
+    // group energies over the 16 warps; group 0 gets the exact between-half
+    // term: sum over 64 offsets of (y - mu)^2 = SS0 + SS1 + 16 (mu0 - mu1)^2.
+    float gv = 0.f;
+    if (lane < 8)
+      for (int w = 0; w < kW; ++w) gv += s_grp[tb][w][lane];
+    float between = 0.f, e_dc = 0.f;
+    for (int c = lane; c < D; c += 32) {
+      const float m0 = s_mu[tb][0][c], m1 = s_mu[tb][1][c];
+      const float dm = m0 - m1;
+      between = fmaf(16.0f * dm, dm, between);
+      const float dcv = (32.0f * (m0 + m1)) / kNorm;  // WHT coefficient 0
+      s_dcw[warp][c] = dcv;
+      e_dc = fmaf(dcv, dcv, e_dc);
     }
-    const int rows = a.q ? a.Sq * a.G : 0;
-    if (warp == 0) {
-      float v = 0.f;
-      if (lane < 9)
-        for (int w = 0; w < kW; ++w) v += s_grp[buf][w][lane];
-      float g[8];
+    between = warp_sum(between);
+    e_dc = warp_sum(e_dc);
+    __syncwarp();
+    float g[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, v, q) * 0.125f;
-      const float e_dc = __shfl_sync(0xffffffffu, v, 8);
-      float e_ac = 0.f;
+    for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, gv, q);
+    g[0] += between;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) e_ac += g[q];
-      const float e_lo = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
-      const float e_mi = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
-      const float e_hi = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
-      if (rows <= 8) {
-        // Small query tile: warp 0 finishes the tile alone; the other warps go on.
-        const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
-        const float* dcp = s_dc[buf];
-        if (a.dc)
-          for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
-        float bmax = -INFINITY;
-        if (a.q) {
-          const float sqrt_d = sqrtf((float)D);
-          const float resid_scale = sqrtf(e_ac);
-          const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
-          for (int r = 0; r < rows; ++r) {
-            const int s = r / a.G, gq = r - s * a.G;
-            const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D;
-            float dot = 0.f, nrm = 0.f;
+    for (int q = 0; q < 8; ++q) g[q] *= 0.125f;  // (64 / 512) Parseval factor of the inner transform
+    float e_ac = 0.f;
 #pragma unroll
-            for (int c = lane; c < D; c += 32) {
-              const float qv = __bfloat162float(qr[c]);
-              dot = fmaf(qv, dcp[c] / kNorm, dot);  // block mean = DC / sqrt(512)
-              nrm = fmaf(qv, qv, nrm);
-            }
-            dot = warp_sum(dot);
-            nrm = warp_sum(nrm);
-            const float bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
-            if (a.bounds && lane == 0)
-              a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + gq] = bound;
-            bmax = fmaxf(bmax, bound);
-          }
+    for (int q = 0; q < 8; ++q) e_ac += g[q];
+    const float e_lo = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
+    const float e_mi = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
+    const float e_hi = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
+    const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
+    const float* dcp = s_dcw[warp];
+    if (a.dc)
+      for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
+    float bmax = -INFINITY;
+    if (a.q) {
+      const int rows = a.Sq * a.G;
+      const float sqrt_d = sqrtf((float)D);
+      const float resid_scale = sqrtf(e_ac);
+      const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+      for (int r = 0; r < rows; ++r) {
+        const int s = r / a.G, gq = r - s * a.G;
+        const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D;
+        float dot = 0.f, nrm = 0.f;
+#pragma unroll
+        for (int c = lane; c < D; c += 32) {
+          const float qv = __bfloat162float(qr[c]);
+          dot = fmaf(qv, dcp[c] / kNorm, dot);  // block mean = DC / sqrt(512)
+          nrm = fmaf(qv, qv, nrm);
         }
-        if (lane == 0) {
-          const float z = e_hi / (e_lo + 1e-6f);
-          if (a.e_low) a.e_low[cell] = e_lo;
-          if (a.e_mid) a.e_mid[cell] = e_mi;
-          if (a.e_high) a.e_high[cell] = e_hi;
-          if (a.zeta) a.zeta[cell] = z;
-          if (a.q && a.bound_max) a.bound_max[cell] = bmax;
-          if (a.keep) a.keep[cell] = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
-        }
-      } else if (lane == 0) {
-        s_band[0] = e_lo;
-        s_band[1] = e_mi;
-        s_band[2] = e_hi;
-        s_band[3] = e_ac;
+        dot = warp_sum(dot);
+        nrm = warp_sum(nrm);
+        const float bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
+        if (a.bounds && lane == 0)
+          a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + gq] = bound;
+        bmax = fmaxf(bmax, bound);
       }
     }
-    if (rows > 8 && tid < kThreads) {  // many query rows: warps 0-7 compute the bound
-      gsync();
-      score_epilogue<__nv_bfloat16, GroupSync>(a, b, j, h, s_dc[buf], s_band, s_red, tid, gsync);
+    if (lane == 0) {
+      const float z = e_hi / (e_lo + 1e-6f);
+      if (a.e_low) a.e_low[cell] = e_lo;
+      if (a.e_mid) a.e_mid[cell] = e_mi;
+      if (a.e_high) a.e_high[cell] = e_hi;
+      if (a.zeta) a.zeta[cell] = z;
+      if (a.q && a.bound_max) a.bound_max[cell] = bmax;
+      if (a.keep) a.keep[cell] = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
     }
+    __syncwarp();
   }
 }
 
@@ -660,7 +654,9 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
 template <typename T>
 int launch_score(const ScoreArgs& a, int mode, int ncta, cudaStream_t st) {
   if constexpr (Elem<T>::kCode == OC_BF16) {
-    if (mode == 1) {
+    // The pipelined scorer evaluates the bound in one warp per tile; with
+    // many query rows (chunked prefill) the 8-warp kernel below is used.
+    if (mode == 1 && (!a.q || a.Sq * a.G <= 8)) {
       switch (a.D) {
         case 64: return launch_tma<64>(a, ncta, st);
         case 128: return launch_tma<128>(a, ncta, st);
