@@ -306,6 +306,32 @@ score_partial_kernel(ScoreArgs a) {
 // Band sums and the DC column sums accumulate across the slabs of a tile; the
 // tile's epilogue (bound, ζ, keep) runs after its last slab.
 // ---------------------------------------------------------------------------
+// Packed float32x2 arithmetic (sm_100a): one instruction for two lanes of math.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pack2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(f32x2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 constexpr int kStages = 3;
 constexpr int kScoreThreads = 512;  // 16 warps consume every stage in order
 constexpr int kSlabC = 64;                                  // channels per slab
@@ -368,6 +394,9 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     float grp[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) grp[q] = 0.f;
+    f32x2 g2[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) g2[q] = pack2(0.f, 0.f);
     for (int part = 0; part < PARTS; ++part) {
       const int k = tile * PARTS + part;
       const int stage = k % kStages;
@@ -380,12 +409,10 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
         return;
       }
       const uint8_t* slab = smem + (size_t)stage * kSlabB;
-      float x[8][8];
+      uint4 raw[8];
 #pragma unroll
-      for (int ih = 0; ih < 8; ++ih) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * 128 + chunk_off);
-        unpack16<__nv_bfloat16>(raw, x[ih]);
-      }
+      for (int ih = 0; ih < 8; ++ih)
+        raw[ih] = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * 128 + chunk_off);
       // This warp is done with the stage; the last of the 16 warps refills it.
       __threadfence_block();
       __syncwarp();
@@ -398,25 +425,32 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
           }
         }
       }
+      // Butterflies on channel pairs with packed float32x2 arithmetic.
       float y0[8];
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        float a0 = x[0][v] + x[1][v], a1 = x[0][v] - x[1][v];  // h = 64
-        float a2 = x[2][v] + x[3][v], a3 = x[2][v] - x[3][v];
-        float a4 = x[4][v] + x[5][v], a5 = x[4][v] - x[5][v];
-        float a6 = x[6][v] + x[7][v], a7 = x[6][v] - x[7][v];
-        float b0 = a0 + a2, b2 = a0 - a2, b1 = a1 + a3, b3 = a1 - a3;  // h = 128
-        float b4 = a4 + a6, b6 = a4 - a6, b5 = a5 + a7, b7 = a5 - a7;
-        float c0 = b0 + b4, c4 = b0 - b4, c1 = b1 + b5, c5 = b1 - b5;  // h = 256
-        float c2 = b2 + b6, c6 = b2 - b6, c3 = b3 + b7, c7 = b3 - b7;
-        y0[v] = c0;
-        grp[1] = fmaf(c1, c1, grp[1]);
-        grp[2] = fmaf(c2, c2, grp[2]);
-        grp[3] = fmaf(c3, c3, grp[3]);
-        grp[4] = fmaf(c4, c4, grp[4]);
-        grp[5] = fmaf(c5, c5, grp[5]);
-        grp[6] = fmaf(c6, c6, grp[6]);
-        grp[7] = fmaf(c7, c7, grp[7]);
+      for (int p = 0; p < 4; ++p) {
+        f32x2 x[8];
+#pragma unroll
+        for (int ih = 0; ih < 8; ++ih) {
+          const uint32_t w = p == 0 ? raw[ih].x : p == 1 ? raw[ih].y : p == 2 ? raw[ih].z : raw[ih].w;
+          x[ih] = pack2(bf16lo(w), bf16hi(w));
+        }
+        const f32x2 a0 = add2(x[0], x[1]), a1 = sub2(x[0], x[1]);  // h = 64
+        const f32x2 a2 = add2(x[2], x[3]), a3 = sub2(x[2], x[3]);
+        const f32x2 a4 = add2(x[4], x[5]), a5 = sub2(x[4], x[5]);
+        const f32x2 a6 = add2(x[6], x[7]), a7 = sub2(x[6], x[7]);
+        const f32x2 b0 = add2(a0, a2), b2 = sub2(a0, a2), b1 = add2(a1, a3), b3 = sub2(a1, a3);  // h = 128
+        const f32x2 b4 = add2(a4, a6), b6 = sub2(a4, a6), b5 = add2(a5, a7), b7 = sub2(a5, a7);
+        const f32x2 c0 = add2(b0, b4), c4 = sub2(b0, b4), c1 = add2(b1, b5), c5 = sub2(b1, b5);  // h = 256
+        const f32x2 c2 = add2(b2, b6), c6 = sub2(b2, b6), c3 = add2(b3, b7), c7 = sub2(b3, b7);
+        unpack2(c0, y0[2 * p], y0[2 * p + 1]);
+        g2[1] = fma2(c1, c1, g2[1]);
+        g2[2] = fma2(c2, c2, g2[2]);
+        g2[3] = fma2(c3, c3, g2[3]);
+        g2[4] = fma2(c4, c4, g2[4]);
+        g2[5] = fma2(c5, c5, g2[5]);
+        g2[6] = fma2(c6, c6, g2[6]);
+        g2[7] = fma2(c7, c7, g2[7]);
       }
       // Mean of y0 over this warp's 32 inner offsets, per channel; centred
       // squares against it (the halves are combined exactly at the epilogue).
@@ -430,6 +464,12 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
         grp[0] = fmaf(dl, dl, grp[0]);
         if (lane == v) s_mu[tb][hf][part * kSlabC + cg * 8 + v] = mu;
       }
+    }
+#pragma unroll
+    for (int q = 1; q < 8; ++q) {
+      float lo, hi;
+      unpack2(g2[q], lo, hi);
+      grp[q] = lo + hi;
     }
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
