@@ -333,7 +333,8 @@ __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
 }
 
 constexpr int kStages = 3;
-constexpr int kScoreThreads = 512;  // 16 warps consume every stage in order
+constexpr int kScoreThreads = 512;
+constexpr int kQCacheBytes = 16384;  // queries staged in shared memory up to this size  // 16 warps consume every stage in order
 constexpr int kSlabC = 64;                                  // channels per slab
 constexpr int kSlabB = kBlock * kSlabC * 2;                 // bytes per slab (bf16)
 
@@ -353,7 +354,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   __shared__ int s_cnt[NBUF];                // warps done with a tile
   __shared__ float s_grp[NBUF][kW][8];       // per-warp coefficient-group energies
   __shared__ float s_mu[NBUF][2][D];         // per-channel means of y0 over each half of the inner offsets
-  __shared__ float s_dcw[kW][D];             // the epilogue warp's DC coefficients
+  __shared__ float s_dcw[NBUF][D];           // DC coefficients of the tile in buffer tb
   __shared__ volatile int s_abort;
 
   const int tid = threadIdx.x;
@@ -363,6 +364,11 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   const int ilo = 32 * hf + lane;
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int n_units = my_tiles * PARTS;
+  // Queries staged in shared memory when they fit (decode), so the tile
+  // epilogue never waits on global memory.
+  const size_t q_elems = a.q ? (size_t)(n_tiles / (a.H * a.nb)) * a.Sq * a.Hq * D : 0;
+  const bool q_cached = a.q && q_elems * 2 <= (size_t)kQCacheBytes;
+  __nv_bfloat16* s_q = reinterpret_cast<__nv_bfloat16*>(smem + (size_t)kStages * kSlabB);
 
   auto issue = [&](int k) {
     const int t = blockIdx.x + (k / PARTS) * gridDim.x;
@@ -383,6 +389,11 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     fence_mbar_init();
     s_abort = 0;
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
+  }
+  if (q_cached) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.q);
+    uint4* dst = reinterpret_cast<uint4*>(s_q);
+    for (size_t i = tid; i < q_elems / 8; i += kScoreThreads) dst[i] = src[i];
   }
   __syncthreads();  // the only CTA-wide barrier
 
@@ -506,7 +517,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       const float dm = m0 - m1;
       between = fmaf(16.0f * dm, dm, between);
       const float dcv = (32.0f * (m0 + m1)) / kNorm;  // WHT coefficient 0
-      s_dcw[warp][c] = dcv;
+      s_dcw[tb][c] = dcv;
       e_dc = fmaf(dcv, dcv, e_dc);
     }
     between = warp_sum(between);
@@ -525,7 +536,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     const float e_mi = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
     const float e_hi = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
     const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
-    const float* dcp = s_dcw[warp];
+    const float* dcp = s_dcw[tb];
     if (a.dc)
       for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
     float bmax = -INFINITY;
@@ -533,7 +544,8 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       const int rows = a.Sq * a.G;
       const float sqrt_d = sqrtf((float)D);
       const float resid_scale = sqrtf(e_ac);
-      const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+      const __nv_bfloat16* qb = (q_cached ? s_q : reinterpret_cast<const __nv_bfloat16*>(a.q)) +
+                                (size_t)b * a.Sq * a.Hq * D;
       for (int r = 0; r < rows; ++r) {
         const int s = r / a.G, gq = r - s * a.G;
         const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D;
@@ -684,7 +696,7 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   const uint64_t rows = (uint64_t)ntiles / ((uint64_t)a.H * a.nb) * a.S;  // B * S
   int rc = encode_map_2d(&map, a.keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, kSlabC, kBlock / 2, true);
   if (rc) return set_error(OC_ERR_CUDA, "oc_score_blocks: tensor map encode failed (%d)", rc);
-  const int smem = kStages * kSlabB + 1024;
+  const int smem = kStages * kSlabB + kQCacheBytes + 1024;
   cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
   score_tma_kernel<D><<<grid, kScoreThreads, smem, st>>>(map, a, ntiles);
@@ -760,6 +772,7 @@ extern "C" int oc_score_blocks(const void* keys, const void* q, int dtype,
              "oc_score_blocks: head_dim %d not in {64,128,256}", head_dim);
   OC_REQUIRE(dtype == OC_F32 || dtype == OC_BF16, OC_ERR_DTYPE, "oc_score_blocks: dtype %d", dtype);
   OC_REQUIRE(aligned16(keys), OC_ERR_ALIGN, "oc_score_blocks: keys not 16-byte aligned");
+  OC_REQUIRE(!q || aligned16(q), OC_ERR_ALIGN, "oc_score_blocks: q not 16-byte aligned");
   if (q) {
     OC_REQUIRE(q_len >= 1 && q_heads >= 1 && q_heads % kv_heads == 0, OC_ERR_SHAPE,
                "oc_score_blocks: q_heads %d must be a positive multiple of kv_heads %d (q_len %d)",
