@@ -255,228 +255,343 @@ attn_partial_kernel(AttnArgs a) {
 
 
 // ---------------------------------------------------------------------------
-// bfloat16 path: the same work items, with K and V chunks streamed by 2-D
-// bulk-tensor loads into a ring of shared-memory stages (persistent grid, one
-// CTA per SM, thread 0 keeps kAStages chunks in flight).  A stage holds the
-// CH x D keys and the CH x D values of one item; it is refilled with the item
-// kAStages ahead as soon as the softmax-weighted sum has read it.
+// bfloat16 path.  Work items are ordered (batch, kv head, row tile, index
+// slot, chunk) and every CTA of the persistent grid takes one contiguous range
+// of them, so a CTA walks long runs of items that share (batch, head, row
+// tile).  The K and V rows of each item (CH = 8192 / D tokens) stream through
+// a ring of kVStages shared-memory stages by 2-D tensor loads.  All 16 warps
+// consume every stage in order (a stage is refilled by the last warp done
+// with it, counted in shared memory), so no warp ever waits on a stage whose
+// previous phase is still pending.  Warp w takes tokens w*TPW .. w*TPW+TPW-1
+// of each item and keeps its own online-softmax state (running max m, sum l
+// and output o, lanes holding D/32 output channels) across the items of a
+// run; logits are reduced across lanes by a transpose-reduce.  At the end of
+// a run (uniform across the CTA) the 16 warp states are combined through
+// shared memory into one (m, l, o) partial, written at the run's first item;
+// the other items of the run get m = -inf and are skipped by the merge.
 // ---------------------------------------------------------------------------
-constexpr int kAStages = 3;
-constexpr int kAStageBytes = 65536;  // 2 * CH * D * 2 with CH * D = 16384
-constexpr int kAThreads = 512;
-constexpr int kAWarps = kAThreads / 32;
-
-struct CtaBarrier {
-  __device__ void operator()() const { __syncthreads(); }
-};
+constexpr int kVThreads = 512;
+constexpr int kVWarps = kVThreads / 32;
+constexpr int kVStages = 4;
+constexpr int kVStageBytes = 32768;  // K + V of one item: 2 * CH * D * 2 with CH * D = 8192
 
 __device__ int g_attn_status = 0;
 
-struct GroupSync {
-  int id;  // named barrier 1 or 2 for a 256-thread consumer group
-  __device__ void operator()() const { asm volatile("bar.sync %0, 256;" ::"r"(id) : "memory"); }
-};
+// Item w of the (batch, head, row tile, slot, chunk) order; false past the end.
+__device__ __forceinline__ bool run_item(const AttnArgs& a, int w, int& b, int& h, int& rt, int& item) {
+  for (b = 0; b < a.B; ++b)
+    for (h = 0; h < a.Hkv; ++h) {
+      const int n = list_len(a, b, h) * a.chunks;
+      const int tot = n * a.n_rt;
+      if (w < tot) {
+        rt = w / n;
+        item = w - rt * n;
+        return true;
+      }
+      w -= tot;
+    }
+  return false;
+}
+
+__device__ __forceinline__ int total_items(const AttnArgs& a) {
+  int n = 0;
+  for (int b = 0; b < a.B; ++b)
+    for (int h = 0; h < a.Hkv; ++h) n += list_len(a, b, h) * a.chunks * a.n_rt;
+  return n;
+}
+
+template <int NV>
+__device__ __forceinline__ float transpose_reduce(float (&v)[NV], int lane) {
+  // After the halving steps lane holds the sum of value index lane >> (5 - log2 NV)
+  // over its group; the remaining offsets sum across the group.
+  int c = NV;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    if (c > 1) {
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i) {
+        if (i < c / 2) {
+          const float send = up ? v[i] : v[i + c / 2];
+          const float keep = up ? v[i + c / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      c >>= 1;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+  return v[0];
+}
 
 template <int D, int RT>
-__global__ void __launch_bounds__(kAThreads, 1)
-attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
-  constexpr int CH = 16384 / D;          // tokens per item (128 at D = 128)
-  constexpr int VEC = 8;
-  constexpr int LPR = D / VEC;
-  constexpr int RPW = 32 / LPR;
-  constexpr int ROWS_PER_WARP = CH / kAWarps;
-  constexpr int ITERS = ROWS_PER_WARP / RPW;
-  constexpr int ROWB = D * 2;            // bytes per token row in shared memory
-  static_assert(ROWS_PER_WARP % RPW == 0, "mapping");
-  extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[kAStages];
-  __shared__ float s_p[1][RT][CH];
-  __shared__ float s_m[1][RT], s_l[1][RT];
-  __shared__ float s_o[1][kAWarps / 2][RT][D];
-  __shared__ int s_abort[1];
+__global__ void __launch_bounds__(kVThreads, 1)
+attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+  constexpr int CH = 8192 / D;           // tokens per item
+  constexpr int TPW = CH / kVWarps;      // tokens per warp per item
+  constexpr int DPL = D / 32;            // output channels per lane
+  constexpr int NV = TPW * RT;           // logits per warp per item (one per lane after reduction)
+  constexpr int LOGNV = NV == 1 ? 0 : NV == 2 ? 1 : NV == 4 ? 2 : NV == 8 ? 3 : NV == 16 ? 4 : 5;
+  constexpr int SH = 5 - LOGNV;          // lane = (value index << SH) | group position
+  static_assert(NV <= 32 && (NV & (NV - 1)) == 0 && TPW * kVWarps == CH, "tile mapping");
+  constexpr int KB = CH * D * 2;         // bytes of the K (or V) half of a stage
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full[kVStages];
+  __shared__ int s_rel[kVStages];
+  __shared__ volatile int s_abort;
+  __shared__ float s_wm[kVWarps][RT], s_wl[kVWarps][RT];
+  __shared__ float s_wo[kVWarps][RT][D];
 
-  // One group of 16 warps consumes every stage in ring order, so a wait on a
-  // stage always follows this CTA's own consumption of the stage's previous
-  // phase (no parity aliasing between independent consumers).
-  const int gid = 0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const CtaBarrier gsync;
-  const int sub = lane / LPR, vl = lane % LPR, d0 = vl * VEC;
+  const int N = total_items(a);
+  const int per = (N + gridDim.x - 1) / gridDim.x;
+  const int beg = min(N, (int)blockIdx.x * per), end = min(N, beg + per);
+  const int n_mine = end - beg;
 
-  auto issue = [&](int k) -> bool {
-    int b, item, h, rt;
-    if (!decode_item(a, blockIdx.x + k * gridDim.x, b, item, h, rt)) return false;
+  auto issue = [&](int k) {
+    int b, h, rt, item;
+    run_item(a, beg + k, b, h, rt, item);
     const int slot = item / a.chunks, c = item - slot * a.chunks;
     const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
-    uint64_t* bar = &full[k % kAStages];
-    uint8_t* dst = smem + (size_t)(k % kAStages) * kAStageBytes;
-    mbar_expect_tx(bar, kAStageBytes);
     // An out-of-range index is never dereferenced: block 0 is loaded instead
-    // and the item contributes nothing.
+    // and the item is skipped.
     const int y = (blk < 0 || blk >= a.S / a.bs) ? b * a.S : b * a.S + blk * a.bs + c * CH;
+    uint8_t* dst = smem + (size_t)(k % kVStages) * kVStageBytes;
+    uint64_t* bar = &full[k % kVStages];
+    mbar_expect_tx(bar, 2 * KB);
     tma_load_2d(dst, &kmap, bar, h * D, y);
-    tma_load_2d(dst + kAStageBytes / 2, &vmap, bar, h * D, y);
-    return true;
+    tma_load_2d(dst + KB, &vmap, bar, h * D, y);
   };
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kAStages; ++i) mbar_init(&full[i], 1);
+  if (tid == 0) {
+    for (int i = 0; i < kVStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
     fence_mbar_init();
-    for (int k = 0; k < kAStages; ++k)
-      if (!issue(k)) break;
+    s_abort = 0;
+    for (int k = 0; k < kVStages && k < n_mine; ++k) issue(k);
   }
-  if (tid == 0) s_abort[gid] = 0;
   __syncthreads();
 
-  for (int k = 0;; ++k) {
-    int b, item, h, rt;
-    if (!decode_item(a, blockIdx.x + k * gridDim.x, b, item, h, rt)) break;
-    const int stage = k % kAStages;
-    if (!mbar_wait(&full[stage], (k / kAStages) & 1)) s_abort[gid] = 1;
-    gsync();
-    if (s_abort[gid]) {
-      if (tid == 0) atomicExch(&g_attn_status, 1);
-      return;
+  // Per-warp online-softmax state of the current run.
+  float m_run[RT], o[RT][DPL];
+  float l_acc = 0.f;  // this lane's (token, row) share of l
+  float qv[RT][DPL];
+  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0;
+  const int my_v = lane >> SH;            // value index this lane ends up holding
+  const int my_t = my_v / RT, my_r = my_v % RT;
+
+  for (int k = 0; k < n_mine; ++k) {
+    int b, h, rt, item;
+    run_item(a, beg + k, b, h, rt, item);
+    const bool new_run = b != cur_b || h != cur_h || rt != cur_rt;
+    if (new_run && cur_b >= 0) {
+      // ---- flush the finished run (uniform: every warp is at this item) ----
+      const int r0 = cur_rt * RT;
+      const int nr = min(RT, a.R - r0);
+      float l_sum = l_acc;
+#pragma unroll
+      for (int off = 1 << SH; off < 32; off <<= 1)  // lanes of the same row differ in the token bits
+        if ((off >> SH) >= RT) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, off);
+      if ((lane & ((1 << SH) - 1)) == 0 && my_t == 0) {
+#pragma unroll
+        for (int r = 0; r < RT; ++r)
+          if (r == my_r) { s_wl[warp][r] = l_sum; s_wm[warp][r] = m_run[r]; }
+      }
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) s_wo[warp][r][lane * DPL + e] = o[r][e];
+      __syncthreads();
+      for (int x = tid; x < nr * D; x += kVThreads) {
+        const int r = x / D, d = x - r * D;
+        float M = -INFINITY;
+        for (int w = 0; w < kVWarps; ++w) M = fmaxf(M, s_wm[w][r]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY)
+          for (int w = 0; w < kVWarps; ++w) {
+            const float f = exp2f(s_wm[w][r] - M);
+            L = fmaf(s_wl[w][r], f, L);
+            O = fmaf(s_wo[w][r][d], f, O);
+          }
+        const size_t part = (((size_t)cur_b * a.max_items + run_first) * a.Hkv + cur_h) * a.R + r0;
+        a.ws_o[(part + r) * D + d] = O;
+        if (d == 0) { a.ws_m[part + r] = M; a.ws_l[part + r] = L; }
+      }
+      __syncthreads();
+    }
+    if (new_run) {
+      cur_b = b; cur_h = h; cur_rt = rt; run_first = item;
+      const int r0 = rt * RT;
+      const int nr = min(RT, a.R - r0);
+      const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+#pragma unroll
+      for (int r = 0; r < RT; ++r) {
+        m_run[r] = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) { o[r][e] = 0.f; qv[r][e] = 0.f; }
+        if (r < nr) {
+          const int row = r0 + r, s = row / a.G, g = row - s * a.G;
+          const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + g) * D + lane * DPL;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) qv[r][e] = __bfloat162float(qr[e]) * a.scale_log2;
+        }
+      }
+      l_acc = 0.f;
+    } else if (warp == 0 && lane < RT) {
+      // items after the first of a run carry no partial of their own
+      const int r0 = rt * RT;
+      if (r0 + lane < a.R) {
+        const size_t part = (((size_t)b * a.max_items + item) * a.Hkv + h) * a.R + r0;
+        a.ws_m[part + lane] = -INFINITY;
+      }
+    }
+
+    const int stage = k % kVStages;
+    if (!s_abort && !mbar_wait(&full[stage], (k / kVStages) & 1)) {
+      s_abort = 1;
+      if (lane == 0) atomicExch(&g_attn_status, 1);
     }
     const int slot = item / a.chunks;
     const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
-    const int r0 = rt * RT;
-    const int nr = min(RT, a.R - r0);
-    const size_t part = (((size_t)b * a.max_items + item) * a.Hkv + h) * a.R + r0;
-    const uint8_t* ks = smem + (size_t)stage * kAStageBytes;
-    const uint8_t* vs = ks + kAStageBytes / 2;
-    const bool valid = blk >= 0 && blk < a.S / a.bs;
-
-    float qv[RT][VEC];
-    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+    const bool valid = !s_abort && blk >= 0 && blk < a.S / a.bs;
+    const uint8_t* ks = smem + (size_t)stage * kVStageBytes;
+    const uint8_t* vs = ks + KB;
+    // K and V rows of this warp's tokens into registers, then release the stage.
+    float kf[TPW][DPL], vf[TPW][DPL];
 #pragma unroll
-    for (int r = 0; r < RT; ++r) {
-      if (r < nr) {
-        const int row = r0 + r, s = row / a.G, g = row - s * a.G;
-        const uint4 raw = *reinterpret_cast<const uint4*>(qb + ((size_t)s * a.Hq + (size_t)h * a.G + g) * D + d0);
-        unpack16<__nv_bfloat16>(raw, qv[r]);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) qv[r][e] *= a.scale_log2;
+    for (int t = 0; t < TPW; ++t) {
+      const uint8_t* kr = ks + (size_t)(warp * TPW + t) * (D * 2) + lane * DPL * 2;
+      const uint8_t* vr = vs + (size_t)(warp * TPW + t) * (D * 2) + lane * DPL * 2;
+      if constexpr (DPL == 8) {
+        const uint4 kw = *reinterpret_cast<const uint4*>(kr), vw = *reinterpret_cast<const uint4*>(vr);
+        unpack16<__nv_bfloat16>(kw, kf[t]);
+        unpack16<__nv_bfloat16>(vw, vf[t]);
+      } else if constexpr (DPL == 4) {
+        const uint2 kw = *reinterpret_cast<const uint2*>(kr), vw = *reinterpret_cast<const uint2*>(vr);
+        kf[t][0] = bf16lo(kw.x); kf[t][1] = bf16hi(kw.x); kf[t][2] = bf16lo(kw.y); kf[t][3] = bf16hi(kw.y);
+        vf[t][0] = bf16lo(vw.x); vf[t][1] = bf16hi(vw.x); vf[t][2] = bf16lo(vw.y); vf[t][3] = bf16hi(vw.y);
       } else {
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) qv[r][e] = 0.f;
+        const uint32_t kw = *reinterpret_cast<const uint32_t*>(kr), vw = *reinterpret_cast<const uint32_t*>(vr);
+        kf[t][0] = bf16lo(kw); kf[t][1] = bf16hi(kw);
+        vf[t][0] = bf16lo(vw); vf[t][1] = bf16hi(vw);
       }
     }
-    const int trow0 = warp * ROWS_PER_WARP + sub;
+    __threadfence_block();
+    __syncwarp();
+    if (lane == 0 && atomicAdd(&s_rel[stage], 1) == kVWarps - 1) {
+      s_rel[stage] = 0;
+      if (k + kVStages < n_mine && !s_abort) {
+        fence_proxy_async();
+        issue(k + kVStages);
+      }
+    }
+    if (!valid) continue;
+
+    // logits of (token t, row r): partial dots over this lane's channels, reduced across lanes
+    float lv[NV];
 #pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-      const int t = trow0 + i * RPW;
-      float kf[VEC];
-      unpack16<__nv_bfloat16>(*reinterpret_cast<const uint4*>(ks + (size_t)t * ROWB + d0 * 2), kf);
+    for (int t = 0; t < TPW; ++t)
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
         float acc = 0.f;
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) acc = fmaf(qv[r][e], kf[e], acc);
+        for (int e = 0; e < DPL; ++e) acc = fmaf(qv[r][e], kf[t][e], acc);
+        lv[t * RT + r] = acc;
+      }
+    const float s = transpose_reduce<NV>(lv, lane);  // logit of (my_t, my_r)
+    // row max over this warp's tokens: lanes of the same row differ in the token bits
+    float mx = s;
 #pragma unroll
-        for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (vl == 0) s_p[gid][r][t] = acc;
-      }
+    for (int off = 1 << SH; off < 32; off <<= 1)
+      if ((off >> SH) >= RT) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float alpha[RT];
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      const float mr = __shfl_sync(0xffffffffu, mx, r << SH);
+      const float mn = fmaxf(m_run[r], mr);
+      alpha[r] = exp2f(m_run[r] - mn);  // 0 on the first item (m_run = -inf)
+      m_run[r] = mn;
     }
-    gsync();
-    for (int r = warp; r < RT; r += kAWarps) {
-      float m = -INFINITY;
-      for (int t = lane; t < CH; t += 32) m = fmaxf(m, s_p[gid][r][t]);
-      m = warp_max(m);
-      float l = 0.f;
-      for (int t = lane; t < CH; t += 32) {
-        const float p = exp2f(s_p[gid][r][t] - m);
-        s_p[gid][r][t] = p;
-        l += p;
-      }
-      l = warp_sum(l);
-      if (lane == 0) { s_m[gid][r] = m; s_l[gid][r] = l; }
-    }
-    gsync();
-    float acc[RT][VEC];
+    float m_mine = 0.f, a_mine = 0.f;  // register-only selection of this lane's row
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+      if (r == my_r) { m_mine = m_run[r]; a_mine = alpha[r]; }
+    const float p = exp2f(s - m_mine);
+    l_acc = fmaf(l_acc, a_mine, p);
 #pragma unroll
     for (int r = 0; r < RT; ++r)
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) acc[r][e] = 0.f;
+      for (int e = 0; e < DPL; ++e) o[r][e] *= alpha[r];
 #pragma unroll
-    for (int i = 0; i < ITERS; ++i) {
-      const int t = trow0 + i * RPW;
-      float vf[VEC];
-      unpack16<__nv_bfloat16>(*reinterpret_cast<const uint4*>(vs + (size_t)t * ROWB + d0 * 2), vf);
+    for (int t = 0; t < TPW; ++t)
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
-        const float p = s_p[gid][r][t];
+        const float ptr = __shfl_sync(0xffffffffu, p, (t * RT + r) << SH);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[r][e] = fmaf(p, vf[e], acc[r][e]);
+        for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(ptr, vf[t][e], o[r][e]);
       }
+  }
+  // ---- flush the last run ----
+  if (cur_b >= 0) {
+    const int r0 = cur_rt * RT;
+    const int nr = min(RT, a.R - r0);
+    float l_sum = l_acc;
+#pragma unroll
+    for (int off = 1 << SH; off < 32; off <<= 1)
+      if ((off >> SH) >= RT) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, off);
+    if ((lane & ((1 << SH) - 1)) == 0 && my_t == 0) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+        if (r == my_r) { s_wl[warp][r] = l_sum; s_wm[warp][r] = m_run[r]; }
     }
 #pragma unroll
     for (int r = 0; r < RT; ++r)
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        float x = acc[r][e];
-#pragma unroll
-        for (int o = LPR; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-        acc[r][e] = x;
-      }
-    // Cross-warp sum in two rounds through half-size scratch.
-    if (sub == 0 && warp >= kAWarps / 2) {
-#pragma unroll
-      for (int r = 0; r < RT; ++r)
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) s_o[gid][warp - kAWarps / 2][r][d0 + e] = acc[r][e];
-    }
-    gsync();  // stage fully read; upper warps' sums visible
-    if (tid == 0) {
-      fence_proxy_async();
-      issue(k + kAStages);
-    }
-    if (sub == 0 && warp < kAWarps / 2) {
-#pragma unroll
-      for (int r = 0; r < RT; ++r)
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) s_o[gid][warp][r][d0 + e] += acc[r][e];
-    }
-    gsync();
-    for (int x = tid; x < nr * D; x += kAThreads) {
+      for (int e = 0; e < DPL; ++e) s_wo[warp][r][lane * DPL + e] = o[r][e];
+    __syncthreads();
+    for (int x = tid; x < nr * D; x += kVThreads) {
       const int r = x / D, d = x - r * D;
-      float sum = 0.f;
-#pragma unroll
-      for (int ww = 0; ww < kAWarps / 2; ++ww) sum += s_o[gid][ww][r][d];
-      a.ws_o[(part + r) * D + d] = valid ? sum : 0.f;
+      float M = -INFINITY;
+      for (int w = 0; w < kVWarps; ++w) M = fmaxf(M, s_wm[w][r]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY)
+        for (int w = 0; w < kVWarps; ++w) {
+          const float f = exp2f(s_wm[w][r] - M);
+          L = fmaf(s_wl[w][r], f, L);
+          O = fmaf(s_wo[w][r][d], f, O);
+        }
+      const size_t part = (((size_t)cur_b * a.max_items + run_first) * a.Hkv + cur_h) * a.R + r0;
+      a.ws_o[(part + r) * D + d] = O;
+      if (d == 0) { a.ws_m[part + r] = M; a.ws_l[part + r] = L; }
     }
-    if (tid < nr) {
-      a.ws_m[part + tid] = valid ? s_m[gid][tid] : -INFINITY;
-      a.ws_l[part + tid] = valid ? s_l[gid][tid] : 0.f;
-    }
-    gsync();
   }
 }
 
 template <int D>
-int launch_attn_tma(const AttnArgs& a, int rt, cudaStream_t st) {
-  constexpr int CH = 16384 / D;
+int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
+  constexpr int CH = 8192 / D;
   CUtensorMap km, vm;
   const uint64_t cols = (uint64_t)a.Hkv * D, rows = (uint64_t)a.B * a.S;
   int rc = encode_map_2d(&km, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, D, CH);
   if (!rc) rc = encode_map_2d(&vm, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, D, CH);
   if (rc) return set_error(OC_ERR_CUDA, "attention: tensor map encode failed (%d)", rc);
-  const int smem = kAStages * kAStageBytes;
+  const int smem = kVStages * kVStageBytes + 1024;
   const int grid = device_sm_count();
-#define OC_ATMA(RTV)                                                                                   \
-  do {                                                                                                 \
-    cudaFuncSetAttribute(attn_tma_kernel<D, RTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    attn_tma_kernel<D, RTV><<<grid, kAThreads, smem, st>>>(km, vm, a);                                  \
+#define OC_ASTREAM(RTV)                                                                                   \
+  do {                                                                                                    \
+    cudaFuncSetAttribute(attn_stream_kernel<D, RTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    attn_stream_kernel<D, RTV><<<grid, kVThreads, smem, st>>>(km, vm, a);                                 \
   } while (0)
-  if (rt == 1) OC_ATMA(1);
-  else if (rt == 2) OC_ATMA(2);
+  if (rt == 1) OC_ASTREAM(1);
+  else if (rt == 2) OC_ASTREAM(2);
   else if constexpr (D <= 128) {
-    if (rt == 4) OC_ATMA(4);
+    if (rt == 4) OC_ASTREAM(4);
     else return set_error(OC_ERR_SHAPE, "attention: row tile %d", rt);
   } else
     return set_error(OC_ERR_SHAPE, "attention: row tile %d", rt);
-#undef OC_ATMA
-  return check_launch("attn_tma_kernel");
+#undef OC_ASTREAM
+  return check_launch("attn_stream_kernel");
 }
 
 // Combine the items of one (batch, kv head, row): M = max m_i,
@@ -529,7 +644,8 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
       const int cn = min(256, n - c0);
       const float* ob = a.ws_o + (p0 + (size_t)c0 * stride) * a.D + d;
 #pragma unroll 8
-      for (int j = 0; j < cn; ++j) O = fmaf(s_f[j], ob[(size_t)j * stride * a.D], O);
+      for (int j = 0; j < cn; ++j)  // items without a partial (f == 0) hold no output row
+        if (s_f[j] != 0.f) O = fmaf(s_f[j], ob[(size_t)j * stride * a.D], O);
     }
     __syncthreads();
   }
@@ -607,14 +723,12 @@ int pick_rt(int R, int D) {
   return D == 256 && rt > 4 ? 4 : rt;
 }
 
-// Tokens per work item: 128 (64 when the block size is not a multiple of
-// 128, or at D = 256 so that a K + V chunk stays within one 64 KB stage).
-int chunk_for(int bs, int D) { return (bs % 128 == 0 && D <= 128) ? 128 : 64; }
+// Tokens per work item: CH = 8192 / D (a K + V chunk of 32 KB in bfloat16),
+// or 64 when the block size is not a multiple of CH.
+int chunk_for(int bs, int D) { return bs % (8192 / D) == 0 ? 8192 / D : 64; }
 
-// The bulk-tensor path streams CH = 16384 / D tokens per item.
-bool use_tma_path(int dtype, int bs, int D) {
-  return dtype == OC_BF16 && chunk_for(bs, D) == 16384 / D;
-}
+// bfloat16 inputs stream through the bulk-tensor path when the chunk fits.
+bool use_tma_path(int dtype, int bs, int D) { return dtype == OC_BF16 && bs % (8192 / D) == 0; }
 
 size_t attn_ws_bytes(int B, int Sq, int Hq, int Hkv, int D, int bs, int max_blocks) {
   const int G = Hq / Hkv;
@@ -708,8 +822,8 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   if (max_blocks > 0) {
     const int grid = device_sm_count() * 2;
     if (tma)
-      rc = D == 64 ? launch_attn_tma<64>(a, rt, st) : D == 128 ? launch_attn_tma<128>(a, rt, st)
-                                                     : launch_attn_tma<256>(a, rt, st);
+      rc = D == 64 ? launch_attn_stream<64>(a, rt, st) : D == 128 ? launch_attn_stream<128>(a, rt, st)
+                                                        : launch_attn_stream<256>(a, rt, st);
     else
       rc = dtype == OC_F32 ? launch_partials<float>(a, rt, grid, st)
                            : launch_partials<__nv_bfloat16>(a, rt, grid, st);
