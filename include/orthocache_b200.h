@@ -213,7 +213,7 @@ int oc_empty_heads_mean(const void* v, int dtype, const int32_t* count, int coun
  * they run the attention (an allocator-free FFI host, a serving loop whose
  * memory pool forbids allocations during a step, a process whose allocator
  * is exhausted).  Same inputs, outputs and results as oc_indirect_attention;
- * the scratch comes from a fixed 16 MiB device array that every GPU which
+ * the scratch comes from a fixed 32 MiB device array that every GPU which
  * loads this library holds until the process exits.  It never calls
  * cudaMalloc or cudaFree.
  *   - Shapes whose scratch need (oc_indirect_attention_workspace_bytes) is

@@ -270,6 +270,26 @@ attn_partial_kernel(AttnArgs a) {
 // shared memory into one (m, l, o) partial, written at the run's first item;
 // the other items of the run get m = -inf and are skipped by the merge.
 // ---------------------------------------------------------------------------
+typedef unsigned long long f32x2;  // packed float32 pair (sm_100a f32x2 arithmetic)
+__device__ __forceinline__ f32x2 pack2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(f32x2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f32x2 fmul2(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 constexpr int kVThreads = 512;
 constexpr int kVWarps = kVThreads / 32;
 constexpr int kVStages = 4;
@@ -299,6 +319,28 @@ __device__ __forceinline__ int total_items(const AttnArgs& a) {
     for (int h = 0; h < a.Hkv; ++h) n += list_len(a, b, h) * a.chunks * a.n_rt;
   return n;
 }
+
+// Incremental walk over the (batch, head, row tile, item) order, skipping
+// empty lists; b == B marks the end.
+struct ItemIter {
+  int b, h, rt, item, n;
+  __device__ void start(const AttnArgs& a, int w, int N) {
+    if (w >= N) { b = a.B; h = rt = item = 0; n = 1; return; }
+    run_item(a, w, b, h, rt, item);
+    n = list_len(a, b, h) * a.chunks;
+  }
+  __device__ void next(const AttnArgs& a) {
+    if (b >= a.B) return;
+    if (++item < n) return;
+    item = 0;
+    if (++rt < a.n_rt) return;
+    rt = 0;
+    do {
+      if (++h >= a.Hkv) { h = 0; ++b; }
+      n = b < a.B ? list_len(a, b, h) * a.chunks : 1;
+    } while (n == 0);
+  }
+};
 
 template <int NV>
 __device__ __forceinline__ float transpose_reduce(float (&v)[NV], int lane) {
@@ -350,40 +392,51 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   const int beg = min(N, (int)blockIdx.x * per), end = min(N, beg + per);
   const int n_mine = end - beg;
 
-  auto issue = [&](int k) {
-    int b, h, rt, item;
-    run_item(a, beg + k, b, h, rt, item);
-    const int slot = item / a.chunks, c = item - slot * a.chunks;
-    const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
+  // Loads item position `pos` (the CTA's k-th item) into stage k % kVStages.
+  auto issue = [&](int k, const ItemIter& pos) {
+    const int slot = pos.item / a.chunks, c = pos.item - slot * a.chunks;
+    const int blk = a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
     // An out-of-range index is never dereferenced: block 0 is loaded instead
     // and the item is skipped.
-    const int y = (blk < 0 || blk >= a.S / a.bs) ? b * a.S : b * a.S + blk * a.bs + c * CH;
+    const int y = (blk < 0 || blk >= a.S / a.bs) ? pos.b * a.S : pos.b * a.S + blk * a.bs + c * CH;
     uint8_t* dst = smem + (size_t)(k % kVStages) * kVStageBytes;
     uint64_t* bar = &full[k % kVStages];
     mbar_expect_tx(bar, 2 * KB);
-    tma_load_2d(dst, &kmap, bar, h * D, y);
-    tma_load_2d(dst + KB, &vmap, bar, h * D, y);
+    tma_load_2d(dst, &kmap, bar, pos.h * D, y);
+    tma_load_2d(dst + KB, &vmap, bar, pos.h * D, y);
   };
 
   if (tid == 0) {
     for (int i = 0; i < kVStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
     fence_mbar_init();
     s_abort = 0;
-    for (int k = 0; k < kVStages && k < n_mine; ++k) issue(k);
+    ItemIter pre;
+    pre.start(a, beg, N);
+    for (int k = 0; k < kVStages && k < n_mine; ++k) {
+      issue(k, pre);
+      pre.next(a);
+    }
   }
   __syncthreads();
 
   // Per-warp online-softmax state of the current run.
-  float m_run[RT], o[RT][DPL];
+  float m_run[RT];
+  f32x2 o2[RT][DPL / 2];  // output channels in packed pairs
   float l_acc = 0.f;  // this lane's (token, row) share of l
   float qv[RT][DPL];
   int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0;
+  // Position of the item being consumed, and of the item kVStages ahead
+  // (the one a stage released now is refilled with).
+  ItemIter cur, ahead;
+  cur.start(a, beg, N);
+  ahead.start(a, beg, N);
+  for (int i = 0; i < kVStages; ++i) ahead.next(a);
   const int my_v = lane >> SH;            // value index this lane ends up holding
   const int my_t = my_v / RT, my_r = my_v % RT;
 
   for (int k = 0; k < n_mine; ++k) {
-    int b, h, rt, item;
-    run_item(a, beg + k, b, h, rt, item);
+    const int b = cur.b, h = cur.h, rt = cur.rt, item = cur.item;
+    cur.next(a);
     const bool new_run = b != cur_b || h != cur_h || rt != cur_rt;
     if (new_run && cur_b >= 0) {
       // ---- flush the finished run (uniform: every warp is at this item) ----
@@ -401,7 +454,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 #pragma unroll
       for (int r = 0; r < RT; ++r)
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) s_wo[warp][r][lane * DPL + e] = o[r][e];
+        for (int e = 0; e < DPL; e += 2) unpack2(o2[r][e / 2], s_wo[warp][r][lane * DPL + e], s_wo[warp][r][lane * DPL + e + 1]);
       __syncthreads();
       for (int x = tid; x < nr * D; x += kVThreads) {
         const int r = x / D, d = x - r * D;
@@ -429,7 +482,9 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       for (int r = 0; r < RT; ++r) {
         m_run[r] = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) { o[r][e] = 0.f; qv[r][e] = 0.f; }
+        for (int e = 0; e < DPL; ++e) qv[r][e] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL / 2; ++e) o2[r][e] = pack2(0.f, 0.f);
         if (r < nr) {
           const int row = r0 + r, s = row / a.G, g = row - s * a.G;
           const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + g) * D + lane * DPL;
@@ -483,9 +538,10 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       s_rel[stage] = 0;
       if (k + kVStages < n_mine && !s_abort) {
         fence_proxy_async();
-        issue(k + kVStages);
+        issue(k + kVStages, ahead);
       }
     }
+    ahead.next(a);
     if (!valid) continue;
 
     // logits of (token t, row r): partial dots over this lane's channels, reduced across lanes
@@ -494,10 +550,12 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     for (int t = 0; t < TPW; ++t)
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
-        float acc = 0.f;
+        f32x2 acc = fmul2(pack2(qv[r][0], qv[r][1]), pack2(kf[t][0], kf[t][1]));
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) acc = fmaf(qv[r][e], kf[t][e], acc);
-        lv[t * RT + r] = acc;
+        for (int e = 2; e < DPL; e += 2) acc = fma2(pack2(qv[r][e], qv[r][e + 1]), pack2(kf[t][e], kf[t][e + 1]), acc);
+        float lo, hi;
+        unpack2(acc, lo, hi);
+        lv[t * RT + r] = lo + hi;
       }
     const float s = transpose_reduce<NV>(lv, lane);  // logit of (my_t, my_r)
     // row max over this warp's tokens: lanes of the same row differ in the token bits
@@ -520,16 +578,19 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     const float p = exp2f(s - m_mine);
     l_acc = fmaf(l_acc, a_mine, p);
 #pragma unroll
-    for (int r = 0; r < RT; ++r)
+    for (int r = 0; r < RT; ++r) {
+      const f32x2 al = pack2(alpha[r], alpha[r]);
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) o[r][e] *= alpha[r];
+      for (int e = 0; e < DPL; e += 2) o2[r][e / 2] = fmul2(o2[r][e / 2], al);
+    }
 #pragma unroll
     for (int t = 0; t < TPW; ++t)
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
         const float ptr = __shfl_sync(0xffffffffu, p, (t * RT + r) << SH);
+        const f32x2 pp = pack2(ptr, ptr);
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) o[r][e] = fmaf(ptr, vf[t][e], o[r][e]);
+        for (int e = 0; e < DPL; e += 2) o2[r][e / 2] = fma2(pp, pack2(vf[t][e], vf[t][e + 1]), o2[r][e / 2]);
       }
   }
   // ---- flush the last run ----
@@ -548,7 +609,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 #pragma unroll
     for (int r = 0; r < RT; ++r)
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) s_wo[warp][r][lane * DPL + e] = o[r][e];
+      for (int e = 0; e < DPL; e += 2) unpack2(o2[r][e / 2], s_wo[warp][r][lane * DPL + e], s_wo[warp][r][lane * DPL + e + 1]);
     __syncthreads();
     for (int x = tid; x < nr * D; x += kVThreads) {
       const int r = x / D, d = x - r * D;
@@ -969,7 +1030,7 @@ int attn_status(int* status, int reset) {
 namespace oc {
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB per device
+constexpr size_t kNoAllocScratchBytes = 32u << 20;  // 32 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
