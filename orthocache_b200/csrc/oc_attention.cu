@@ -51,6 +51,8 @@ struct AttnArgs {
   float* ws_m;      // [B][max_items][Hkv][R]
   float* ws_l;
   float* ws_o;      // [B][max_items][Hkv][R][D]
+  int run_grid;     // > 0: stream kernel on this many CTAs (partials only at run starts)
+  int rt_tile;      // query rows per row tile
 };
 
 __device__ __forceinline__ int list_len(const AttnArgs& a, int b, int h) {
@@ -493,13 +495,6 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         }
       }
       l_acc = 0.f;
-    } else if (warp == 0 && lane < RT) {
-      // items after the first of a run carry no partial of their own
-      const int r0 = rt * RT;
-      if (r0 + lane < a.R) {
-        const size_t part = (((size_t)b * a.max_items + item) * a.Hkv + h) * a.R + r0;
-        a.ws_m[part + lane] = -INFINITY;
-      }
     }
 
     const int stage = k % kVStages;
@@ -675,9 +670,29 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
   const size_t stride = (size_t)a.Hkv * a.R;
   const size_t p0 = ((size_t)b * a.max_items * a.Hkv + h) * a.R + r;
 
-  // M = max_i m_i (all items in parallel)
+  // Items holding a partial.  Dense layout: every item.  Stream kernel: the
+  // first item of each CTA run -- local index 0 of this (batch, head, row
+  // tile) list and every CTA boundary c * per that falls inside it.
+  int np = n, s0 = 0, per = 1, c1 = 0;
+  if (a.run_grid > 0 && n > 0) {
+    int total = 0, before = 0;
+    for (int bb = 0; bb < a.B; ++bb)
+      for (int hh = 0; hh < a.Hkv; ++hh) {
+        const int len = list_len(a, bb, hh) * a.chunks * a.n_rt;
+        if (bb < b || (bb == b && hh < h)) before += len;
+        total += len;
+      }
+    per = (total + a.run_grid - 1) / a.run_grid;
+    s0 = before + (r / a.rt_tile) * n;
+    c1 = s0 / per + 1;                                   // first CTA boundary after s0
+    const int last = (s0 + n - 1) / per;                 // last CTA touching the list
+    np = 1 + max(0, last - c1 + 1);
+  }
+  auto pos = [&](int j) -> int { return (a.run_grid > 0 && j > 0) ? (c1 + j - 1) * per - s0 : j; };
+
+  // M = max over the partials (in parallel)
   float M = -INFINITY;
-  for (int i = tid; i < n; i += 256) M = fmaxf(M, a.ws_m[p0 + (size_t)i * stride]);
+  for (int j = tid; j < np; j += 256) M = fmaxf(M, a.ws_m[p0 + (size_t)pos(j) * stride]);
   M = warp_max(M);
   if (lane == 0) s_red[warp] = M;
   __syncthreads();
@@ -685,14 +700,14 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
   for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
   __syncthreads();
 
-  // Weights f_i = 2^(m_i - M) staged 256 at a time; thread d accumulates O[d].
+  // Weights f_j = 2^(m_j - M) staged 256 at a time; thread d accumulates O[d].
   float lpart = 0.f, O = 0.f;
   const int d = tid;
-  for (int c0 = 0; c0 < n; c0 += 256) {
-    const int i = c0 + tid;
+  for (int c0 = 0; c0 < np; c0 += 256) {
+    const int j = c0 + tid;
     float f = 0.f;
-    if (i < n) {
-      const size_t p = p0 + (size_t)i * stride;
+    if (j < np) {
+      const size_t p = p0 + (size_t)pos(j) * stride;
       const float mi = a.ws_m[p];
       if (mi != -INFINITY) {
         f = exp2f(mi - M);
@@ -702,11 +717,9 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
     s_f[tid] = f;
     __syncthreads();
     if (d < a.D) {
-      const int cn = min(256, n - c0);
-      const float* ob = a.ws_o + (p0 + (size_t)c0 * stride) * a.D + d;
-#pragma unroll 8
-      for (int j = 0; j < cn; ++j)  // items without a partial (f == 0) hold no output row
-        if (s_f[j] != 0.f) O = fmaf(s_f[j], ob[(size_t)j * stride * a.D], O);
+      const int cn = min(256, np - c0);
+      for (int jj = 0; jj < cn; ++jj)
+        if (s_f[jj] != 0.f) O = fmaf(s_f[jj], a.ws_o[(p0 + (size_t)pos(c0 + jj) * stride) * a.D + d], O);
     }
     __syncthreads();
   }
@@ -872,6 +885,8 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.chunks = bs / a.chunk;
   a.max_items = max_blocks * a.chunks;
   a.scale_log2 = kLog2e / sqrtf((float)D);
+  a.run_grid = tma ? device_sm_count() : 0;
+  a.rt_tile = rt;
   const size_t parts = (size_t)B * a.max_items * Hkv * a.R;
   char* w = static_cast<char*>(ws);
   a.ws_m = reinterpret_cast<float*>(w);

@@ -58,6 +58,17 @@ compact_kernel(const uint8_t* __restrict__ keep, int nb, int heads,
   const uint8_t* kb = keep + (size_t)b * nb * heads;
   int32_t* pb = perm + (size_t)b * nb;
 
+  if (nb <= kScanThreads) {  // one tile: count and scatter from the same scan
+    const int j = threadIdx.x;
+    bool act = false;
+    if (j < nb)
+      for (int h = 0; h < heads; ++h) act |= kb[(size_t)j * heads + h] != 0;
+    int tot;
+    const int pre = tile_scan(act, s_warp, &tot);
+    if (j < nb) pb[act ? pre : tot + (j - pre)] = j;
+    if (threadIdx.x == 0) count[b] = tot;
+    return;
+  }
   // Pass 1: number of active blocks.
   int n_active = 0;
   for (int t0 = 0; t0 < nb; t0 += kScanThreads) {
