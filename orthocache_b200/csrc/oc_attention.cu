@@ -717,9 +717,18 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
     s_f[tid] = f;
     __syncthreads();
     if (d < a.D) {
+      // Every listed partial holds a written output row (zeros when its max
+      // is -inf), so the loads are unconditional and issue together.
       const int cn = min(256, np - c0);
-      for (int jj = 0; jj < cn; ++jj)
-        if (s_f[jj] != 0.f) O = fmaf(s_f[jj], a.ws_o[(p0 + (size_t)pos(c0 + jj) * stride) * a.D + d], O);
+      int jj = 0;
+      for (; jj + 8 <= cn; jj += 8) {
+        float ov[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ov[u] = a.ws_o[(p0 + (size_t)pos(c0 + jj + u) * stride) * a.D + d];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) O = fmaf(s_f[jj + u], ov[u], O);
+      }
+      for (; jj < cn; ++jj) O = fmaf(s_f[jj], a.ws_o[(p0 + (size_t)pos(c0 + jj) * stride) * a.D + d], O);
     }
     __syncthreads();
   }
