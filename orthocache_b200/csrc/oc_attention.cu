@@ -53,6 +53,11 @@ struct AttnArgs {
   float* ws_o;      // [B][max_items][Hkv][R][D]
   int run_grid;     // > 0: stream kernel on this many CTAs (partials only at run starts)
   int rt_tile;      // query rows per row tile
+  int* ctr;         // stream kernel: per-segment arrival counters (zeroed per call)
+  void* out;        // final output (mode 0), bf16 if out_bf16
+  int out_bf16;
+  float *pm, *pl, *po;  // mode 1: (m, l, o) per output row
+  int mode;
 };
 
 __device__ __forceinline__ int list_len(const AttnArgs& a, int b, int h) {
@@ -387,6 +392,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __shared__ volatile int s_abort;
   __shared__ float s_wm[kVWarps][RT], s_wl[kVWarps][RT];
   __shared__ float s_wo[kVWarps][RT][D];
+  __shared__ int s_np, s_c1, s_s0, s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int N = total_items(a);
@@ -419,6 +425,23 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       pre.next(a);
     }
   }
+  // (batch, head) lists with no retained block produce no partial: their
+  // output rows are written here (zeros; or max -inf, sum 0 for partials).
+  for (int bh = blockIdx.x; bh < a.B * a.Hkv; bh += gridDim.x) {
+    const int bb = bh / a.Hkv, hh = bh - bb * a.Hkv;
+    if (list_len(a, bb, hh) != 0) continue;
+    for (int x = tid; x < a.R * D; x += kVThreads) {
+      const int row = x / D, d = x - row * D, sq = row / a.G, g = row - sq * a.G;
+      const size_t orow = ((size_t)bb * a.Sq + sq) * a.Hq + (size_t)hh * a.G + g;
+      if (a.mode == 0) {
+        if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(0.f);
+        else reinterpret_cast<float*>(a.out)[orow * D + d] = 0.f;
+      } else {
+        a.po[orow * D + d] = 0.f;
+        if (d == 0) { a.pm[orow] = -INFINITY; a.pl[orow] = 0.f; }
+      }
+    }
+  }
   __syncthreads();
 
   // Per-warp online-softmax state of the current run.
@@ -426,7 +449,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   f32x2 o2[RT][DPL / 2];  // output channels in packed pairs
   float l_acc = 0.f;  // this lane's (token, row) share of l
   float qv[RT][DPL];
-  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0;
+  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0, run_first_global = 0;
   // Position of the item being consumed, and of the item kVStages ahead
   // (the one a stage released now is refilled with).
   ItemIter cur, ahead;
@@ -436,47 +459,98 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   const int my_v = lane >> SH;            // value index this lane ends up holding
   const int my_t = my_v / RT, my_r = my_v % RT;
 
+  // End of a run (CTA-uniform): combine the 16 warp states into one partial,
+  // publish it, and if it is the last partial of its (batch, head, row tile)
+  // segment, merge the segment's partials into the final output.
+  auto flush_run = [&]() {
+    const int r0 = cur_rt * RT;
+    const int nr = min(RT, a.R - r0);
+    float l_sum = l_acc;
+#pragma unroll
+    for (int off = 1 << SH; off < 32; off <<= 1)  // lanes of the same row differ in the token bits
+      if ((off >> SH) >= RT) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, off);
+    if ((lane & ((1 << SH) - 1)) == 0 && my_t == 0) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+        if (r == my_r) { s_wl[warp][r] = l_sum; s_wm[warp][r] = m_run[r]; }
+    }
+#pragma unroll
+    for (int r = 0; r < RT; ++r)
+#pragma unroll
+      for (int e = 0; e < DPL; e += 2) unpack2(o2[r][e / 2], s_wo[warp][r][lane * DPL + e], s_wo[warp][r][lane * DPL + e + 1]);
+    __syncthreads();
+    const size_t stride = (size_t)a.Hkv * a.R;
+    const size_t p0 = ((size_t)cur_b * a.max_items * a.Hkv + cur_h) * a.R + r0;  // item 0, row r0
+    for (int x = tid; x < nr * D; x += kVThreads) {
+      const int r = x / D, d = x - r * D;
+      float M = -INFINITY;
+      for (int w = 0; w < kVWarps; ++w) M = fmaxf(M, s_wm[w][r]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY)
+        for (int w = 0; w < kVWarps; ++w) {
+          const float f = exp2f(s_wm[w][r] - M);
+          L = fmaf(s_wl[w][r], f, L);
+          O = fmaf(s_wo[w][r][d], f, O);
+        }
+      const size_t pr = p0 + (size_t)run_first * stride + r;
+      a.ws_o[pr * D + d] = O;
+      if (d == 0) { a.ws_m[pr] = M; a.ws_l[pr] = L; }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      // partials of this segment: its first item, and every CTA boundary inside it
+      const int n = list_len(a, cur_b, cur_h) * a.chunks;
+      const int s0 = run_first_global - run_first;
+      const int c1 = s0 / per + 1, lastc = (s0 + n - 1) / per;
+      s_np = 1 + max(0, lastc - c1 + 1);
+      s_c1 = c1;
+      s_s0 = s0;
+      const int seg = (cur_b * a.Hkv + cur_h) * a.n_rt + cur_rt;
+      s_last = atomicAdd(&a.ctr[seg], 1) == s_np - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const int np = s_np, c1 = s_c1, s0 = s_s0;
+      for (int x = tid; x < nr * D; x += kVThreads) {
+        const int r = x / D, d = x - r * D;
+        float M = -INFINITY;
+        for (int j = 0; j < np; ++j) {
+          const int it = j == 0 ? 0 : (c1 + j - 1) * per - s0;
+          M = fmaxf(M, __ldcg(a.ws_m + p0 + (size_t)it * stride + r));
+        }
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY)
+          for (int j = 0; j < np; ++j) {
+            const int it = j == 0 ? 0 : (c1 + j - 1) * per - s0;
+            const size_t pr = p0 + (size_t)it * stride + r;
+            const float f = exp2f(__ldcg(a.ws_m + pr) - M);
+            L = fmaf(__ldcg(a.ws_l + pr), f, L);
+            O = fmaf(__ldcg(a.ws_o + pr * D + d), f, O);
+          }
+        const int row = r0 + r, sq = row / a.G, g = row - sq * a.G;
+        const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + g;
+        if (a.mode == 0) {
+          const float v = L > 0.f ? O / L : 0.f;
+          if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
+          else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
+        } else {
+          a.po[orow * D + d] = L > 0.f ? O : 0.f;
+          if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
+        }
+      }
+    }
+    __syncthreads();
+  };
+
   for (int k = 0; k < n_mine; ++k) {
     const int b = cur.b, h = cur.h, rt = cur.rt, item = cur.item;
     cur.next(a);
     const bool new_run = b != cur_b || h != cur_h || rt != cur_rt;
-    if (new_run && cur_b >= 0) {
-      // ---- flush the finished run (uniform: every warp is at this item) ----
-      const int r0 = cur_rt * RT;
-      const int nr = min(RT, a.R - r0);
-      float l_sum = l_acc;
-#pragma unroll
-      for (int off = 1 << SH; off < 32; off <<= 1)  // lanes of the same row differ in the token bits
-        if ((off >> SH) >= RT) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, off);
-      if ((lane & ((1 << SH) - 1)) == 0 && my_t == 0) {
-#pragma unroll
-        for (int r = 0; r < RT; ++r)
-          if (r == my_r) { s_wl[warp][r] = l_sum; s_wm[warp][r] = m_run[r]; }
-      }
-#pragma unroll
-      for (int r = 0; r < RT; ++r)
-#pragma unroll
-        for (int e = 0; e < DPL; e += 2) unpack2(o2[r][e / 2], s_wo[warp][r][lane * DPL + e], s_wo[warp][r][lane * DPL + e + 1]);
-      __syncthreads();
-      for (int x = tid; x < nr * D; x += kVThreads) {
-        const int r = x / D, d = x - r * D;
-        float M = -INFINITY;
-        for (int w = 0; w < kVWarps; ++w) M = fmaxf(M, s_wm[w][r]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY)
-          for (int w = 0; w < kVWarps; ++w) {
-            const float f = exp2f(s_wm[w][r] - M);
-            L = fmaf(s_wl[w][r], f, L);
-            O = fmaf(s_wo[w][r][d], f, O);
-          }
-        const size_t part = (((size_t)cur_b * a.max_items + run_first) * a.Hkv + cur_h) * a.R + r0;
-        a.ws_o[(part + r) * D + d] = O;
-        if (d == 0) { a.ws_m[part + r] = M; a.ws_l[part + r] = L; }
-      }
-      __syncthreads();
-    }
+    if (new_run && cur_b >= 0) flush_run();
     if (new_run) {
-      cur_b = b; cur_h = h; cur_rt = rt; run_first = item;
+      cur_b = b; cur_h = h; cur_rt = rt; run_first = item; run_first_global = beg + k;
       const int r0 = rt * RT;
       const int nr = min(RT, a.R - r0);
       const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
@@ -588,40 +662,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         for (int e = 0; e < DPL; e += 2) o2[r][e / 2] = fma2(pp, pack2(vf[t][e], vf[t][e + 1]), o2[r][e / 2]);
       }
   }
-  // ---- flush the last run ----
-  if (cur_b >= 0) {
-    const int r0 = cur_rt * RT;
-    const int nr = min(RT, a.R - r0);
-    float l_sum = l_acc;
-#pragma unroll
-    for (int off = 1 << SH; off < 32; off <<= 1)
-      if ((off >> SH) >= RT) l_sum += __shfl_xor_sync(0xffffffffu, l_sum, off);
-    if ((lane & ((1 << SH) - 1)) == 0 && my_t == 0) {
-#pragma unroll
-      for (int r = 0; r < RT; ++r)
-        if (r == my_r) { s_wl[warp][r] = l_sum; s_wm[warp][r] = m_run[r]; }
-    }
-#pragma unroll
-    for (int r = 0; r < RT; ++r)
-#pragma unroll
-      for (int e = 0; e < DPL; e += 2) unpack2(o2[r][e / 2], s_wo[warp][r][lane * DPL + e], s_wo[warp][r][lane * DPL + e + 1]);
-    __syncthreads();
-    for (int x = tid; x < nr * D; x += kVThreads) {
-      const int r = x / D, d = x - r * D;
-      float M = -INFINITY;
-      for (int w = 0; w < kVWarps; ++w) M = fmaxf(M, s_wm[w][r]);
-      float L = 0.f, O = 0.f;
-      if (M != -INFINITY)
-        for (int w = 0; w < kVWarps; ++w) {
-          const float f = exp2f(s_wm[w][r] - M);
-          L = fmaf(s_wl[w][r], f, L);
-          O = fmaf(s_wo[w][r][d], f, O);
-        }
-      const size_t part = (((size_t)cur_b * a.max_items + run_first) * a.Hkv + cur_h) * a.R + r0;
-      a.ws_o[(part + r) * D + d] = O;
-      if (d == 0) { a.ws_m[part + r] = M; a.ws_l[part + r] = L; }
-    }
-  }
+  if (cur_b >= 0) flush_run();
 }
 
 template <int D>
@@ -818,7 +859,8 @@ size_t attn_ws_bytes(int B, int Sq, int Hq, int Hkv, int D, int bs, int max_bloc
   const size_t R = (size_t)Sq * G;
   const size_t items = (size_t)max_blocks * (bs / chunk_for(bs, D));
   const size_t parts = (size_t)B * items * Hkv * R;
-  return 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float));
+  const size_t segs = (size_t)B * Hkv * R;  // row-tile segments (upper bound) for the arrival counters
+  return 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float)) + align256(segs * sizeof(int));
 }
 
 int validate_attn(const void* q, const void* k, const void* v, int dtype, const int32_t* idx,
@@ -901,16 +943,25 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.ws_m = reinterpret_cast<float*>(w);
   a.ws_l = reinterpret_cast<float*>(w + align256(parts * sizeof(float)));
   a.ws_o = reinterpret_cast<float*>(w + 2 * align256(parts * sizeof(float)));
+  a.ctr = reinterpret_cast<int*>(w + 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float)));
+  a.out = out;
+  a.out_bf16 = out_dtype == OC_BF16;
+  a.pm = pm; a.pl = pl; a.po = po;
+  a.mode = mode;
   const int64_t rows = (int64_t)B * Hkv * a.R;
   OC_REQUIRE(rows < (1ll << 31), OC_ERR_CAPACITY, "attention: too many rows");
 
+  if (tma && max_blocks > 0) {
+    // The stream kernel merges in place: it needs its arrival counters at zero.
+    const size_t segs = (size_t)B * Hkv * a.n_rt;
+    cudaError_t e = cudaMemsetAsync(a.ctr, 0, segs * sizeof(int), st);
+    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "attention: %s", cudaGetErrorString(e));
+    return D == 64 ? launch_attn_stream<64>(a, rt, st) : D == 128 ? launch_attn_stream<128>(a, rt, st)
+                                                       : launch_attn_stream<256>(a, rt, st);
+  }
   if (max_blocks > 0) {
     const int grid = device_sm_count() * 2;
-    if (tma)
-      rc = D == 64 ? launch_attn_stream<64>(a, rt, st) : D == 128 ? launch_attn_stream<128>(a, rt, st)
-                                                        : launch_attn_stream<256>(a, rt, st);
-    else
-      rc = dtype == OC_F32 ? launch_partials<float>(a, rt, grid, st)
+    rc = dtype == OC_F32 ? launch_partials<float>(a, rt, grid, st)
                            : launch_partials<__nv_bfloat16>(a, rt, grid, st);
     if (rc) return rc;
   }
