@@ -393,6 +393,8 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __shared__ float s_wm[kVWarps][RT], s_wl[kVWarps][RT];
   __shared__ float s_wo[kVWarps][RT][D];
   __shared__ int s_np, s_c1, s_s0, s_last;
+  constexpr int kMaxParts = 160;  // partials of one segment staged in shared memory
+  __shared__ float s_pm[kMaxParts][RT], s_pl[kMaxParts][RT];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int N = total_items(a);
@@ -513,22 +515,43 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     if (s_last) {
       __threadfence();
       const int np = s_np, c1 = s_c1, s0 = s_s0;
+      auto item_of = [&](int j) { return j == 0 ? 0 : (c1 + j - 1) * per - s0; };
+      const bool staged = np <= kMaxParts;
+      if (staged) {  // maxima and sums of all partials into shared memory, in parallel
+        for (int idx = tid; idx < np * nr; idx += kVThreads) {
+          const int j = idx / nr, r = idx - j * nr;
+          const size_t pr = p0 + (size_t)item_of(j) * stride + r;
+          s_pm[j][r] = __ldcg(a.ws_m + pr);
+          s_pl[j][r] = __ldcg(a.ws_l + pr);
+        }
+        __syncthreads();
+      }
       for (int x = tid; x < nr * D; x += kVThreads) {
         const int r = x / D, d = x - r * D;
+        auto m_of = [&](int j) { return staged ? s_pm[j][r] : __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r); };
+        auto l_of = [&](int j) { return staged ? s_pl[j][r] : __ldcg(a.ws_l + p0 + (size_t)item_of(j) * stride + r); };
         float M = -INFINITY;
-        for (int j = 0; j < np; ++j) {
-          const int it = j == 0 ? 0 : (c1 + j - 1) * per - s0;
-          M = fmaxf(M, __ldcg(a.ws_m + p0 + (size_t)it * stride + r));
-        }
+        for (int j = 0; j < np; ++j) M = fmaxf(M, m_of(j));
         float L = 0.f, O = 0.f;
-        if (M != -INFINITY)
-          for (int j = 0; j < np; ++j) {
-            const int it = j == 0 ? 0 : (c1 + j - 1) * per - s0;
-            const size_t pr = p0 + (size_t)it * stride + r;
-            const float f = exp2f(__ldcg(a.ws_m + pr) - M);
-            L = fmaf(__ldcg(a.ws_l + pr), f, L);
-            O = fmaf(__ldcg(a.ws_o + pr * D + d), f, O);
+        if (M != -INFINITY) {
+          int j = 0;
+          for (; j + 8 <= np; j += 8) {  // eight output-row loads in flight
+            float ov[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ov[u] = __ldcg(a.ws_o + (p0 + (size_t)item_of(j + u) * stride + r) * D + d);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float f = exp2f(m_of(j + u) - M);
+              L = fmaf(l_of(j + u), f, L);
+              O = fmaf(ov[u], f, O);
+            }
           }
+          for (; j < np; ++j) {
+            const float f = exp2f(m_of(j) - M);
+            L = fmaf(l_of(j), f, L);
+            O = fmaf(__ldcg(a.ws_o + (p0 + (size_t)item_of(j) * stride + r) * D + d), f, O);
+          }
+        }
         const int row = r0 + r, sq = row / a.G, g = row - sq * a.G;
         const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + g;
         if (a.mode == 0) {
