@@ -714,6 +714,374 @@ int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
   return check_launch("attn_stream_kernel");
 }
 
+// ---------------------------------------------------------------------------
+// bfloat16 path on tensor cores (D = 64 or 128).  Same item order, contiguous
+// per-CTA ranges, TMA stage ring and in-place segment merge as the CUDA-core
+// stream kernel above, but each warp owns 16 tokens of every item and does
+// both products with warp-level MMA (m16n8k16, bf16 inputs, fp32
+// accumulation): S = Q K^T with the query rows of the tile as M (padded to
+// 16), then O += P V with P taken straight from the S accumulators.  K and V
+// arrive as 128-byte swizzled boxes of 64 channels, so every ldmatrix of a
+// stage is free of bank conflicts.
+// ---------------------------------------------------------------------------
+constexpr int kMStages = 3;
+constexpr int kMStageBytes = 32768;  // K + V of one item
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Byte offset of (token t, 16-byte chunk of channels c8) in a swizzled tile of
+// CH rows stored as D/64 boxes of 128-byte rows.
+template <int CH>
+__device__ __forceinline__ uint32_t swz(int t, int c8) {
+  return (uint32_t)((c8 >> 3) * (CH * 128) + t * 128 + (((c8 & 7) ^ (t & 7)) << 4));
+}
+
+template <int D, int RT>
+__global__ void __launch_bounds__(32 * (8192 / D) / 16, 1)
+attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+  constexpr int CH = 8192 / D;           // tokens per item
+  constexpr int NW = CH / 16;            // warps: 16 tokens each
+  constexpr int NT = 32 * NW;
+  constexpr int KS = D / 16;             // k-steps of S = Q K^T
+  constexpr int NO = D / 8;              // n-tiles of O
+  constexpr int KB = CH * D * 2;         // bytes of the K (or V) half of a stage
+  static_assert(RT == 4 || RT == 8, "row tile");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full[kMStages];
+  __shared__ int s_rel[kMStages];
+  __shared__ volatile int s_abort;
+  __shared__ float s_wm[NW][RT], s_wl[NW][RT];
+  __shared__ float s_wo[NW][RT][D];
+  __shared__ int s_np, s_c1, s_s0, s_last;
+  constexpr int kMaxParts = 160;
+  __shared__ float s_pm[kMaxParts][RT], s_pl[kMaxParts][RT];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;  // MMA fragment coordinates
+  const int N = total_items(a);
+  const int per = (N + gridDim.x - 1) / gridDim.x;
+  const int beg = min(N, (int)blockIdx.x * per), end = min(N, beg + per);
+  const int n_mine = end - beg;
+
+  auto issue = [&](int k, const ItemIter& pos) {
+    const int slot = pos.item / a.chunks, cc = pos.item - slot * a.chunks;
+    const int blk = a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
+    const int y = (blk < 0 || blk >= a.S / a.bs) ? pos.b * a.S : pos.b * a.S + blk * a.bs + cc * CH;
+    uint8_t* dst = smem + (size_t)(k % kMStages) * kMStageBytes;
+    uint64_t* bar = &full[k % kMStages];
+    mbar_expect_tx(bar, 2 * KB);
+#pragma unroll
+    for (int jb = 0; jb < D / 64; ++jb) {
+      tma_load_2d(dst + jb * (CH * 128), &kmap, bar, pos.h * D + jb * 64, y);
+      tma_load_2d(dst + KB + jb * (CH * 128), &vmap, bar, pos.h * D + jb * 64, y);
+    }
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < kMStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
+    fence_mbar_init();
+    s_abort = 0;
+    ItemIter pre;
+    pre.start(a, beg, N);
+    for (int k = 0; k < kMStages && k < n_mine; ++k) {
+      issue(k, pre);
+      pre.next(a);
+    }
+  }
+  for (int bh = blockIdx.x; bh < a.B * a.Hkv; bh += gridDim.x) {  // lists with no retained block
+    const int bb = bh / a.Hkv, hh = bh - bb * a.Hkv;
+    if (list_len(a, bb, hh) != 0) continue;
+    for (int x = tid; x < a.R * D; x += NT) {
+      const int row = x / D, d = x - row * D, sq = row / a.G, gg = row - sq * a.G;
+      const size_t orow = ((size_t)bb * a.Sq + sq) * a.Hq + (size_t)hh * a.G + gg;
+      if (a.mode == 0) {
+        if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(0.f);
+        else reinterpret_cast<float*>(a.out)[orow * D + d] = 0.f;
+      } else {
+        a.po[orow * D + d] = 0.f;
+        if (d == 0) { a.pm[orow] = -INFINITY; a.pl[orow] = 0.f; }
+      }
+    }
+  }
+  __syncthreads();
+
+  // per-warp online-softmax state of the run: rows g and g + 8 of the tile
+  float m_run[2], l_acc[2];
+  float o[NO][4];
+  uint32_t qa[KS][4];
+  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0, run_first_global = 0;
+  ItemIter cur, ahead;
+  cur.start(a, beg, N);
+  ahead.start(a, beg, N);
+  for (int i = 0; i < kMStages; ++i) ahead.next(a);
+
+  // End of a run (CTA-uniform): combine the warp states into one partial,
+  // publish it, and merge the segment if this is its last partial.
+  auto flush_run = [&]() {
+    const int r0 = cur_rt * RT;
+    const int nr = min(RT, a.R - r0);
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float l = l_acc[hf];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      const int row = g + 8 * hf;
+      if (row < RT) {
+        if (c == 0) { s_wl[warp][row] = l; s_wm[warp][row] = m_run[hf]; }
+#pragma unroll
+        for (int nt = 0; nt < NO; ++nt) {
+          s_wo[warp][row][8 * nt + 2 * c] = o[nt][2 * hf];
+          s_wo[warp][row][8 * nt + 2 * c + 1] = o[nt][2 * hf + 1];
+        }
+      }
+    }
+    __syncthreads();
+    const size_t stride = (size_t)a.Hkv * a.R;
+    const size_t p0 = ((size_t)cur_b * a.max_items * a.Hkv + cur_h) * a.R + r0;  // item 0, row r0
+    for (int x = tid; x < nr * D; x += NT) {
+      const int r = x / D, d = x - r * D;
+      float M = -INFINITY;
+      for (int w = 0; w < NW; ++w) M = fmaxf(M, s_wm[w][r]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY)
+        for (int w = 0; w < NW; ++w) {
+          const float f = exp2f(s_wm[w][r] - M);
+          L = fmaf(s_wl[w][r], f, L);
+          O = fmaf(s_wo[w][r][d], f, O);
+        }
+      const size_t pr = p0 + (size_t)run_first * stride + r;
+      a.ws_o[pr * D + d] = O;
+      if (d == 0) { a.ws_m[pr] = M; a.ws_l[pr] = L; }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int n = list_len(a, cur_b, cur_h) * a.chunks;
+      const int s0 = run_first_global - run_first;
+      const int c1 = s0 / per + 1, lastc = (s0 + n - 1) / per;
+      s_np = 1 + max(0, lastc - c1 + 1);
+      s_c1 = c1;
+      s_s0 = s0;
+      const int seg = (cur_b * a.Hkv + cur_h) * a.n_rt + cur_rt;
+      s_last = atomicAdd(&a.ctr[seg], 1) == s_np - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const int np = s_np, c1 = s_c1, s0 = s_s0;
+      auto item_of = [&](int j) { return j == 0 ? 0 : (c1 + j - 1) * per - s0; };
+      const bool staged = np <= kMaxParts;
+      if (staged) {
+        for (int idx = tid; idx < np * nr; idx += NT) {
+          const int j = idx / nr, r = idx - j * nr;
+          const size_t pr = p0 + (size_t)item_of(j) * stride + r;
+          s_pm[j][r] = __ldcg(a.ws_m + pr);
+          s_pl[j][r] = __ldcg(a.ws_l + pr);
+        }
+        __syncthreads();
+      }
+      for (int x = tid; x < nr * D; x += NT) {
+        const int r = x / D, d = x - r * D;
+        auto m_of = [&](int j) { return staged ? s_pm[j][r] : __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r); };
+        auto l_of = [&](int j) { return staged ? s_pl[j][r] : __ldcg(a.ws_l + p0 + (size_t)item_of(j) * stride + r); };
+        float M = -INFINITY;
+        for (int j = 0; j < np; ++j) M = fmaxf(M, m_of(j));
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+          int j = 0;
+          for (; j + 8 <= np; j += 8) {
+            float ov[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ov[u] = __ldcg(a.ws_o + (p0 + (size_t)item_of(j + u) * stride + r) * D + d);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float f = exp2f(m_of(j + u) - M);
+              L = fmaf(l_of(j + u), f, L);
+              O = fmaf(ov[u], f, O);
+            }
+          }
+          for (; j < np; ++j) {
+            const float f = exp2f(m_of(j) - M);
+            L = fmaf(l_of(j), f, L);
+            O = fmaf(__ldcg(a.ws_o + (p0 + (size_t)item_of(j) * stride + r) * D + d), f, O);
+          }
+        }
+        const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
+        const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
+        if (a.mode == 0) {
+          const float v = L > 0.f ? O / L : 0.f;
+          if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
+          else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
+        } else {
+          a.po[orow * D + d] = L > 0.f ? O : 0.f;
+          if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
+        }
+      }
+    }
+    __syncthreads();
+  };
+
+  for (int k = 0; k < n_mine; ++k) {
+    const int b = cur.b, h = cur.h, rt = cur.rt, item = cur.item;
+    cur.next(a);
+    const bool new_run = b != cur_b || h != cur_h || rt != cur_rt;
+    if (new_run && cur_b >= 0) flush_run();
+    if (new_run) {
+      cur_b = b; cur_h = h; cur_rt = rt; run_first = item; run_first_global = beg + k;
+      const int r0 = rt * RT;
+      const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
+      // A fragments of Q (rows g and g + 8 of the tile; rows past the tile are zero)
+      const uint32_t* qrow[2] = {nullptr, nullptr};
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int rr = g + 8 * hf;
+        const int row = r0 + rr;
+        if (rr < RT && row < a.R) {
+          const int s = row / a.G, gq = row - s * a.G;
+          qrow[hf] = reinterpret_cast<const uint32_t*>(qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D);
+        }
+      }
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        qa[ks][0] = qrow[0] ? qrow[0][8 * ks + c] : 0u;      // row g,     channels 16ks + 2c, +1
+        qa[ks][1] = qrow[1] ? qrow[1][8 * ks + c] : 0u;      // row g + 8
+        qa[ks][2] = qrow[0] ? qrow[0][8 * ks + 4 + c] : 0u;  // row g,     channels 16ks + 8 + 2c, +1
+        qa[ks][3] = qrow[1] ? qrow[1][8 * ks + 4 + c] : 0u;
+      }
+      m_run[0] = m_run[1] = -INFINITY;
+      l_acc[0] = l_acc[1] = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < NO; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    }
+
+    const int stage = k % kMStages;
+    if (!s_abort && !mbar_wait(&full[stage], (k / kMStages) & 1)) {
+      s_abort = 1;
+      if (lane == 0) atomicExch(&g_attn_status, 1);
+    }
+    const int slot = item / a.chunks;
+    const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
+    const bool valid = !s_abort && blk >= 0 && blk < a.S / a.bs;
+    const uint32_t ks_base = smem_u32(smem + (size_t)stage * kMStageBytes);
+    const uint32_t vs_base = ks_base + KB;
+    // All fragments of this warp's 16 tokens, then the stage is released.
+    uint32_t kb[KS][4], vb[NO / 2][4];
+    {
+      const int mm = lane >> 3, rr = lane & 7;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks)  // matrices: (tokens 0-7 | 8-15) x (channels 16ks..+8 | +8..+16)
+        ldsm_x4(kb[ks], ks_base + swz<CH>(16 * warp + 8 * (mm >> 1) + rr, 2 * ks + (mm & 1)));
+#pragma unroll
+      for (int np2 = 0; np2 < NO / 2; ++np2)  // matrices: (tokens 0-7 | 8-15) x (channel tiles 2np2 | 2np2+1)
+        ldsm_x4_t(vb[np2], vs_base + swz<CH>(16 * warp + 8 * (mm & 1) + rr, 2 * np2 + (mm >> 1)));
+    }
+    __syncwarp();
+    if (lane == 0 && atomicAdd(&s_rel[stage], 1) == NW - 1) {
+      s_rel[stage] = 0;
+      if (k + kMStages < n_mine && !s_abort) {
+        fence_proxy_async();
+        issue(k + kMStages, ahead);
+      }
+    }
+    ahead.next(a);
+    if (!valid) continue;
+
+    // S = Q K^T for the two 8-token tiles (rows g, g+8; tokens 2c, 2c+1)
+    float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      mma_bf16_16816(sa[0], qa[ks], kb[ks][0], kb[ks][1]);
+      mma_bf16_16816(sa[1], qa[ks], kb[ks][2], kb[ks][3]);
+    }
+    // online softmax in log2 units
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sa[j][e] *= a.scale_log2;
+    float alpha[2];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float mx = fmaxf(fmaxf(sa[0][2 * hf], sa[0][2 * hf + 1]), fmaxf(sa[1][2 * hf], sa[1][2 * hf + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m_run[hf], mx);
+      alpha[hf] = exp2f(m_run[hf] - mn);
+      m_run[hf] = mn;
+      float ls = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float p = exp2f(sa[j][2 * hf + e] - mn);
+          sa[j][2 * hf + e] = p;
+          ls += p;
+        }
+      l_acc[hf] = fmaf(l_acc[hf], alpha[hf], ls);
+    }
+    const uint32_t pa[4] = {pack_bf16x2(sa[0][0], sa[0][1]), pack_bf16x2(sa[0][2], sa[0][3]),
+                            pack_bf16x2(sa[1][0], sa[1][1]), pack_bf16x2(sa[1][2], sa[1][3])};
+#pragma unroll
+    for (int nt = 0; nt < NO; ++nt) {
+      o[nt][0] *= alpha[0]; o[nt][1] *= alpha[0];
+      o[nt][2] *= alpha[1]; o[nt][3] *= alpha[1];
+    }
+    // O += P V over the warp's 16 tokens
+#pragma unroll
+    for (int np2 = 0; np2 < NO / 2; ++np2) {
+      mma_bf16_16816(o[2 * np2], pa, vb[np2][0], vb[np2][1]);
+      mma_bf16_16816(o[2 * np2 + 1], pa, vb[np2][2], vb[np2][3]);
+    }
+  }
+  if (cur_b >= 0) flush_run();
+}
+
+template <int D>
+int launch_attn_mma(const AttnArgs& a, int rt, cudaStream_t st) {
+  constexpr int CH = 8192 / D;
+  constexpr int NT = 32 * CH / 16;
+  CUtensorMap km, vm;
+  const uint64_t cols = (uint64_t)a.Hkv * D, rows = (uint64_t)a.B * a.S;
+  int rc = encode_map_2d(&km, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, CH, true);
+  if (!rc) rc = encode_map_2d(&vm, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, CH, true);
+  if (rc) return set_error(OC_ERR_CUDA, "attention: tensor map encode failed (%d)", rc);
+  const int smem = kMStages * kMStageBytes + 1024;
+  const int grid = a.run_grid;
+#define OC_AMMA(RTV)                                                                                   \
+  do {                                                                                                 \
+    cudaFuncSetAttribute(attn_mma_kernel<D, RTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    attn_mma_kernel<D, RTV><<<grid, NT, smem, st>>>(km, vm, a);                                        \
+  } while (0)
+  if (rt <= 4) OC_AMMA(4);
+  else OC_AMMA(8);
+#undef OC_AMMA
+  return check_launch("attn_mma_kernel");
+}
+
 // Combine the items of one (batch, kv head, row): M = max m_i,
 // L = sum l_i 2^(m_i - M), O = sum o_i 2^(m_i - M).  mode 0 writes O / L in
 // the output dtype at the reference's (Sq, Hq, D) position (zeros when the
@@ -951,9 +1319,11 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.B = B; a.Sq = Sq; a.Hq = Hq; a.Hkv = Hkv; a.G = Hq / Hkv; a.D = D; a.S = S; a.bs = bs;
   a.R = Sq * a.G;
   const bool tma = use_tma_path(dtype, bs, D);
+  const bool mma = tma && (D == 64 || D == 128);  // tensor-core stream kernel
   int rt = pick_rt(a.R, D);
   if (tma && rt * D > 512) rt = 512 / D;
   if (tma && rt > 4) rt = 4;
+  if (mma) rt = a.R <= 4 ? 4 : 8;
   a.n_rt = (a.R + rt - 1) / rt;
   a.chunk = chunk_for(bs, D);
   a.chunks = bs / a.chunk;
@@ -979,8 +1349,8 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
     const size_t segs = (size_t)B * Hkv * a.n_rt;
     cudaError_t e = cudaMemsetAsync(a.ctr, 0, segs * sizeof(int), st);
     if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "attention: %s", cudaGetErrorString(e));
-    return D == 64 ? launch_attn_stream<64>(a, rt, st) : D == 128 ? launch_attn_stream<128>(a, rt, st)
-                                                       : launch_attn_stream<256>(a, rt, st);
+    if (mma) return D == 64 ? launch_attn_mma<64>(a, rt, st) : launch_attn_mma<128>(a, rt, st);
+    return launch_attn_stream<256>(a, rt, st);
   }
   if (max_blocks > 0) {
     const int grid = device_sm_count() * 2;

@@ -28,6 +28,9 @@ CASES = [  # (Sq, Hq, Hkv, D, nb, bs, dtype, keep_prob)
     (1, 16, 16, 256, 4, 512, torch.bfloat16, 0.5),
     (2, 8, 2, 256, 3, 256, torch.bfloat16, 1.0),   # R = 8 at D=256 -> tiles of 4
     (1, 2, 2, 128, 5, 64, torch.float32, 0.4),      # 64-token blocks
+    (3, 16, 4, 128, 6, 512, torch.bfloat16, 0.5),   # R = 12 rows -> two 8-row tensor-core tiles
+    (1, 8, 8, 64, 6, 512, torch.bfloat16, 0.5),     # D = 64 on tensor cores
+    (2, 4, 1, 128, 9, 128, torch.bfloat16, 0.7),    # 128-token blocks, R = 8
 ]
 
 
