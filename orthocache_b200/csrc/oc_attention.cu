@@ -1329,7 +1329,9 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.chunks = bs / a.chunk;
   a.max_items = max_blocks * a.chunks;
   a.scale_log2 = kLog2e / sqrtf((float)D);
-  a.run_grid = tma ? device_sm_count() : 0;
+  // Stream kernels: persistent grid (two CTAs per SM for the tensor-core one,
+  // whose 115 KB of shared memory and 224 registers per thread allow it).
+  a.run_grid = tma ? device_sm_count() * (mma ? 2 : 1) : 0;
   a.rt_tile = rt;
   const size_t parts = (size_t)B * a.max_items * Hkv * a.R;
   char* w = static_cast<char*>(ws);
