@@ -395,6 +395,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __shared__ int s_np, s_c1, s_s0, s_last;
   constexpr int kMaxParts = 160;  // partials of one segment staged in shared memory
   __shared__ float s_pm[kMaxParts][RT], s_pl[kMaxParts][RT];
+  __shared__ float s_rowM[RT], s_rowL[RT];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int N = total_items(a);
@@ -517,7 +518,8 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       const int np = s_np, c1 = s_c1, s0 = s_s0;
       auto item_of = [&](int j) { return j == 0 ? 0 : (c1 + j - 1) * per - s0; };
       const bool staged = np <= kMaxParts;
-      if (staged) {  // maxima and sums of all partials into shared memory, in parallel
+      if (staged) {
+        // maxima and sums of all partials into shared memory, in parallel
         for (int idx = tid; idx < np * nr; idx += kVThreads) {
           const int j = idx / nr, r = idx - j * nr;
           const size_t pr = p0 + (size_t)item_of(j) * stride + r;
@@ -525,42 +527,85 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
           s_pl[j][r] = __ldcg(a.ws_l + pr);
         }
         __syncthreads();
-      }
-      for (int x = tid; x < nr * D; x += kVThreads) {
-        const int r = x / D, d = x - r * D;
-        auto m_of = [&](int j) { return staged ? s_pm[j][r] : __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r); };
-        auto l_of = [&](int j) { return staged ? s_pl[j][r] : __ldcg(a.ws_l + p0 + (size_t)item_of(j) * stride + r); };
-        float M = -INFINITY;
-        for (int j = 0; j < np; ++j) M = fmaxf(M, m_of(j));
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-          int j = 0;
-          for (; j + 8 <= np; j += 8) {  // eight output-row loads in flight
-            float ov[8];
+        if (tid < nr) {  // per-row max and sum
+          float M = -INFINITY;
+          for (int j = 0; j < np; ++j) M = fmaxf(M, s_pm[j][tid]);
+          float L = 0.f;
+          if (M != -INFINITY)
+            for (int j = 0; j < np; ++j) L = fmaf(s_pl[j][tid], exp2f(s_pm[j][tid] - M), L);
+          s_rowM[tid] = M;
+          s_rowL[tid] = L;
+        }
+        __syncthreads();
+        for (int idx = tid; idx < np * nr; idx += kVThreads) {  // weights, in place of the maxima
+          const int j = idx / nr, r = idx - j * nr;
+          s_pm[j][r] = s_rowM[r] == -INFINITY ? 0.f : exp2f(s_pm[j][r] - s_rowM[r]);
+        }
+        __syncthreads();
+        // every output this thread owns, with all loads of a batch of partials in flight
+        constexpr int XPT = (RT * D + kVThreads - 1) / kVThreads;
+        float acc[XPT];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) ov[u] = __ldcg(a.ws_o + (p0 + (size_t)item_of(j + u) * stride + r) * D + d);
+        for (int i = 0; i < XPT; ++i) acc[i] = 0.f;
+        for (int j0 = 0; j0 < np; j0 += 4) {
+          float ov[4][XPT];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const float f = exp2f(m_of(j + u) - M);
-              L = fmaf(l_of(j + u), f, L);
-              O = fmaf(ov[u], f, O);
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < XPT; ++i) {
+              const int x = tid + i * kVThreads;
+              const int r = x / D, d = x - r * D;
+              ov[u][i] = (j0 + u < np && x < nr * D)
+                             ? __ldcg(a.ws_o + (p0 + (size_t)item_of(j0 + u) * stride + r) * D + d) : 0.f;
             }
-          }
-          for (; j < np; ++j) {
-            const float f = exp2f(m_of(j) - M);
-            L = fmaf(l_of(j), f, L);
-            O = fmaf(__ldcg(a.ws_o + (p0 + (size_t)item_of(j) * stride + r) * D + d), f, O);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < XPT; ++i) {
+              const int x = tid + i * kVThreads;
+              if (j0 + u < np && x < nr * D) acc[i] = fmaf(s_pm[j0 + u][x / D], ov[u][i], acc[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < XPT; ++i) {
+          const int x = tid + i * kVThreads;
+          if (x >= nr * D) continue;
+          const int r = x / D, d = x - r * D;
+          const float M = s_rowM[r], L = s_rowL[r], O = acc[i];
+          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
+          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
+          if (a.mode == 0) {
+            const float v = L > 0.f ? O / L : 0.f;
+            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
+            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
+          } else {
+            a.po[orow * D + d] = L > 0.f ? O : 0.f;
+            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
           }
         }
-        const int row = r0 + r, sq = row / a.G, g = row - sq * a.G;
-        const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + g;
-        if (a.mode == 0) {
-          const float v = L > 0.f ? O / L : 0.f;
-          if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
-          else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
-        } else {
-          a.po[orow * D + d] = L > 0.f ? O : 0.f;
-          if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
+      } else {
+        for (int x = tid; x < nr * D; x += kVThreads) {  // many partials: one output at a time
+          const int r = x / D, d = x - r * D;
+          float M = -INFINITY;
+          for (int j = 0; j < np; ++j) M = fmaxf(M, __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r));
+          float L = 0.f, O = 0.f;
+          if (M != -INFINITY)
+            for (int j = 0; j < np; ++j) {
+              const size_t pr = p0 + (size_t)item_of(j) * stride + r;
+              const float f = exp2f(__ldcg(a.ws_m + pr) - M);
+              L = fmaf(__ldcg(a.ws_l + pr), f, L);
+              O = fmaf(__ldcg(a.ws_o + pr * D + d), f, O);
+            }
+          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
+          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
+          if (a.mode == 0) {
+            const float v = L > 0.f ? O / L : 0.f;
+            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
+            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
+          } else {
+            a.po[orow * D + d] = L > 0.f ? O : 0.f;
+            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
+          }
         }
       }
     }
@@ -727,6 +772,13 @@ int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
 constexpr int kMStages = 3;
 constexpr int kMStageBytes = 32768;  // K + V of one item
 
+#ifdef OC_TIMING
+__device__ unsigned long long g_tstamp[4096][4];
+#define OC_STAMP(i) do { if (threadIdx.x == 0 && blockIdx.x < 4096) g_tstamp[blockIdx.x][i] = globaltimer_ns(); } while (0)
+#else
+#define OC_STAMP(i) do {} while (0)
+#endif
+
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -780,7 +832,9 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   __shared__ int s_np, s_c1, s_s0, s_last;
   constexpr int kMaxParts = 160;
   __shared__ float s_pm[kMaxParts][RT], s_pl[kMaxParts][RT];
+  __shared__ float s_rowM[RT], s_rowL[RT];
 
+  OC_STAMP(0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;  // MMA fragment coordinates
   const int N = total_items(a);
@@ -839,6 +893,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   cur.start(a, beg, N);
   ahead.start(a, beg, N);
   for (int i = 0; i < kMStages; ++i) ahead.next(a);
+  OC_STAMP(1);
 
   // End of a run (CTA-uniform): combine the warp states into one partial,
   // publish it, and merge the segment if this is its last partial.
@@ -897,6 +952,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
       auto item_of = [&](int j) { return j == 0 ? 0 : (c1 + j - 1) * per - s0; };
       const bool staged = np <= kMaxParts;
       if (staged) {
+        // maxima and sums of all partials into shared memory, in parallel
         for (int idx = tid; idx < np * nr; idx += NT) {
           const int j = idx / nr, r = idx - j * nr;
           const size_t pr = p0 + (size_t)item_of(j) * stride + r;
@@ -904,42 +960,85 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
           s_pl[j][r] = __ldcg(a.ws_l + pr);
         }
         __syncthreads();
-      }
-      for (int x = tid; x < nr * D; x += NT) {
-        const int r = x / D, d = x - r * D;
-        auto m_of = [&](int j) { return staged ? s_pm[j][r] : __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r); };
-        auto l_of = [&](int j) { return staged ? s_pl[j][r] : __ldcg(a.ws_l + p0 + (size_t)item_of(j) * stride + r); };
-        float M = -INFINITY;
-        for (int j = 0; j < np; ++j) M = fmaxf(M, m_of(j));
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-          int j = 0;
-          for (; j + 8 <= np; j += 8) {
-            float ov[8];
+        if (tid < nr) {  // per-row max and sum
+          float M = -INFINITY;
+          for (int j = 0; j < np; ++j) M = fmaxf(M, s_pm[j][tid]);
+          float L = 0.f;
+          if (M != -INFINITY)
+            for (int j = 0; j < np; ++j) L = fmaf(s_pl[j][tid], exp2f(s_pm[j][tid] - M), L);
+          s_rowM[tid] = M;
+          s_rowL[tid] = L;
+        }
+        __syncthreads();
+        for (int idx = tid; idx < np * nr; idx += NT) {  // weights, in place of the maxima
+          const int j = idx / nr, r = idx - j * nr;
+          s_pm[j][r] = s_rowM[r] == -INFINITY ? 0.f : exp2f(s_pm[j][r] - s_rowM[r]);
+        }
+        __syncthreads();
+        // every output this thread owns, with all loads of a batch of partials in flight
+        constexpr int XPT = (RT * D + NT - 1) / NT;
+        float acc[XPT];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) ov[u] = __ldcg(a.ws_o + (p0 + (size_t)item_of(j + u) * stride + r) * D + d);
+        for (int i = 0; i < XPT; ++i) acc[i] = 0.f;
+        for (int j0 = 0; j0 < np; j0 += 4) {
+          float ov[4][XPT];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const float f = exp2f(m_of(j + u) - M);
-              L = fmaf(l_of(j + u), f, L);
-              O = fmaf(ov[u], f, O);
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < XPT; ++i) {
+              const int x = tid + i * NT;
+              const int r = x / D, d = x - r * D;
+              ov[u][i] = (j0 + u < np && x < nr * D)
+                             ? __ldcg(a.ws_o + (p0 + (size_t)item_of(j0 + u) * stride + r) * D + d) : 0.f;
             }
-          }
-          for (; j < np; ++j) {
-            const float f = exp2f(m_of(j) - M);
-            L = fmaf(l_of(j), f, L);
-            O = fmaf(__ldcg(a.ws_o + (p0 + (size_t)item_of(j) * stride + r) * D + d), f, O);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < XPT; ++i) {
+              const int x = tid + i * NT;
+              if (j0 + u < np && x < nr * D) acc[i] = fmaf(s_pm[j0 + u][x / D], ov[u][i], acc[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < XPT; ++i) {
+          const int x = tid + i * NT;
+          if (x >= nr * D) continue;
+          const int r = x / D, d = x - r * D;
+          const float M = s_rowM[r], L = s_rowL[r], O = acc[i];
+          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
+          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
+          if (a.mode == 0) {
+            const float v = L > 0.f ? O / L : 0.f;
+            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
+            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
+          } else {
+            a.po[orow * D + d] = L > 0.f ? O : 0.f;
+            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
           }
         }
-        const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
-        const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
-        if (a.mode == 0) {
-          const float v = L > 0.f ? O / L : 0.f;
-          if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
-          else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
-        } else {
-          a.po[orow * D + d] = L > 0.f ? O : 0.f;
-          if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
+      } else {
+        for (int x = tid; x < nr * D; x += NT) {  // many partials: one output at a time
+          const int r = x / D, d = x - r * D;
+          float M = -INFINITY;
+          for (int j = 0; j < np; ++j) M = fmaxf(M, __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r));
+          float L = 0.f, O = 0.f;
+          if (M != -INFINITY)
+            for (int j = 0; j < np; ++j) {
+              const size_t pr = p0 + (size_t)item_of(j) * stride + r;
+              const float f = exp2f(__ldcg(a.ws_m + pr) - M);
+              L = fmaf(__ldcg(a.ws_l + pr), f, L);
+              O = fmaf(__ldcg(a.ws_o + pr * D + d), f, O);
+            }
+          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
+          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
+          if (a.mode == 0) {
+            const float v = L > 0.f ? O / L : 0.f;
+            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
+            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
+          } else {
+            a.po[orow * D + d] = L > 0.f ? O : 0.f;
+            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
+          }
         }
       }
     }
@@ -984,6 +1083,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
       s_abort = 1;
       if (lane == 0) atomicExch(&g_attn_status, 1);
     }
+    if (k == 0) OC_STAMP(2);
     const int slot = item / a.chunks;
     const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
     const bool valid = !s_abort && blk >= 0 && blk < a.S / a.bs;
@@ -1058,6 +1158,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     }
   }
   if (cur_b >= 0) flush_run();
+  OC_STAMP(3);
 }
 
 template <int D>
@@ -1558,3 +1659,9 @@ extern "C" int oc_indirect_attention_noalloc(const void* q, const void* k, const
                            max_blocks, out, out_dtype, nullptr, nullptr, nullptr, scratch, oc::kNoAllocScratchBytes,
                            0, reinterpret_cast<cudaStream_t>(stream));
 }
+
+#ifdef OC_TIMING
+extern "C" int oc_probe_read_stamps(unsigned long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, oc::g_tstamp, sizeof(unsigned long long) * 4 * n);
+}
+#endif
