@@ -773,7 +773,7 @@ constexpr int kMStages = 3;
 constexpr int kMStageBytes = 32768;  // K + V of one item
 
 #ifdef OC_TIMING
-__device__ unsigned long long g_tstamp[4096][4];
+__device__ unsigned long long g_tstamp[4096][8];
 #define OC_STAMP(i) do { if (threadIdx.x == 0 && blockIdx.x < 4096) g_tstamp[blockIdx.x][i] = globaltimer_ns(); } while (0)
 #else
 #define OC_STAMP(i) do {} while (0)
@@ -833,6 +833,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   constexpr int kMaxParts = 160;
   __shared__ float s_pm[kMaxParts][RT], s_pl[kMaxParts][RT];
   __shared__ float s_rowM[RT], s_rowL[RT];
+  __shared__ __align__(8) uint64_t s_mbar_merge;
 
   OC_STAMP(0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -897,7 +898,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
 
   // End of a run (CTA-uniform): combine the warp states into one partial,
   // publish it, and merge the segment if this is its last partial.
-  auto flush_run = [&]() {
+  auto flush_run = [&](bool final_run) {
     const int r0 = cur_rt * RT;
     const int nr = min(RT, a.R - r0);
 #pragma unroll
@@ -946,10 +947,69 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
       s_last = atomicAdd(&a.ctr[seg], 1) == s_np - 1;
     }
     __syncthreads();
+    if (s_last) OC_STAMP(5);
     if (s_last) {
       __threadfence();
       const int np = s_np, c1 = s_c1, s0 = s_s0;
       auto item_of = [&](int j) { return j == 0 ? 0 : (c1 + j - 1) * per - s0; };
+      // Final run: the stage ring is idle, so every partial's output block
+      // (nr * D floats, contiguous) arrives in one burst of bulk copies.
+      const uint32_t blk_bytes = (uint32_t)(nr * D * 4);
+      if (final_run && np <= kMaxParts && (size_t)np * blk_bytes <= (size_t)kMStages * kMStageBytes) {
+        float* sbuf = reinterpret_cast<float*>(smem);
+        if (tid == 0) {
+          // the ring was last read through the generic proxy, the partials were
+          // written through it by other CTAs: order both before the bulk copies
+          asm volatile("fence.proxy.async.shared::cta;\n\tfence.proxy.async.global;" ::: "memory");
+          mbar_init(&s_mbar_merge, 1);
+          fence_mbar_init();
+          mbar_expect_tx(&s_mbar_merge, (uint32_t)np * blk_bytes);
+          for (int j = 0; j < np; ++j)
+            bulk_load(sbuf + (size_t)j * nr * D, a.ws_o + (p0 + (size_t)item_of(j) * stride) * D, blk_bytes, &s_mbar_merge);
+        }
+        for (int idx = tid; idx < np * nr; idx += NT) {
+          const int j = idx / nr, r = idx - j * nr;
+          const size_t pr = p0 + (size_t)item_of(j) * stride + r;
+          s_pm[j][r] = __ldcg(a.ws_m + pr);
+          s_pl[j][r] = __ldcg(a.ws_l + pr);
+        }
+        __syncthreads();
+        if (tid < nr) {
+          float M = -INFINITY;
+          for (int j = 0; j < np; ++j) M = fmaxf(M, s_pm[j][tid]);
+          float L = 0.f;
+          if (M != -INFINITY)
+            for (int j = 0; j < np; ++j) L = fmaf(s_pl[j][tid], exp2f(s_pm[j][tid] - M), L);
+          s_rowM[tid] = M;
+          s_rowL[tid] = L;
+        }
+        __syncthreads();
+        for (int idx = tid; idx < np * nr; idx += NT) {
+          const int j = idx / nr, r = idx - j * nr;
+          s_pm[j][r] = s_rowM[r] == -INFINITY ? 0.f : exp2f(s_pm[j][r] - s_rowM[r]);
+        }
+        const bool ok = mbar_wait(&s_mbar_merge, 0);
+        if (!ok && tid == 0) atomicExch(&g_attn_status, 1);
+        __syncthreads();
+        for (int x = tid; x < nr * D; x += NT) {
+          const int r = x / D, d = x - r * D;
+          float O = 0.f;
+          for (int j = 0; j < np; ++j) O = fmaf(s_pm[j][r], sbuf[(size_t)j * nr * D + x], O);
+          const float M = s_rowM[r], L = s_rowL[r];
+          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
+          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
+          if (a.mode == 0) {
+            const float v = (ok && L > 0.f) ? O / L : 0.f;
+            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
+            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
+          } else {
+            a.po[orow * D + d] = (ok && L > 0.f) ? O : 0.f;
+            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
+          }
+        }
+        __syncthreads();
+        return;
+      }
       const bool staged = np <= kMaxParts;
       if (staged) {
         // maxima and sums of all partials into shared memory, in parallel
@@ -1042,6 +1102,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         }
       }
     }
+    if (s_last) OC_STAMP(6);
     __syncthreads();
   };
 
@@ -1049,7 +1110,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     const int b = cur.b, h = cur.h, rt = cur.rt, item = cur.item;
     cur.next(a);
     const bool new_run = b != cur_b || h != cur_h || rt != cur_rt;
-    if (new_run && cur_b >= 0) flush_run();
+    if (new_run && cur_b >= 0) flush_run(false);
     if (new_run) {
       cur_b = b; cur_h = h; cur_rt = rt; run_first = item; run_first_global = beg + k;
       const int r0 = rt * RT;
@@ -1157,7 +1218,8 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
       mma_bf16_16816(o[2 * np2 + 1], pa, vb[np2][2], vb[np2][3]);
     }
   }
-  if (cur_b >= 0) flush_run();
+  OC_STAMP(4);
+  if (cur_b >= 0) flush_run(true);
   OC_STAMP(3);
 }
 
@@ -1430,9 +1492,8 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.chunks = bs / a.chunk;
   a.max_items = max_blocks * a.chunks;
   a.scale_log2 = kLog2e / sqrtf((float)D);
-  // Stream kernels: persistent grid (two CTAs per SM for the tensor-core one,
-  // whose 115 KB of shared memory and 224 registers per thread allow it).
-  a.run_grid = tma ? device_sm_count() * (mma ? 2 : 1) : 0;
+  // Stream kernels: persistent grid, one CTA per SM.
+  a.run_grid = tma ? device_sm_count() : 0;
   a.rt_tile = rt;
   const size_t parts = (size_t)B * a.max_items * Hkv * a.R;
   char* w = static_cast<char*>(ws);
@@ -1662,6 +1723,6 @@ extern "C" int oc_indirect_attention_noalloc(const void* q, const void* k, const
 
 #ifdef OC_TIMING
 extern "C" int oc_probe_read_stamps(unsigned long long* host, int n) {
-  return (int)cudaMemcpyFromSymbol(host, oc::g_tstamp, sizeof(unsigned long long) * 4 * n);
+  return (int)cudaMemcpyFromSymbol(host, oc::g_tstamp, sizeof(unsigned long long) * 8 * n);
 }
 #endif

@@ -74,6 +74,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (no multicast); both addresses 16-byte
+// aligned, bytes a multiple of 16; completion as transaction bytes on bar.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Host: encode a row-major 2-D tensor map (cols innermost).  Returns 0 or a
 // CUresult code.
 // swizzle128: 16-byte chunk c of box row r lands at chunk c ^ (r % 8) within
