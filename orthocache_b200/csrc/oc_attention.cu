@@ -769,7 +769,7 @@ int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
 // arrive as 128-byte swizzled boxes of 64 channels, so every ldmatrix of a
 // stage is free of bank conflicts.
 // ---------------------------------------------------------------------------
-constexpr int kMStages = 3;
+constexpr int kMStages = 6;
 constexpr int kMStageBytes = 32768;  // K + V of one item
 
 #ifdef OC_TIMING
