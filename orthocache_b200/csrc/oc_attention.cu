@@ -769,7 +769,7 @@ int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
 // arrive as 128-byte swizzled boxes of 64 channels, so every ldmatrix of a
 // stage is free of bank conflicts.
 // ---------------------------------------------------------------------------
-constexpr int kMStages = 6;
+constexpr int kMStages = 3;
 constexpr int kMStageBytes = 32768;  // K + V of one item
 
 #ifdef OC_TIMING
@@ -813,7 +813,7 @@ __device__ __forceinline__ uint32_t swz(int t, int c8) {
 }
 
 template <int D, int RT>
-__global__ void __launch_bounds__(32 * (8192 / D) / 16, 1)
+__global__ void __launch_bounds__(32 * (8192 / D) / 16, 2)
 attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
   constexpr int CH = 8192 / D;           // tokens per item
   constexpr int NW = CH / 16;            // warps: 16 tokens each
@@ -1492,8 +1492,9 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.chunks = bs / a.chunk;
   a.max_items = max_blocks * a.chunks;
   a.scale_log2 = kLog2e / sqrtf((float)D);
-  // Stream kernels: persistent grid, one CTA per SM.
-  a.run_grid = tma ? device_sm_count() : 0;
+  // Stream kernels: persistent grid; two CTAs per SM for the tensor-core one
+  // (its 4 warps per CTA leave the SM latency-bound otherwise).
+  a.run_grid = tma ? device_sm_count() * (mma ? 2 : 1) : 0;
   a.rt_tile = rt;
   const size_t parts = (size_t)B * a.max_items * Hkv * a.R;
   char* w = static_cast<char*>(ws);
