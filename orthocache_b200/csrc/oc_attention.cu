@@ -53,7 +53,6 @@ struct AttnArgs {
   float* ws_o;      // [B][max_items][Hkv][R][D]
   int run_grid;     // > 0: stream kernel on this many CTAs (partials only at run starts)
   int rt_tile;      // query rows per row tile
-  int* ctr;         // stream kernel: per-segment arrival counters (zeroed per call)
   void* out;        // final output (mode 0), bf16 if out_bf16
   int out_bf16;
   float *pm, *pl, *po;  // mode 1: (m, l, o) per output row
@@ -392,10 +391,6 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __shared__ volatile int s_abort;
   __shared__ float s_wm[kVWarps][RT], s_wl[kVWarps][RT];
   __shared__ float s_wo[kVWarps][RT][D];
-  __shared__ int s_np, s_c1, s_s0, s_last;
-  constexpr int kMaxParts = 160;  // partials of one segment staged in shared memory
-  __shared__ float s_pm[kMaxParts][RT], s_pl[kMaxParts][RT];
-  __shared__ float s_rowM[RT], s_rowL[RT];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int N = total_items(a);
@@ -428,31 +423,16 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       pre.next(a);
     }
   }
-  // (batch, head) lists with no retained block produce no partial: their
-  // output rows are written here (zeros; or max -inf, sum 0 for partials).
-  for (int bh = blockIdx.x; bh < a.B * a.Hkv; bh += gridDim.x) {
-    const int bb = bh / a.Hkv, hh = bh - bb * a.Hkv;
-    if (list_len(a, bb, hh) != 0) continue;
-    for (int x = tid; x < a.R * D; x += kVThreads) {
-      const int row = x / D, d = x - row * D, sq = row / a.G, g = row - sq * a.G;
-      const size_t orow = ((size_t)bb * a.Sq + sq) * a.Hq + (size_t)hh * a.G + g;
-      if (a.mode == 0) {
-        if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(0.f);
-        else reinterpret_cast<float*>(a.out)[orow * D + d] = 0.f;
-      } else {
-        a.po[orow * D + d] = 0.f;
-        if (d == 0) { a.pm[orow] = -INFINITY; a.pl[orow] = 0.f; }
-      }
-    }
-  }
   __syncthreads();
+  // The merge kernel may now be scheduled (it waits for this grid to finish).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // Per-warp online-softmax state of the current run.
   float m_run[RT];
   f32x2 o2[RT][DPL / 2];  // output channels in packed pairs
   float l_acc = 0.f;  // this lane's (token, row) share of l
   float qv[RT][DPL];
-  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0, run_first_global = 0;
+  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0;
   // Position of the item being consumed, and of the item kVStages ahead
   // (the one a stage released now is refilled with).
   ItemIter cur, ahead;
@@ -462,9 +442,9 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   const int my_v = lane >> SH;            // value index this lane ends up holding
   const int my_t = my_v / RT, my_r = my_v % RT;
 
-  // End of a run (CTA-uniform): combine the 16 warp states into one partial,
-  // publish it, and if it is the last partial of its (batch, head, row tile)
-  // segment, merge the segment's partials into the final output.
+  // End of a run (CTA-uniform): combine the 16 warp states into one partial
+  // and publish it at the run's first item; the merge kernel combines the
+  // runs of each (batch, head, row tile) segment.
   auto flush_run = [&]() {
     const int r0 = cur_rt * RT;
     const int nr = min(RT, a.R - r0);
@@ -499,116 +479,6 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       a.ws_o[pr * D + d] = O;
       if (d == 0) { a.ws_m[pr] = M; a.ws_l[pr] = L; }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      // partials of this segment: its first item, and every CTA boundary inside it
-      const int n = list_len(a, cur_b, cur_h) * a.chunks;
-      const int s0 = run_first_global - run_first;
-      const int c1 = s0 / per + 1, lastc = (s0 + n - 1) / per;
-      s_np = 1 + max(0, lastc - c1 + 1);
-      s_c1 = c1;
-      s_s0 = s0;
-      const int seg = (cur_b * a.Hkv + cur_h) * a.n_rt + cur_rt;
-      s_last = atomicAdd(&a.ctr[seg], 1) == s_np - 1;
-    }
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      const int np = s_np, c1 = s_c1, s0 = s_s0;
-      auto item_of = [&](int j) { return j == 0 ? 0 : (c1 + j - 1) * per - s0; };
-      const bool staged = np <= kMaxParts;
-      if (staged) {
-        // maxima and sums of all partials into shared memory, in parallel
-        for (int idx = tid; idx < np * nr; idx += kVThreads) {
-          const int j = idx / nr, r = idx - j * nr;
-          const size_t pr = p0 + (size_t)item_of(j) * stride + r;
-          s_pm[j][r] = __ldcg(a.ws_m + pr);
-          s_pl[j][r] = __ldcg(a.ws_l + pr);
-        }
-        __syncthreads();
-        if (tid < nr) {  // per-row max and sum
-          float M = -INFINITY;
-          for (int j = 0; j < np; ++j) M = fmaxf(M, s_pm[j][tid]);
-          float L = 0.f;
-          if (M != -INFINITY)
-            for (int j = 0; j < np; ++j) L = fmaf(s_pl[j][tid], exp2f(s_pm[j][tid] - M), L);
-          s_rowM[tid] = M;
-          s_rowL[tid] = L;
-        }
-        __syncthreads();
-        for (int idx = tid; idx < np * nr; idx += kVThreads) {  // weights, in place of the maxima
-          const int j = idx / nr, r = idx - j * nr;
-          s_pm[j][r] = s_rowM[r] == -INFINITY ? 0.f : exp2f(s_pm[j][r] - s_rowM[r]);
-        }
-        __syncthreads();
-        // every output this thread owns, with all loads of a batch of partials in flight
-        constexpr int XPT = (RT * D + kVThreads - 1) / kVThreads;
-        float acc[XPT];
-#pragma unroll
-        for (int i = 0; i < XPT; ++i) acc[i] = 0.f;
-        for (int j0 = 0; j0 < np; j0 += 4) {
-          float ov[4][XPT];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int i = 0; i < XPT; ++i) {
-              const int x = tid + i * kVThreads;
-              const int r = x / D, d = x - r * D;
-              ov[u][i] = (j0 + u < np && x < nr * D)
-                             ? __ldcg(a.ws_o + (p0 + (size_t)item_of(j0 + u) * stride + r) * D + d) : 0.f;
-            }
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int i = 0; i < XPT; ++i) {
-              const int x = tid + i * kVThreads;
-              if (j0 + u < np && x < nr * D) acc[i] = fmaf(s_pm[j0 + u][x / D], ov[u][i], acc[i]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < XPT; ++i) {
-          const int x = tid + i * kVThreads;
-          if (x >= nr * D) continue;
-          const int r = x / D, d = x - r * D;
-          const float M = s_rowM[r], L = s_rowL[r], O = acc[i];
-          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
-          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
-          if (a.mode == 0) {
-            const float v = L > 0.f ? O / L : 0.f;
-            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
-            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
-          } else {
-            a.po[orow * D + d] = L > 0.f ? O : 0.f;
-            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
-          }
-        }
-      } else {
-        for (int x = tid; x < nr * D; x += kVThreads) {  // many partials: one output at a time
-          const int r = x / D, d = x - r * D;
-          float M = -INFINITY;
-          for (int j = 0; j < np; ++j) M = fmaxf(M, __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r));
-          float L = 0.f, O = 0.f;
-          if (M != -INFINITY)
-            for (int j = 0; j < np; ++j) {
-              const size_t pr = p0 + (size_t)item_of(j) * stride + r;
-              const float f = exp2f(__ldcg(a.ws_m + pr) - M);
-              L = fmaf(__ldcg(a.ws_l + pr), f, L);
-              O = fmaf(__ldcg(a.ws_o + pr * D + d), f, O);
-            }
-          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
-          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
-          if (a.mode == 0) {
-            const float v = L > 0.f ? O / L : 0.f;
-            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
-            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
-          } else {
-            a.po[orow * D + d] = L > 0.f ? O : 0.f;
-            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
-          }
-        }
-      }
-    }
     __syncthreads();
   };
 
@@ -618,7 +488,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     const bool new_run = b != cur_b || h != cur_h || rt != cur_rt;
     if (new_run && cur_b >= 0) flush_run();
     if (new_run) {
-      cur_b = b; cur_h = h; cur_rt = rt; run_first = item; run_first_global = beg + k;
+      cur_b = b; cur_h = h; cur_rt = rt; run_first = item;
       const int r0 = rt * RT;
       const int nr = min(RT, a.R - r0);
       const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
@@ -761,7 +631,7 @@ int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
 
 // ---------------------------------------------------------------------------
 // bfloat16 path on tensor cores (D = 64 or 128).  Same item order, contiguous
-// per-CTA ranges, TMA stage ring and in-place segment merge as the CUDA-core
+// per-CTA ranges, TMA stage ring and run partials as the CUDA-core
 // stream kernel above, but each warp owns 16 tokens of every item and does
 // both products with warp-level MMA (m16n8k16, bf16 inputs, fp32
 // accumulation): S = Q K^T with the query rows of the tile as M (padded to
@@ -829,11 +699,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   __shared__ volatile int s_abort;
   __shared__ float s_wm[NW][RT], s_wl[NW][RT];
   __shared__ float s_wo[NW][RT][D];
-  __shared__ int s_np, s_c1, s_s0, s_last;
-  constexpr int kMaxParts = 160;
-  __shared__ float s_pm[kMaxParts][RT], s_pl[kMaxParts][RT];
-  __shared__ float s_rowM[RT], s_rowL[RT];
-  __shared__ __align__(8) uint64_t s_mbar_merge;
+
 
   OC_STAMP(0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -868,37 +734,24 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
       pre.next(a);
     }
   }
-  for (int bh = blockIdx.x; bh < a.B * a.Hkv; bh += gridDim.x) {  // lists with no retained block
-    const int bb = bh / a.Hkv, hh = bh - bb * a.Hkv;
-    if (list_len(a, bb, hh) != 0) continue;
-    for (int x = tid; x < a.R * D; x += NT) {
-      const int row = x / D, d = x - row * D, sq = row / a.G, gg = row - sq * a.G;
-      const size_t orow = ((size_t)bb * a.Sq + sq) * a.Hq + (size_t)hh * a.G + gg;
-      if (a.mode == 0) {
-        if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(0.f);
-        else reinterpret_cast<float*>(a.out)[orow * D + d] = 0.f;
-      } else {
-        a.po[orow * D + d] = 0.f;
-        if (d == 0) { a.pm[orow] = -INFINITY; a.pl[orow] = 0.f; }
-      }
-    }
-  }
   __syncthreads();
+  // The merge kernel may now be scheduled (it waits for this grid to finish).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // per-warp online-softmax state of the run: rows g and g + 8 of the tile
   float m_run[2], l_acc[2];
   float o[NO][4];
   uint32_t qa[KS][4];
-  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0, run_first_global = 0;
+  int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0;
   ItemIter cur, ahead;
   cur.start(a, beg, N);
   ahead.start(a, beg, N);
   for (int i = 0; i < kMStages; ++i) ahead.next(a);
   OC_STAMP(1);
 
-  // End of a run (CTA-uniform): combine the warp states into one partial,
-  // publish it, and merge the segment if this is its last partial.
-  auto flush_run = [&](bool final_run) {
+  // End of a run (CTA-uniform): combine the warp states into one partial and
+  // publish it at the run's first item.
+  auto flush_run = [&]() {
     const int r0 = cur_rt * RT;
     const int nr = min(RT, a.R - r0);
 #pragma unroll
@@ -934,175 +787,6 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
       a.ws_o[pr * D + d] = O;
       if (d == 0) { a.ws_m[pr] = M; a.ws_l[pr] = L; }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int n = list_len(a, cur_b, cur_h) * a.chunks;
-      const int s0 = run_first_global - run_first;
-      const int c1 = s0 / per + 1, lastc = (s0 + n - 1) / per;
-      s_np = 1 + max(0, lastc - c1 + 1);
-      s_c1 = c1;
-      s_s0 = s0;
-      const int seg = (cur_b * a.Hkv + cur_h) * a.n_rt + cur_rt;
-      s_last = atomicAdd(&a.ctr[seg], 1) == s_np - 1;
-    }
-    __syncthreads();
-    if (s_last) OC_STAMP(5);
-    if (s_last) {
-      __threadfence();
-      const int np = s_np, c1 = s_c1, s0 = s_s0;
-      auto item_of = [&](int j) { return j == 0 ? 0 : (c1 + j - 1) * per - s0; };
-      // Final run: the stage ring is idle, so every partial's output block
-      // (nr * D floats, contiguous) arrives in one burst of bulk copies.
-      const uint32_t blk_bytes = (uint32_t)(nr * D * 4);
-      if (final_run && np <= kMaxParts && (size_t)np * blk_bytes <= (size_t)kMStages * kMStageBytes) {
-        float* sbuf = reinterpret_cast<float*>(smem);
-        if (tid == 0) {
-          // the ring was last read through the generic proxy, the partials were
-          // written through it by other CTAs: order both before the bulk copies
-          asm volatile("fence.proxy.async.shared::cta;\n\tfence.proxy.async.global;" ::: "memory");
-          mbar_init(&s_mbar_merge, 1);
-          fence_mbar_init();
-          mbar_expect_tx(&s_mbar_merge, (uint32_t)np * blk_bytes);
-          for (int j = 0; j < np; ++j)
-            bulk_load(sbuf + (size_t)j * nr * D, a.ws_o + (p0 + (size_t)item_of(j) * stride) * D, blk_bytes, &s_mbar_merge);
-        }
-        for (int idx = tid; idx < np * nr; idx += NT) {
-          const int j = idx / nr, r = idx - j * nr;
-          const size_t pr = p0 + (size_t)item_of(j) * stride + r;
-          s_pm[j][r] = __ldcg(a.ws_m + pr);
-          s_pl[j][r] = __ldcg(a.ws_l + pr);
-        }
-        __syncthreads();
-        if (tid < nr) {
-          float M = -INFINITY;
-          for (int j = 0; j < np; ++j) M = fmaxf(M, s_pm[j][tid]);
-          float L = 0.f;
-          if (M != -INFINITY)
-            for (int j = 0; j < np; ++j) L = fmaf(s_pl[j][tid], exp2f(s_pm[j][tid] - M), L);
-          s_rowM[tid] = M;
-          s_rowL[tid] = L;
-        }
-        __syncthreads();
-        for (int idx = tid; idx < np * nr; idx += NT) {
-          const int j = idx / nr, r = idx - j * nr;
-          s_pm[j][r] = s_rowM[r] == -INFINITY ? 0.f : exp2f(s_pm[j][r] - s_rowM[r]);
-        }
-        const bool ok = mbar_wait(&s_mbar_merge, 0);
-        if (!ok && tid == 0) atomicExch(&g_attn_status, 1);
-        __syncthreads();
-        for (int x = tid; x < nr * D; x += NT) {
-          const int r = x / D, d = x - r * D;
-          float O = 0.f;
-          for (int j = 0; j < np; ++j) O = fmaf(s_pm[j][r], sbuf[(size_t)j * nr * D + x], O);
-          const float M = s_rowM[r], L = s_rowL[r];
-          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
-          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
-          if (a.mode == 0) {
-            const float v = (ok && L > 0.f) ? O / L : 0.f;
-            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
-            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
-          } else {
-            a.po[orow * D + d] = (ok && L > 0.f) ? O : 0.f;
-            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
-          }
-        }
-        __syncthreads();
-        return;
-      }
-      const bool staged = np <= kMaxParts;
-      if (staged) {
-        // maxima and sums of all partials into shared memory, in parallel
-        for (int idx = tid; idx < np * nr; idx += NT) {
-          const int j = idx / nr, r = idx - j * nr;
-          const size_t pr = p0 + (size_t)item_of(j) * stride + r;
-          s_pm[j][r] = __ldcg(a.ws_m + pr);
-          s_pl[j][r] = __ldcg(a.ws_l + pr);
-        }
-        __syncthreads();
-        if (tid < nr) {  // per-row max and sum
-          float M = -INFINITY;
-          for (int j = 0; j < np; ++j) M = fmaxf(M, s_pm[j][tid]);
-          float L = 0.f;
-          if (M != -INFINITY)
-            for (int j = 0; j < np; ++j) L = fmaf(s_pl[j][tid], exp2f(s_pm[j][tid] - M), L);
-          s_rowM[tid] = M;
-          s_rowL[tid] = L;
-        }
-        __syncthreads();
-        for (int idx = tid; idx < np * nr; idx += NT) {  // weights, in place of the maxima
-          const int j = idx / nr, r = idx - j * nr;
-          s_pm[j][r] = s_rowM[r] == -INFINITY ? 0.f : exp2f(s_pm[j][r] - s_rowM[r]);
-        }
-        __syncthreads();
-        // every output this thread owns, with all loads of a batch of partials in flight
-        constexpr int XPT = (RT * D + NT - 1) / NT;
-        float acc[XPT];
-#pragma unroll
-        for (int i = 0; i < XPT; ++i) acc[i] = 0.f;
-        for (int j0 = 0; j0 < np; j0 += 4) {
-          float ov[4][XPT];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int i = 0; i < XPT; ++i) {
-              const int x = tid + i * NT;
-              const int r = x / D, d = x - r * D;
-              ov[u][i] = (j0 + u < np && x < nr * D)
-                             ? __ldcg(a.ws_o + (p0 + (size_t)item_of(j0 + u) * stride + r) * D + d) : 0.f;
-            }
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int i = 0; i < XPT; ++i) {
-              const int x = tid + i * NT;
-              if (j0 + u < np && x < nr * D) acc[i] = fmaf(s_pm[j0 + u][x / D], ov[u][i], acc[i]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < XPT; ++i) {
-          const int x = tid + i * NT;
-          if (x >= nr * D) continue;
-          const int r = x / D, d = x - r * D;
-          const float M = s_rowM[r], L = s_rowL[r], O = acc[i];
-          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
-          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
-          if (a.mode == 0) {
-            const float v = L > 0.f ? O / L : 0.f;
-            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
-            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
-          } else {
-            a.po[orow * D + d] = L > 0.f ? O : 0.f;
-            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
-          }
-        }
-      } else {
-        for (int x = tid; x < nr * D; x += NT) {  // many partials: one output at a time
-          const int r = x / D, d = x - r * D;
-          float M = -INFINITY;
-          for (int j = 0; j < np; ++j) M = fmaxf(M, __ldcg(a.ws_m + p0 + (size_t)item_of(j) * stride + r));
-          float L = 0.f, O = 0.f;
-          if (M != -INFINITY)
-            for (int j = 0; j < np; ++j) {
-              const size_t pr = p0 + (size_t)item_of(j) * stride + r;
-              const float f = exp2f(__ldcg(a.ws_m + pr) - M);
-              L = fmaf(__ldcg(a.ws_l + pr), f, L);
-              O = fmaf(__ldcg(a.ws_o + pr * D + d), f, O);
-            }
-          const int row = r0 + r, sq = row / a.G, gg = row - sq * a.G;
-          const size_t orow = ((size_t)cur_b * a.Sq + sq) * a.Hq + (size_t)cur_h * a.G + gg;
-          if (a.mode == 0) {
-            const float v = L > 0.f ? O / L : 0.f;
-            if (a.out_bf16) reinterpret_cast<__nv_bfloat16*>(a.out)[orow * D + d] = __float2bfloat16_rn(v);
-            else reinterpret_cast<float*>(a.out)[orow * D + d] = v;
-          } else {
-            a.po[orow * D + d] = L > 0.f ? O : 0.f;
-            if (d == 0) { a.pm[orow] = M; a.pl[orow] = L; }
-          }
-        }
-      }
-    }
-    if (s_last) OC_STAMP(6);
     __syncthreads();
   };
 
@@ -1110,9 +794,9 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     const int b = cur.b, h = cur.h, rt = cur.rt, item = cur.item;
     cur.next(a);
     const bool new_run = b != cur_b || h != cur_h || rt != cur_rt;
-    if (new_run && cur_b >= 0) flush_run(false);
+    if (new_run && cur_b >= 0) flush_run();
     if (new_run) {
-      cur_b = b; cur_h = h; cur_rt = rt; run_first = item; run_first_global = beg + k;
+      cur_b = b; cur_h = h; cur_rt = rt; run_first = item;
       const int r0 = rt * RT;
       const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + (size_t)b * a.Sq * a.Hq * D;
       // A fragments of Q (rows g and g + 8 of the tile; rows past the tile are zero)
@@ -1219,7 +903,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     }
   }
   OC_STAMP(4);
-  if (cur_b >= 0) flush_run(true);
+  if (cur_b >= 0) flush_run();
   OC_STAMP(3);
 }
 
@@ -1284,6 +968,9 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
     np = 1 + max(0, last - c1 + 1);
   }
   auto pos = [&](int j) -> int { return (a.run_grid > 0 && j > 0) ? (c1 + j - 1) * per - s0 : j; };
+  // Launched as a programmatic dependent of the stream kernel: wait for it to
+  // finish (and its partials to be visible).  A no-op for a plain launch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // M = max over the partials (in parallel)
   float M = -INFINITY;
@@ -1413,8 +1100,7 @@ size_t attn_ws_bytes(int B, int Sq, int Hq, int Hkv, int D, int bs, int max_bloc
   const size_t R = (size_t)Sq * G;
   const size_t items = (size_t)max_blocks * (bs / chunk_for(bs, D));
   const size_t parts = (size_t)B * items * Hkv * R;
-  const size_t segs = (size_t)B * Hkv * R;  // row-tile segments (upper bound) for the arrival counters
-  return 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float)) + align256(segs * sizeof(int));
+  return 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float));
 }
 
 int validate_attn(const void* q, const void* k, const void* v, int dtype, const int32_t* idx,
@@ -1501,7 +1187,6 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.ws_m = reinterpret_cast<float*>(w);
   a.ws_l = reinterpret_cast<float*>(w + align256(parts * sizeof(float)));
   a.ws_o = reinterpret_cast<float*>(w + 2 * align256(parts * sizeof(float)));
-  a.ctr = reinterpret_cast<int*>(w + 2 * align256(parts * sizeof(float)) + align256(parts * D * sizeof(float)));
   a.out = out;
   a.out_bf16 = out_dtype == OC_BF16;
   a.pm = pm; a.pl = pl; a.po = po;
@@ -1509,29 +1194,42 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   const int64_t rows = (int64_t)B * Hkv * a.R;
   OC_REQUIRE(rows < (1ll << 31), OC_ERR_CAPACITY, "attention: too many rows");
 
-  if (tma && max_blocks > 0) {
-    // The stream kernel merges in place: it needs its arrival counters at zero.
-    const size_t segs = (size_t)B * Hkv * a.n_rt;
-    cudaError_t e = cudaMemsetAsync(a.ctr, 0, segs * sizeof(int), st);
-    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "attention: %s", cudaGetErrorString(e));
-    if (mma) return D == 64 ? launch_attn_mma<64>(a, rt, st) : launch_attn_mma<128>(a, rt, st);
-    return launch_attn_stream<256>(a, rt, st);
-  }
-  if (max_blocks > 0) {
+  const bool stream_path = tma && max_blocks > 0;
+  if (stream_path) {
+    rc = mma ? (D == 64 ? launch_attn_mma<64>(a, rt, st) : launch_attn_mma<128>(a, rt, st))
+             : launch_attn_stream<256>(a, rt, st);
+    if (rc) return rc;
+  } else if (max_blocks > 0) {
     const int grid = device_sm_count() * 2;
     rc = dtype == OC_F32 ? launch_partials<float>(a, rt, grid, st)
                            : launch_partials<__nv_bfloat16>(a, rt, grid, st);
     if (rc) return rc;
   }
+  // After a stream kernel the merge is a programmatic dependent launch: its
+  // CTAs become resident while the stream kernel drains and wait for it with
+  // griddepcontrol.wait before reading the run partials.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)rows);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = stream_path ? 1 : 0;
+  cudaError_t e;
   if (mode == 0) {
     if (out_dtype == OC_F32)
-      attn_merge_kernel<float><<<(unsigned)rows, 256, 0, st>>>(a, (float*)out, nullptr, nullptr, nullptr, 0);
+      e = cudaLaunchKernelEx(&cfg, attn_merge_kernel<float>, a, (float*)out, (float*)nullptr, (float*)nullptr,
+                             (float*)nullptr, 0);
     else
-      attn_merge_kernel<__nv_bfloat16><<<(unsigned)rows, 256, 0, st>>>(a, (__nv_bfloat16*)out, nullptr,
-                                                                        nullptr, nullptr, 0);
+      e = cudaLaunchKernelEx(&cfg, attn_merge_kernel<__nv_bfloat16>, a, (__nv_bfloat16*)out, (float*)nullptr,
+                             (float*)nullptr, (float*)nullptr, 0);
   } else {
-    attn_merge_kernel<float><<<(unsigned)rows, 256, 0, st>>>(a, nullptr, pm, pl, po, 1);
+    e = cudaLaunchKernelEx(&cfg, attn_merge_kernel<float>, a, (float*)nullptr, pm, pl, po, 1);
   }
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "attn_merge_kernel: %s", cudaGetErrorString(e));
   return check_launch("attn_merge_kernel");
 }
 
