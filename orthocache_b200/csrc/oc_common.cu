@@ -98,6 +98,20 @@ int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, in
   return (int)r;
 }
 
+int encode_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t dims[4],
+                  const uint64_t strides[3], const uint32_t box[4], bool swizzle128) {
+  auto fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t s[3] = {strides[0], strides[1], strides[2]};
+  cuuint32_t b[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, dt, 4, const_cast<void*>(base), d, s, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
 }  // namespace oc
 
 extern "C" int oc_device_status(int reset) {

@@ -299,10 +299,20 @@ score_partial_kernel(ScoreArgs a) {
 // Persistent grid, one CTA per SM.  The unit of work is a slab of 512 tokens
 // x 64 channels of one (batch, block, kv head) tile (64 KB); a tile of D
 // channels is D / 64 consecutive slabs.  Thread 0 keeps kStages slabs in
-// flight with 2-D tensor loads (two 256-row boxes per slab) into a ring of
-// shared-memory stages, each completed on its own mbarrier.  The 256 threads
-// transform a slab straight out of shared memory (thread = 8 channels x 2
-// inner offsets), then the stage is refilled with the slab kStages ahead.
+// flight with 4-D tensor loads (one box per half of the inner offsets) into
+// a ring of shared-memory stages, each completed on its own mbarrier.
+//
+// With token i = 64 i_hi + i_lo, the natural-order transform factors as
+// H512 = H8 (x) H64, and coefficient group q (indices 64q .. 64q+63) holds
+// the 64-point transform of z_q(i_lo) = sum_i_hi H8[q][i_hi] x(64 i_hi + i_lo).
+// By Parseval its energy is (64 / 512) sum_i_lo z_q^2, except group 0, whose
+// coefficient 0 (the DC) is split off: (64 / 512) sum (z_0 - mean z_0)^2.
+// The 8-point transforms run on the tensor cores: each warp takes one
+// 8-channel chunk and 32 inner offsets of a slab, loads them as transposed
+// 8x8 matrices (ldmatrix) and multiplies by diag(H8, H8) (m16n8k16, fp32
+// accumulation; sums of eight bfloat16 values are exact in fp32), then
+// squares and sums the results in registers.  The stage is refilled with
+// the slab kStages ahead as soon as the last warp holds its operands.
 // Band sums and the DC column sums accumulate across the slabs of a tile; the
 // tile's epilogue (bound, ζ, keep) runs after its last slab.
 // ---------------------------------------------------------------------------
@@ -332,6 +342,25 @@ __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
   return d;
 }
 
+// ldmatrix of four transposed 8x8 bf16 matrices: lane (g, c) receives
+// M[2c][g], M[2c + 1][g] of each matrix (row addresses from lanes 8m .. 8m+7).
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+// D = diag(H8, H8) B + C on the tensor cores (m16n8k16, bf16 in, fp32 out):
+// A fragment a0 = a3 = hA, a1 = a2 = 0; C = (c0, c1) on both row halves.
+__device__ __forceinline__ void mma_h8(float (&d)[4], uint32_t hA, uint32_t b0, uint32_t b1, float c0, float c1) {
+  const uint32_t zero = 0;
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %11, %12, %13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(hA), "r"(zero), "r"(zero), "r"(hA), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c0), "f"(c1));
+}
+
 constexpr int kStages = 3;
 constexpr int kScoreThreads = 512;
 constexpr int kQCacheBytes = 16384;  // queries staged in shared memory up to this size  // 16 warps consume every stage in order
@@ -359,9 +388,13 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
-  const int cg = warp & 7;    // channels 8cg .. 8cg+7 of a slab (one 16-byte chunk)
-  const int hf = warp >> 3;   // inner offsets 32hf .. 32hf+31, one per lane
-  const int ilo = 32 * hf + lane;
+  const int ch = warp & 7;    // channels 8ch .. 8ch+7 of a slab (one 16-byte chunk)
+  const int hb = warp >> 3;   // inner offsets 32hb .. 32hb+31 (one box of the stage)
+  const int g = lane >> 2, c4 = lane & 3;  // MMA fragment coordinates
+  // A = diag(H8, H8) in bfloat16, H8[q][i] = (-1)^popcount(q & i):
+  // a0 = a3 = (H8[g][2c4], H8[g][2c4 + 1]), a1 = a2 = 0.
+  const uint32_t hA = ((__popc(g & (2 * c4)) & 1) ? 0xBF80u : 0x3F80u) |
+                      (((__popc(g & (2 * c4 + 1)) & 1) ? 0xBF80u : 0x3F80u) << 16);
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const int n_units = my_tiles * PARTS;
   // Queries staged in shared memory when they fit (decode), so the tile
@@ -379,8 +412,9 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     uint8_t* dst = smem + (size_t)(k % kStages) * kSlabB;
     uint64_t* bar = &full[k % kStages];
     mbar_expect_tx(bar, kSlabB);
-    tma_load_2d(dst, &kmap, bar, h * D + part * kSlabC, b * a.S + j * kBlock);
-    tma_load_2d(dst + kSlabB / 2, &kmap, bar, h * D + part * kSlabC, b * a.S + j * kBlock + kBlock / 2);
+    const int col = h * D + part * kSlabC, blk = b * a.nb + j;
+    tma_load_4d(dst, &kmap, bar, col, 0, 0, blk);                 // inner offsets 0..31
+    tma_load_4d(dst + kSlabB / 2, &kmap, bar, col, 0, 32, blk);   // inner offsets 32..63
   };
 
   if (tid == 0) {
@@ -397,17 +431,16 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   }
   __syncthreads();  // the only CTA-wide barrier
 
-  // 16-byte chunk cg of row r sits at chunk cg ^ (r % 8) (128-byte swizzle);
-  // rows ih*64 + ilo all have r % 8 == ilo % 8.
-  const int chunk_off = (cg ^ (ilo & 7)) * 16;
+  // Stage layout (4-D box: 64 channels x 8 i_hi x 32 i_lo, per half of the
+  // inner offsets): row = (i_lo % 32) * 8 + i_hi, 128 bytes, 16-byte chunk ch
+  // at chunk ch ^ i_hi (128-byte swizzle, row % 8 == i_hi).  The 8 rows of one
+  // 8x8 matrix (i_hi = 0..7 at one i_lo) are consecutive rows in distinct
+  // bank groups.  Lane (matrix lane / 8, row lane % 8) addresses:
+  const uint32_t lane_off = (uint32_t)hb * (kSlabB / 2) + (uint32_t)((lane >> 3) * 8 + (lane & 7)) * 128 +
+                            (uint32_t)((ch ^ (lane & 7)) << 4);
   for (int tile = 0; tile < my_tiles; ++tile) {
     const int tb = tile % NBUF;
-    float grp[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) grp[q] = 0.f;
-    f32x2 g2[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) g2[q] = pack2(0.f, 0.f);
+    float gacc = 0.f;  // this lane's share of the energy of coefficient group g
     for (int part = 0; part < PARTS; ++part) {
       const int k = tile * PARTS + part;
       const int stage = k % kStages;
@@ -419,11 +452,12 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
         if (lane == 0) atomicExch(&g_score_status, 1);
         return;
       }
-      const uint8_t* slab = smem + (size_t)stage * kSlabB;
-      uint4 raw[8];
+      // 32 transposed 8x8 matrices: B operands (k = i_hi, n = channel) of
+      // the inner offsets 32hb + 4s + m, m = 0..3.
+      const uint32_t sbase = smem_u32(smem + (size_t)stage * kSlabB) + lane_off;
+      uint32_t bm[8][4];
 #pragma unroll
-      for (int ih = 0; ih < 8; ++ih)
-        raw[ih] = *reinterpret_cast<const uint4*>(slab + (size_t)(ih * 64 + ilo) * 128 + chunk_off);
+      for (int s = 0; s < 8; ++s) ldsm_x4_trans(bm[s], sbase + s * 4096);
       // This warp is done with the stage; the last of the 16 warps refills it.
       __threadfence_block();
       __syncwarp();
@@ -436,57 +470,49 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
           }
         }
       }
-      // Butterflies on channel pairs with packed float32x2 arithmetic.
-      float y0[8];
+      // z = H8 x over i_hi for two inner offsets per MMA: rows 0-7 of D are
+      // groups q = 0..7 at the first offset, rows 8-15 at the second.  Lane
+      // (g, c4) receives group g at channels 2c4, 2c4 + 1 of its chunk.
+      // Row g = 0 is y0, whose per-channel mean is needed: it is accumulated
+      // relative to a pivot (its first value) as sum and sum of squares, so
+      // the centred sum loses nothing to cancellation.
+      float d[4];
+      mma_h8(d, hA, bm[0][0], bm[0][1], 0.f, 0.f);
+      const float p0 = g == 0 ? d[0] : 0.f, p1 = g == 0 ? d[1] : 0.f;
+      const f32x2 piv = pack2(p0, p1);
+      f32x2 s1 = sub2(pack2(d[2], d[3]), piv);
+      f32x2 s2 = fma2(s1, s1, pack2(0.f, 0.f));
+      {
+        f32x2 da = sub2(pack2(d[0], d[1]), piv);  // zero on row 0; z on the others
+        s2 = fma2(da, da, s2);
+      }
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        f32x2 x[8];
+      for (int s = 0; s < 8; ++s) {
 #pragma unroll
-        for (int ih = 0; ih < 8; ++ih) {
-          const uint32_t w = p == 0 ? raw[ih].x : p == 1 ? raw[ih].y : p == 2 ? raw[ih].z : raw[ih].w;
-          x[ih] = pack2(bf16lo(w), bf16hi(w));
+        for (int m = 0; m < 2; ++m) {
+          if (s == 0 && m == 0) continue;
+          mma_h8(d, hA, bm[s][2 * m], bm[s][2 * m + 1], -p0, -p1);  // D = z - pivot
+          const f32x2 da = pack2(d[0], d[1]), db = pack2(d[2], d[3]);
+          s1 = add2(s1, add2(da, db));
+          s2 = fma2(da, da, s2);
+          s2 = fma2(db, db, s2);
         }
-        const f32x2 a0 = add2(x[0], x[1]), a1 = sub2(x[0], x[1]);  // h = 64
-        const f32x2 a2 = add2(x[2], x[3]), a3 = sub2(x[2], x[3]);
-        const f32x2 a4 = add2(x[4], x[5]), a5 = sub2(x[4], x[5]);
-        const f32x2 a6 = add2(x[6], x[7]), a7 = sub2(x[6], x[7]);
-        const f32x2 b0 = add2(a0, a2), b2 = sub2(a0, a2), b1 = add2(a1, a3), b3 = sub2(a1, a3);  // h = 128
-        const f32x2 b4 = add2(a4, a6), b6 = sub2(a4, a6), b5 = add2(a5, a7), b7 = sub2(a5, a7);
-        const f32x2 c0 = add2(b0, b4), c4 = sub2(b0, b4), c1 = add2(b1, b5), c5 = sub2(b1, b5);  // h = 256
-        const f32x2 c2 = add2(b2, b6), c6 = sub2(b2, b6), c3 = add2(b3, b7), c7 = sub2(b3, b7);
-        unpack2(c0, y0[2 * p], y0[2 * p + 1]);
-        g2[1] = fma2(c1, c1, g2[1]);
-        g2[2] = fma2(c2, c2, g2[2]);
-        g2[3] = fma2(c3, c3, g2[3]);
-        g2[4] = fma2(c4, c4, g2[4]);
-        g2[5] = fma2(c5, c5, g2[5]);
-        g2[6] = fma2(c6, c6, g2[6]);
-        g2[7] = fma2(c7, c7, g2[7]);
       }
-      // Mean of y0 over this warp's 32 inner offsets, per channel; centred
-      // squares against it (the halves are combined exactly at the epilogue).
-#pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        float cs = y0[v];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-        const float mu = cs * (1.0f / 32.0f);
-        const float dl = y0[v] - mu;
-        grp[0] = fmaf(dl, dl, grp[0]);
-        if (lane == v) s_mu[tb][hf][part * kSlabC + cg * 8 + v] = mu;
+      float s1a, s1b, s2a, s2b;
+      unpack2(s1, s1a, s1b);
+      unpack2(s2, s2a, s2b);
+      if (g == 0) {
+        // 32 offsets: mean = pivot + S1 / 32, centred squares = S2 - S1^2 / 32
+        s_mu[tb][hb][part * kSlabC + ch * 8 + 2 * c4] = p0 + s1a * (1.0f / 32.0f);
+        s_mu[tb][hb][part * kSlabC + ch * 8 + 2 * c4 + 1] = p1 + s1b * (1.0f / 32.0f);
+        gacc += fmaf(-s1a * (1.0f / 32.0f), s1a, s2a) + fmaf(-s1b * (1.0f / 32.0f), s1b, s2b);
+      } else {
+        gacc += s2a + s2b;
       }
     }
-#pragma unroll
-    for (int q = 1; q < 8; ++q) {
-      float lo, hi;
-      unpack2(g2[q], lo, hi);
-      grp[q] = lo + hi;
-    }
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float sq = warp_sum(grp[q]);
-      if (lane == 0) s_grp[tb][warp][q] = sq;
-    }
+    gacc += __shfl_xor_sync(0xffffffffu, gacc, 1);
+    gacc += __shfl_xor_sync(0xffffffffu, gacc, 2);
+    if (c4 == 0) s_grp[tb][warp][g] = gacc;
     // The last warp to finish the tile runs its epilogue; nobody waits.  The
     // buffer tb is reused NBUF tiles later: a warp can only get there after
     // consuming a stage that the epilogue warp releases after finishing this
@@ -692,9 +718,14 @@ bool bands_partial_ok(const Bands& bd) {
 template <int D>
 int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   CUtensorMap map;
-  const uint64_t cols = (uint64_t)a.H * D;
-  const uint64_t rows = (uint64_t)ntiles / ((uint64_t)a.H * a.nb) * a.S;  // B * S
-  int rc = encode_map_2d(&map, a.keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, kSlabC, kBlock / 2, true);
+  // Keys viewed as (channel, i_hi, i_lo, block) with token = 512 block +
+  // 64 i_hi + i_lo, so that a box lands in shared memory i_hi fastest.
+  const uint64_t cols = (uint64_t)a.H * D, row_b = cols * 2;
+  const uint64_t blocks = (uint64_t)ntiles / a.H;  // B * nb
+  const uint64_t dims[4] = {cols, 8, 64, blocks};
+  const uint64_t strides[3] = {64 * row_b, row_b, (uint64_t)kBlock * row_b};
+  const uint32_t box[4] = {(uint32_t)kSlabC, 8, 32, 1};
+  int rc = encode_map_4d(&map, a.keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, box, true);
   if (rc) return set_error(OC_ERR_CUDA, "oc_score_blocks: tensor map encode failed (%d)", rc);
   const int smem = kStages * kSlabB + kQCacheBytes + 1024;
   cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -74,6 +74,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 4-D tiled bulk tensor load (no multicast); x innermost, same rules as 2-D.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w),
+        "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Untiled bulk copy global -> shared (no multicast); both addresses 16-byte
 // aligned, bytes a multiple of 16; completion as transaction bytes on bar.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -88,5 +99,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // each 1024-byte group of 8 rows (needs box_cols * elem_bytes == 128).
 int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
                   uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128 = false);
+
+// Host: encode a 4-D tensor map; dims[0] is innermost (contiguous), strides
+// are the byte strides of dims 1..3 in any order of size (a box is laid out
+// in shared memory dim 0 fastest, then 1, 2, 3).  Returns 0 or a CUresult.
+int encode_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t dims[4],
+                  const uint64_t strides[3], const uint32_t box[4], bool swizzle128);
 
 }  // namespace oc
