@@ -370,17 +370,17 @@ constexpr int kSlabB = kBlock * kSlabC * 2;                 // bytes per slab (b
 __device__ int g_score_status = 0;
 
 template <int D>
-__global__ void __launch_bounds__(kScoreThreads, 1)
+__global__ void __launch_bounds__(kScoreThreads + 32, 1)
 score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_tiles) {
   constexpr int PARTS = D / kSlabC;
   constexpr int kW = kScoreThreads / 32;  // 16 warps
-  constexpr int NBUF = 4;                 // tile buffers in flight (see the note at the epilogue)
+  constexpr int NBUF = 4;                 // tile buffers between the compute warps and the epilogue warp
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte swizzled stages must start on a 1024-byte boundary.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full[kStages];
   __shared__ int s_rel[kStages];             // warps done with a stage
-  __shared__ int s_cnt[NBUF];                // warps done with a tile
+  __shared__ __align__(8) uint64_t tfull[NBUF], tempty[NBUF];  // tile buffer hand-over
   __shared__ float s_grp[NBUF][kW][8];       // per-warp coefficient-group energies
   __shared__ float s_mu[NBUF][2][D];         // per-channel means of y0 over each half of the inner offsets
   __shared__ float s_dcw[NBUF][D];           // DC coefficients of the tile in buffer tb
@@ -419,7 +419,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
-    for (int i = 0; i < NBUF; ++i) s_cnt[i] = 0;
+    for (int i = 0; i < NBUF; ++i) { mbar_init(&tfull[i], kW); mbar_init(&tempty[i], 1); }
     fence_mbar_init();
     s_abort = 0;
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
@@ -427,9 +427,98 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   if (q_cached) {
     const uint4* src = reinterpret_cast<const uint4*>(a.q);
     uint4* dst = reinterpret_cast<uint4*>(s_q);
-    for (size_t i = tid; i < q_elems / 8; i += kScoreThreads) dst[i] = src[i];
+    for (size_t i = tid; i < q_elems / 8; i += blockDim.x) dst[i] = src[i];
   }
   __syncthreads();  // the only CTA-wide barrier
+
+  // Warp kW runs the tile epilogues (bound, zeta, keep) while the 16
+  // compute warps go on with the next tiles: tile buffer tb is handed over
+  // on tfull[tb] (16 arrivals) and handed back on tempty[tb].
+  if (warp == kW) {
+    for (int tile = 0; tile < my_tiles; ++tile) {
+      const int tb = tile % NBUF;
+      if (!mbar_wait(&tfull[tb], (tile / NBUF) & 1)) {
+        s_abort = 1;
+        if (lane == 0) atomicExch(&g_score_status, 1);
+        return;
+      }
+
+      const int t = blockIdx.x + tile * gridDim.x;
+      const int h = t % a.H;
+      const int j = (t / a.H) % a.nb;
+      const int b = t / (a.H * a.nb);
+      // group energies over the 16 warps; group 0 gets the exact between-half
+      // term: sum over 64 offsets of (y - mu)^2 = SS0 + SS1 + 16 (mu0 - mu1)^2.
+      float gv = 0.f;
+      if (lane < 8)
+        for (int w = 0; w < kW; ++w) gv += s_grp[tb][w][lane];
+      float between = 0.f, e_dc = 0.f;
+      for (int c = lane; c < D; c += 32) {
+        const float m0 = s_mu[tb][0][c], m1 = s_mu[tb][1][c];
+        const float dm = m0 - m1;
+        between = fmaf(16.0f * dm, dm, between);
+        const float dcv = (32.0f * (m0 + m1)) / kNorm;  // WHT coefficient 0
+        s_dcw[tb][c] = dcv;
+        e_dc = fmaf(dcv, dcv, e_dc);
+      }
+      between = warp_sum(between);
+      e_dc = warp_sum(e_dc);
+      __syncwarp();
+      float g[8];
+  #pragma unroll
+      for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, gv, q);
+      g[0] += between;
+  #pragma unroll
+      for (int q = 0; q < 8; ++q) g[q] *= 0.125f;  // (64 / 512) Parseval factor of the inner transform
+      float e_ac = 0.f;
+  #pragma unroll
+      for (int q = 0; q < 8; ++q) e_ac += g[q];
+      const float e_lo = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
+      const float e_mi = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
+      const float e_hi = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
+      const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
+      const float* dcp = s_dcw[tb];
+      if (a.dc)
+        for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
+      float bmax = -INFINITY;
+      if (a.q) {
+        const int rows = a.Sq * a.G;
+        const float sqrt_d = sqrtf((float)D);
+        const float resid_scale = sqrtf(e_ac);
+        const __nv_bfloat16* qb = (q_cached ? s_q : reinterpret_cast<const __nv_bfloat16*>(a.q)) +
+                                  (size_t)b * a.Sq * a.Hq * D;
+        for (int r = 0; r < rows; ++r) {
+          const int s = r / a.G, gq = r - s * a.G;
+          const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D;
+          float dot = 0.f, nrm = 0.f;
+  #pragma unroll
+          for (int c = lane; c < D; c += 32) {
+            const float qv = __bfloat162float(qr[c]);
+            dot = fmaf(qv, dcp[c] / kNorm, dot);  // block mean = DC / sqrt(512)
+            nrm = fmaf(qv, qv, nrm);
+          }
+          dot = warp_sum(dot);
+          nrm = warp_sum(nrm);
+          const float bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
+          if (a.bounds && lane == 0)
+            a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + gq] = bound;
+          bmax = fmaxf(bmax, bound);
+        }
+      }
+      if (lane == 0) {
+        const float z = e_hi / (e_lo + 1e-6f);
+        if (a.e_low) a.e_low[cell] = e_lo;
+        if (a.e_mid) a.e_mid[cell] = e_mi;
+        if (a.e_high) a.e_high[cell] = e_hi;
+        if (a.zeta) a.zeta[cell] = z;
+        if (a.q && a.bound_max) a.bound_max[cell] = bmax;
+        if (a.keep) a.keep[cell] = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[tb]);
+    }
+    return;
+  }
 
   // Stage layout (4-D box: 64 channels x 8 i_hi x 32 i_lo, per half of the
   // inner offsets): row = (i_lo % 32) * 8 + i_hi, 128 bytes, 16-byte chunk ch
@@ -440,6 +529,11 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
                             (uint32_t)((ch ^ (lane & 7)) << 4);
   for (int tile = 0; tile < my_tiles; ++tile) {
     const int tb = tile % NBUF;
+    if (tile >= NBUF && !mbar_wait(&tempty[tb], (tile / NBUF - 1) & 1)) {
+      s_abort = 1;
+      if (lane == 0) atomicExch(&g_score_status, 1);
+      return;
+    }
     float gacc = 0.f;  // this lane's share of the energy of coefficient group g
     for (int part = 0; part < PARTS; ++part) {
       const int k = tile * PARTS + part;
@@ -513,93 +607,10 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     gacc += __shfl_xor_sync(0xffffffffu, gacc, 1);
     gacc += __shfl_xor_sync(0xffffffffu, gacc, 2);
     if (c4 == 0) s_grp[tb][warp][g] = gacc;
-    // The last warp to finish the tile runs its epilogue; nobody waits.  The
-    // buffer tb is reused NBUF tiles later: a warp can only get there after
-    // consuming a stage that the epilogue warp releases after finishing this
-    // epilogue (NBUF * PARTS >= kStages + 1), so the reads below are safe.
-    int last = 0;
+    // Publish this warp's share of the tile to the epilogue warp.
     __threadfence_block();
     __syncwarp();
-    if (lane == 0) {
-      last = atomicAdd(&s_cnt[tb], 1) == kW - 1;
-      if (last) s_cnt[tb] = 0;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) continue;
-    __threadfence_block();  // see every warp's s_grp / s_mu of this tile
-
-    const int t = blockIdx.x + tile * gridDim.x;
-    const int h = t % a.H;
-    const int j = (t / a.H) % a.nb;
-    const int b = t / (a.H * a.nb);
-    // group energies over the 16 warps; group 0 gets the exact between-half
-    // term: sum over 64 offsets of (y - mu)^2 = SS0 + SS1 + 16 (mu0 - mu1)^2.
-    float gv = 0.f;
-    if (lane < 8)
-      for (int w = 0; w < kW; ++w) gv += s_grp[tb][w][lane];
-    float between = 0.f, e_dc = 0.f;
-    for (int c = lane; c < D; c += 32) {
-      const float m0 = s_mu[tb][0][c], m1 = s_mu[tb][1][c];
-      const float dm = m0 - m1;
-      between = fmaf(16.0f * dm, dm, between);
-      const float dcv = (32.0f * (m0 + m1)) / kNorm;  // WHT coefficient 0
-      s_dcw[tb][c] = dcv;
-      e_dc = fmaf(dcv, dcv, e_dc);
-    }
-    between = warp_sum(between);
-    e_dc = warp_sum(e_dc);
-    __syncwarp();
-    float g[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, gv, q);
-    g[0] += between;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) g[q] *= 0.125f;  // (64 / 512) Parseval factor of the inner transform
-    float e_ac = 0.f;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) e_ac += g[q];
-    const float e_lo = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
-    const float e_mi = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
-    const float e_hi = band_from_groups(a.bands.lo[2], a.bands.hi[2], g, e_dc);
-    const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
-    const float* dcp = s_dcw[tb];
-    if (a.dc)
-      for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
-    float bmax = -INFINITY;
-    if (a.q) {
-      const int rows = a.Sq * a.G;
-      const float sqrt_d = sqrtf((float)D);
-      const float resid_scale = sqrtf(e_ac);
-      const __nv_bfloat16* qb = (q_cached ? s_q : reinterpret_cast<const __nv_bfloat16*>(a.q)) +
-                                (size_t)b * a.Sq * a.Hq * D;
-      for (int r = 0; r < rows; ++r) {
-        const int s = r / a.G, gq = r - s * a.G;
-        const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D;
-        float dot = 0.f, nrm = 0.f;
-#pragma unroll
-        for (int c = lane; c < D; c += 32) {
-          const float qv = __bfloat162float(qr[c]);
-          dot = fmaf(qv, dcp[c] / kNorm, dot);  // block mean = DC / sqrt(512)
-          nrm = fmaf(qv, qv, nrm);
-        }
-        dot = warp_sum(dot);
-        nrm = warp_sum(nrm);
-        const float bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
-        if (a.bounds && lane == 0)
-          a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + gq] = bound;
-        bmax = fmaxf(bmax, bound);
-      }
-    }
-    if (lane == 0) {
-      const float z = e_hi / (e_lo + 1e-6f);
-      if (a.e_low) a.e_low[cell] = e_lo;
-      if (a.e_mid) a.e_mid[cell] = e_mi;
-      if (a.e_high) a.e_high[cell] = e_hi;
-      if (a.zeta) a.zeta[cell] = z;
-      if (a.q && a.bound_max) a.bound_max[cell] = bmax;
-      if (a.keep) a.keep[cell] = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
-    }
-    __syncwarp();
+    if (lane == 0) mbar_arrive(&tfull[tb]);
   }
 }
 
@@ -730,7 +741,7 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   const int smem = kStages * kSlabB + kQCacheBytes + 1024;
   cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
-  score_tma_kernel<D><<<grid, kScoreThreads, smem, st>>>(map, a, ntiles);
+  score_tma_kernel<D><<<grid, kScoreThreads + 32, smem, st>>>(map, a, ntiles);
   return check_launch("score_tma_kernel");
 }
 
