@@ -361,20 +361,49 @@ __device__ __forceinline__ void mma_h8(float (&d)[4], uint32_t hA, uint32_t b0, 
       : "r"(hA), "r"(zero), "r"(zero), "r"(hA), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c0), "f"(c1));
 }
 
+// Sum each of v[0..7] over the warp; lanes 4r .. 4r+3 return the sum of v[r]
+// (halving exchanges, 9 shuffles instead of 40).
+__device__ __forceinline__ float transpose_sum8(float (&v)[8], int lane) {
+#pragma unroll
+  for (int o = 16, c = 8; o >= 4; o >>= 1, c >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (i < c / 2) {
+        const float send = up ? v[i] : v[i + c / 2];
+        const float keep = up ? v[i + c / 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  return v[0];
+}
+
 constexpr int kStages = 3;
-constexpr int kScoreThreads = 512;
+constexpr int kScoreThreads = 512;  // compute warps
+constexpr int kEpiWarps = 4;        // epilogue warps (and tile buffers)
 constexpr int kQCacheBytes = 16384;  // queries staged in shared memory up to this size  // 16 warps consume every stage in order
 constexpr int kSlabC = 64;                                  // channels per slab
 constexpr int kSlabB = kBlock * kSlabC * 2;                 // bytes per slab (bf16)
 
 __device__ int g_score_status = 0;
 
+#ifdef OC_TIMING
+// Diagnostic build only: per-CTA time stamps of the pipelined scorer.
+__device__ unsigned long long g_sstamp[1024][16];
+#define OC_SSTAMP(i, v) do { if (blockIdx.x < 1024) g_sstamp[blockIdx.x][i] = (v); } while (0)
+#else
+#define OC_SSTAMP(i, v) do {} while (0)
+#endif
+
 template <int D>
-__global__ void __launch_bounds__(kScoreThreads + 32, 1)
+__global__ void __launch_bounds__(kScoreThreads + kEpiWarps * 32, 1)
 score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_tiles) {
   constexpr int PARTS = D / kSlabC;
   constexpr int kW = kScoreThreads / 32;  // 16 warps
-  constexpr int NBUF = 4;                 // tile buffers between the compute warps and the epilogue warp
+  constexpr int NE = kEpiWarps;           // epilogue warps
+  constexpr int NBUF = NE;                // tile buffers, one per epilogue warp
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte swizzled stages must start on a 1024-byte boundary.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -384,9 +413,16 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   __shared__ float s_grp[NBUF][kW][8];       // per-warp coefficient-group energies
   __shared__ float s_mu[NBUF][2][D];         // per-channel means of y0 over each half of the inner offsets
   __shared__ float s_dcw[NBUF][D];           // DC coefficients of the tile in buffer tb
+  __shared__ float s_qn[kQCacheBytes / (2 * 64)];  // squared norms of the staged query rows
   __shared__ volatile int s_abort;
+#ifdef OC_TIMING
+  __shared__ unsigned long long s_tarr[kStages];
+  __shared__ unsigned long long s_trel;
+  if (threadIdx.x == 0) s_trel = 0;
+#endif
 
   const int tid = threadIdx.x;
+  if (tid == 0) OC_SSTAMP(0, globaltimer_ns());
   const int lane = tid & 31, warp = tid >> 5;
   const int ch = warp & 7;    // channels 8ch .. 8ch+7 of a slab (one 16-byte chunk)
   const int hb = warp >> 3;   // inner offsets 32hb .. 32hb+31 (one box of the stage)
@@ -422,37 +458,61 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     for (int i = 0; i < NBUF; ++i) { mbar_init(&tfull[i], kW); mbar_init(&tempty[i], 1); }
     fence_mbar_init();
     s_abort = 0;
+    OC_SSTAMP(10, globaltimer_ns());
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
-  }
-  if (q_cached) {
-    const uint4* src = reinterpret_cast<const uint4*>(a.q);
-    uint4* dst = reinterpret_cast<uint4*>(s_q);
-    for (size_t i = tid; i < q_elems / 8; i += blockDim.x) dst[i] = src[i];
+    OC_SSTAMP(8, globaltimer_ns());
   }
   __syncthreads();  // the only CTA-wide barrier
+  if (tid == 0) OC_SSTAMP(1, globaltimer_ns());
+#ifdef OC_TIMING
+  unsigned long long t_wait = 0;
+#endif
 
-  // Warp kW runs the tile epilogues (bound, zeta, keep) while the 16
-  // compute warps go on with the next tiles: tile buffer tb is handed over
-  // on tfull[tb] (16 arrivals) and handed back on tempty[tb].
-  if (warp == kW) {
-    for (int tile = 0; tile < my_tiles; ++tile) {
-      const int tb = tile % NBUF;
-      if (!mbar_wait(&tfull[tb], (tile / NBUF) & 1)) {
+  // Warps kW .. kW+NE-1 run the tile epilogues (bound, zeta, keep) while the
+  // 16 compute warps go on with the next tiles.  Epilogue warp e owns tile
+  // buffer e and the tiles e, e + NE, ...; the buffer is handed over on
+  // tfull[e] (16 arrivals) and handed back on tempty[e].
+  if (warp >= kW) {
+    const int e = warp - kW;
+    const int qrows = q_cached ? (int)(q_elems / D) : 0;
+    if (q_cached) {
+      // Queries and their squared norms, staged once (only these warps read them).
+      const uint4* src = reinterpret_cast<const uint4*>(a.q);
+      uint4* dst = reinterpret_cast<uint4*>(s_q);
+      for (size_t i = e * 32 + lane; i < q_elems / 8; i += NE * 32) dst[i] = src[i];
+      asm volatile("bar.sync 1, %0;" ::"r"(NE * 32) : "memory");
+      for (int r = e; r < qrows; r += NE) {
+        float nrm = 0.f;
+#pragma unroll
+        for (int c = lane; c < D; c += 32) {
+          const float qv = __bfloat162float(s_q[(size_t)r * D + c]);
+          nrm = fmaf(qv, qv, nrm);
+        }
+        nrm = warp_sum(nrm);
+        if (lane == 0) s_qn[r] = nrm;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(NE * 32) : "memory");
+    }
+    for (int tile = e; tile < my_tiles; tile += NE) {
+      const int tb = e;
+      if (!mbar_wait(&tfull[tb], (tile / NE) & 1)) {
         s_abort = 1;
         if (lane == 0) atomicExch(&g_score_status, 1);
         return;
       }
-
       const int t = blockIdx.x + tile * gridDim.x;
       const int h = t % a.H;
       const int j = (t / a.H) % a.nb;
       const int b = t / (a.H * a.nb);
-      // group energies over the 16 warps; group 0 gets the exact between-half
-      // term: sum over 64 offsets of (y - mu)^2 = SS0 + SS1 + 16 (mu0 - mu1)^2.
-      float gv = 0.f;
-      if (lane < 8)
-        for (int w = 0; w < kW; ++w) gv += s_grp[tb][w][lane];
+      // Group energies over the 16 warps (lanes 4q .. 4q+3 sum group q); group
+      // 0 gets the exact between-half term: the sum over 64 offsets of
+      // (y - mu)^2 = SS0 + SS1 + 16 (mu0 - mu1)^2.
+      const int q8 = lane >> 2, wq = lane & 3;
+      float gv = (s_grp[tb][wq][q8] + s_grp[tb][wq + 4][q8]) + (s_grp[tb][wq + 8][q8] + s_grp[tb][wq + 12][q8]);
+      gv += __shfl_xor_sync(0xffffffffu, gv, 1);
+      gv += __shfl_xor_sync(0xffffffffu, gv, 2);
       float between = 0.f, e_dc = 0.f;
+#pragma unroll
       for (int c = lane; c < D; c += 32) {
         const float m0 = s_mu[tb][0][c], m1 = s_mu[tb][1][c];
         const float dm = m0 - m1;
@@ -465,13 +525,13 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       e_dc = warp_sum(e_dc);
       __syncwarp();
       float g[8];
-  #pragma unroll
-      for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, gv, q);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) g[q] = __shfl_sync(0xffffffffu, gv, 4 * q);
       g[0] += between;
-  #pragma unroll
+#pragma unroll
       for (int q = 0; q < 8; ++q) g[q] *= 0.125f;  // (64 / 512) Parseval factor of the inner transform
       float e_ac = 0.f;
-  #pragma unroll
+#pragma unroll
       for (int q = 0; q < 8; ++q) e_ac += g[q];
       const float e_lo = band_from_groups(a.bands.lo[0], a.bands.hi[0], g, e_dc);
       const float e_mi = band_from_groups(a.bands.lo[1], a.bands.hi[1], g, e_dc);
@@ -482,28 +542,58 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
         for (int c = lane; c < D; c += 32) a.dc[cell * D + c] = dcp[c];
       float bmax = -INFINITY;
       if (a.q) {
+        // rows = Sq * G <= 8 on this path: all rows' dot products at once,
+        // reduced so that lanes 4r .. 4r+3 hold row r.
         const int rows = a.Sq * a.G;
         const float sqrt_d = sqrtf((float)D);
         const float resid_scale = sqrtf(e_ac);
-        const __nv_bfloat16* qb = (q_cached ? s_q : reinterpret_cast<const __nv_bfloat16*>(a.q)) +
-                                  (size_t)b * a.Sq * a.Hq * D;
-        for (int r = 0; r < rows; ++r) {
-          const int s = r / a.G, gq = r - s * a.G;
-          const __nv_bfloat16* qr = qb + ((size_t)s * a.Hq + (size_t)h * a.G + gq) * D;
-          float dot = 0.f, nrm = 0.f;
-  #pragma unroll
-          for (int c = lane; c < D; c += 32) {
-            const float qv = __bfloat162float(qr[c]);
-            dot = fmaf(qv, dcp[c] / kNorm, dot);  // block mean = DC / sqrt(512)
-            nrm = fmaf(qv, qv, nrm);
-          }
-          dot = warp_sum(dot);
-          nrm = warp_sum(nrm);
-          const float bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
-          if (a.bounds && lane == 0)
-            a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + gq] = bound;
-          bmax = fmaxf(bmax, bound);
+        const __nv_bfloat16* qb = q_cached ? s_q : reinterpret_cast<const __nv_bfloat16*>(a.q);
+        float dv[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) dv[r] = 0.f;
+#pragma unroll
+        for (int c = lane; c < D; c += 32) {
+          const float mean = dcp[c] / kNorm;  // block mean = DC / sqrt(512)
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            if (r < rows) {
+              const int s = r / a.G, gq = r - s * a.G;
+              const size_t qrow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + gq;
+              dv[r] = fmaf(__bfloat162float(qb[qrow * D + c]), mean, dv[r]);
+            }
         }
+        const float dot = transpose_sum8(dv, lane);
+        const int r = lane >> 2;
+        float nrm = 0.f;
+        size_t qrow = 0;
+        if (r < rows) {
+          const int s = r / a.G, gq = r - s * a.G;
+          qrow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + gq;
+        }
+        if (q_cached) {
+          if (r < rows) nrm = s_qn[qrow];
+        } else {
+          for (int rr = 0; rr < rows; ++rr) {
+            const int s = rr / a.G, gq = rr - s * a.G;
+            const size_t qr = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + gq;
+            float n2 = 0.f;
+            for (int c = lane; c < D; c += 32) {
+              const float qv = __bfloat162float(qb[qr * D + c]);
+              n2 = fmaf(qv, qv, n2);
+            }
+            n2 = warp_sum(n2);
+            if (rr == r) nrm = n2;
+          }
+        }
+        float bound = -INFINITY;
+        if (r < rows) {
+          bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
+          if (a.bounds && (lane & 3) == 0) {
+            const int s = r / a.G, gq = r - s * a.G;
+            a.bounds[(((size_t)b * a.Sq + s) * a.nb + j) * a.Hq + (size_t)h * a.G + gq] = bound;
+          }
+        }
+        bmax = warp_max(bound);
       }
       if (lane == 0) {
         const float z = e_hi / (e_lo + 1e-6f);
@@ -517,6 +607,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[tb]);
     }
+    if (lane == 0 && e == 0) OC_SSTAMP(4, globaltimer_ns());
     return;
   }
 
@@ -541,11 +632,19 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       // A copy that never completes sets the abort flag: every warp stops
       // waiting and leaves (there is no barrier left to meet).
       if (s_abort) return;
+#ifdef OC_TIMING
+      const unsigned long long tw0 = globaltimer_ns();
+#endif
       if (!mbar_wait(&full[stage], (k / kStages) & 1)) {
         s_abort = 1;
         if (lane == 0) atomicExch(&g_score_status, 1);
         return;
       }
+#ifdef OC_TIMING
+      const unsigned long long tw1 = globaltimer_ns();
+      t_wait += tw1 - tw0;
+      if (warp == 0 && lane == 0) { s_tarr[stage] = tw1; if (k == 0) OC_SSTAMP(2, tw1); }
+#endif
       // 32 transposed 8x8 matrices: B operands (k = i_hi, n = channel) of
       // the inner offsets 32hb + 4s + m, m = 0..3.
       const uint32_t sbase = smem_u32(smem + (size_t)stage * kSlabB) + lane_off;
@@ -561,6 +660,9 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
           if (k + kStages < n_units && !s_abort) {
             fence_proxy_async();
             issue(k + kStages);
+#ifdef OC_TIMING
+            s_trel += globaltimer_ns() - s_tarr[stage];
+#endif
           }
         }
       }
@@ -612,6 +714,14 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     __syncwarp();
     if (lane == 0) mbar_arrive(&tfull[tb]);
   }
+#ifdef OC_TIMING
+  if (warp == 0 && lane == 0) {
+    OC_SSTAMP(3, globaltimer_ns());
+    OC_SSTAMP(5, t_wait);
+    OC_SSTAMP(6, s_trel);
+    OC_SSTAMP(7, n_units);
+  }
+#endif
 }
 
 // ---------------------------------------------------------------------------
@@ -741,7 +851,7 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   const int smem = kStages * kSlabB + kQCacheBytes + 1024;
   cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
-  score_tma_kernel<D><<<grid, kScoreThreads + 32, smem, st>>>(map, a, ntiles);
+  score_tma_kernel<D><<<grid, kScoreThreads + kEpiWarps * 32, smem, st>>>(map, a, ntiles);
   return check_launch("score_tma_kernel");
 }
 
@@ -855,3 +965,9 @@ int score_status(int* status, int reset) {
   return OC_OK;
 }
 }  // namespace oc
+
+#ifdef OC_TIMING
+extern "C" int oc_probe_read_score_stamps(unsigned long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, oc::g_sstamp, sizeof(unsigned long long) * 16 * n);
+}
+#endif
