@@ -169,7 +169,9 @@ class Engine:
         self.gm = torch.empty((world, rows), dtype=torch.float32, device=device)
         self.gl = torch.empty((world, rows), dtype=torch.float32, device=device)
         self.go = torch.empty((world, rows, D), dtype=torch.float32, device=device)
-        self.launches_per_step = 4 if world == 1 else 5
+        # our kernels per layer: scorer, attention (compaction fused), merge;
+        # sequence-parallel: scorer, compaction, attention, run merge, shard merge
+        self.launches_per_step = 3 if world == 1 else 5
 
     @property
     def stream(self):
@@ -205,18 +207,21 @@ class Engine:
         _l.call("oc_merge_partials", _l.ptr(self.gm), _l.ptr(self.gl), _l.ptr(self.go), self.world, HQ, D,
                 _l.ptr(self.out), 1, self.stream)
 
-    def step(self, L, ev=None):
-        if ev is not None:
-            ev[0].record()
-        self.score(L)
-        if ev is not None:
-            ev[1].record()
+    def decode(self, L, q=None):
+        """One layer through the one-call C ABI (score -> compact -> attend)."""
+        _l = self.lib
+        q = L.q if q is None else q
+        _l.call("oc_decode_step", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, 1, 1, HQ, HKV, D, S_SHARD, L.tau, ZETA_MAX,
+                _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(self.out), 1,
+                _l.ptr(self.ws), self.ws_bytes, self.stream)
+
+    def step(self, L, q=None):
+        if self.world == 1:
+            self.decode(L, q)
+            return
+        self.score(L, q)
         self.compact()
-        if ev is not None:
-            ev[2].record()
-        self.attend(L)
-        if ev is not None:
-            ev[3].record()
+        self.attend(L, q)
 
 
 # ---------------------------------------------------------------------------
@@ -308,12 +313,12 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     K = args.steps
-    # The timed region replays one CUDA graph per layer (score -> compact ->
-    # attend captured from the same C-ABI calls), so host launch latency is
-    # not on the clock.  Multi-GPU steps run eagerly (NCCL in the step).
+    # The timed region replays a CUDA graph of LAYERS consecutive layers (the
+    # same C-ABI calls captured), so host launch latency is not on the clock
+    # and each kernel may start while the one before it drains (programmatic
+    # dependent launch).  Multi-GPU steps run eagerly (NCCL in the step).
     graphs = None
     if world == 1:
-        graphs = []
         cap = torch.cuda.Stream()
         cap.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(cap):
@@ -321,37 +326,53 @@ def run_ours(args, rank, world, local_rank):
                 eng.step(L)
         torch.cuda.current_stream().wait_stream(cap)
         torch.cuda.synchronize()
+        g_all = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_all):
+            for L in layers:
+                eng.step(L)
+        g_one = []
         for L in layers:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 eng.step(L)
-            graphs.append(g)
-        for s in range(2 * LAYERS):
-            graphs[s % LAYERS].replay()
+            g_one.append(g)
+        graphs = (g_all, g_one)
+        for s in range(2):
+            g_all.replay()
         torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local_rank) as clk:
         barrier()
         torch.cuda.synchronize()
         start.record()
-        for s in range(K):
-            if graphs is not None:
-                graphs[s % LAYERS].replay()
-            else:
+        if graphs is not None:
+            for s in range(K // LAYERS):
+                graphs[0].replay()
+            for s in range(K % LAYERS):
+                graphs[1][s].replay()
+        else:
+            for s in range(K):
                 eng.step(layers[s % LAYERS])
         stop.record()
         torch.cuda.synchronize()
         barrier()
     ms = start.elapsed_time(stop) / K
-    # Per-kernel durations: eager launches with an event between kernels.
+    # Scorer launch duration (the roofline kernel): CUDA events bracketing
+    # each launch on the launching stream, eager, inputs rotating past L2.
     Kb = max(LAYERS, min(K, 400))
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(Kb)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(Kb)]
     for s in range(Kb):
-        eng.step(layers[s % LAYERS], evs[s])
+        evs[s][0].record()
+        eng.score(layers[s % LAYERS])
+        evs[s][1].record()
     torch.cuda.synchronize()
     t_score = statistics.median(e[0].elapsed_time(e[1]) for e in evs)
-    t_comp = statistics.median(e[1].elapsed_time(e[2]) for e in evs)
-    t_attn = statistics.median(e[2].elapsed_time(e[3]) for e in evs)
+    for s in range(Kb):
+        evs[s][0].record()
+        eng.step(layers[s % LAYERS])
+        evs[s][1].record()
+    torch.cuda.synchronize()
+    t_step_eager = statistics.median(e[0].elapsed_time(e[1]) for e in evs)
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -366,7 +387,7 @@ def run_ours(args, rank, world, local_rank):
     Ke = max(8, min(K, 2000))
     for s in range(4):
         q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
-        eng.score(layers[s % LAYERS], q_dev); eng.compact(); eng.attend(layers[s % LAYERS], q_dev)
+        eng.step(layers[s % LAYERS], q_dev)
         out_host.copy_(eng.out, non_blocking=True)
     torch.cuda.synchronize()
     barrier()
@@ -375,9 +396,7 @@ def run_ours(args, rank, world, local_rank):
     for s in range(Ke):
         L = layers[s % LAYERS]
         q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
-        eng.score(L, q_dev)
-        eng.compact()
-        eng.attend(L, q_dev)
+        eng.step(L, q_dev)
         out_host.copy_(eng.out, non_blocking=True)
         cnt_host.copy_(eng.count, non_blocking=True)
     e1.record()
@@ -411,16 +430,15 @@ def run_ours(args, rank, world, local_rank):
                                "(%d total), evict=%.2f, zeta_max=5" % (S_SHARD, S_SHARD * world, args.evict),
                    "l2": "inputs > L2: 4 layers of KV (1.07 GB) rotate per step",
                    "parallelism": "single GPU" if world == 1 else f"sequence-parallel x{world}, LSE merge"},
-        "roofline": {"bound": "hbm", "kernel": "score_partial_kernel (fused scorer)",
+        "roofline": {"bound": "hbm", "kernel": "score_tma_kernel (fused scorer)",
                      "achieved": round(score_gbs, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(score_gbs / hbm, 4), "traffic": None, "peak_kind": peak_kind,
                      "bytes_per_launch": k_bytes},
         "step_roofline": {"alg_bytes": int(alg_bytes), "achieved_gbs": round(alg_bytes / (ms * 1e-3) / 1e9, 1),
                           "frac": round(alg_bytes / (ms * 1e-3) / 1e9 / hbm, 4)},
-        "kernel_us": {"score": round(t_score * 1e3, 2), "compact": round(t_comp * 1e3, 2),
-                      "attention": round(t_attn * 1e3, 2),
-                      "how": "median over eager steps with CUDA events between the launches"},
-        "timed_region": "CUDA-graph replay of each layer's step" if world == 1 else "eager launches",
+        "kernel_us": {"score": round(t_score * 1e3, 2), "step_eager": round(t_step_eager * 1e3, 2),
+                      "how": "median of eager launches bracketed by CUDA events"},
+        "timed_region": ("CUDA-graph replay of %d consecutive layers" % LAYERS) if world == 1 else "eager launches",
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": UNIT, "h2d_bytes_per_step": HQ * D * 2,
                 "d2h_bytes_per_step": HQ * D * 2 + 4,

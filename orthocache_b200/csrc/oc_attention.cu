@@ -56,6 +56,8 @@ struct AttnArgs {
   void* out;        // final output (mode 0), bf16 if out_bf16
   int out_bf16;
   float *pm, *pl, *po;  // mode 1: (m, l, o) per output row
+  const uint8_t* keep;  // non-null: build the union lists from this (B, S / bs, Hkv) mask in the kernel
+  int32_t* perm_out;    // ... and CTA 0 writes the permutation here (count goes to `count`)
   int mode;
 };
 
@@ -373,6 +375,37 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[NV], int lane) {
   return v[0];
 }
 
+// Block indices of a CTA's first kBlkCache items, loaded by one warp in a
+// single round of independent loads (lane i walks from the CTA's first item
+// to item i list by list), so that no stage refill waits on a global load.
+constexpr int kBlkCache = 64;
+
+__device__ __forceinline__ void fill_blk_cache(const AttnArgs& a, int beg, int N, int n_mine, int* s_blk,
+                                               int lane) {
+  const int n = min(n_mine, kBlkCache);
+  for (int i = lane; i < n; i += 32) {
+    ItemIter p;
+    p.start(a, beg, N);
+    int off = i;
+    while (off > 0 && p.b < a.B) {
+      const int rem = p.n - 1 - p.item;  // items after this one in its (batch, head, row tile) list
+      if (off <= rem) {
+        p.item += off;
+        off = 0;
+      } else {
+        off -= rem + 1;
+        p.item = p.n - 1;
+        p.next(a);
+      }
+    }
+    s_blk[i] = p.b < a.B ? a.idx[(size_t)p.b * a.idx_stride + (size_t)p.h * a.idx_hstride + p.item / a.chunks] : 0;
+  }
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
 template <int D, int RT>
 __global__ void __launch_bounds__(kVThreads, 1)
 attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
@@ -389,10 +422,21 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __shared__ __align__(8) uint64_t full[kVStages];
   __shared__ int s_rel[kVStages];
   __shared__ volatile int s_abort;
+  __shared__ int s_blk[kBlkCache];
   __shared__ float s_wm[kVWarps][RT], s_wl[kVWarps][RT];
   __shared__ float s_wo[kVWarps][RT][D];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    for (int i = 0; i < kVStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
+    fence_mbar_init();
+    s_abort = 0;
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
+  // Launched as a programmatic dependent of the compaction: the lists and
+  // counts (and everything else) are read only after it has finished.
+  pdl_wait();
   const int N = total_items(a);
   const int per = (N + gridDim.x - 1) / gridDim.x;
   const int beg = min(N, (int)blockIdx.x * per), end = min(N, beg + per);
@@ -401,7 +445,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   // Loads item position `pos` (the CTA's k-th item) into stage k % kVStages.
   auto issue = [&](int k, const ItemIter& pos) {
     const int slot = pos.item / a.chunks, c = pos.item - slot * a.chunks;
-    const int blk = a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
+    const int blk = k < kBlkCache ? s_blk[k] : a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
     // An out-of-range index is never dereferenced: block 0 is loaded instead
     // and the item is skipped.
     const int y = (blk < 0 || blk >= a.S / a.bs) ? pos.b * a.S : pos.b * a.S + blk * a.bs + c * CH;
@@ -412,10 +456,11 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     tma_load_2d(dst + KB, &vmap, bar, pos.h * D, y);
   };
 
+  if (warp == 0) {
+    fill_blk_cache(a, beg, N, n_mine, s_blk, lane);
+    __syncwarp();
+  }
   if (tid == 0) {
-    for (int i = 0; i < kVStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
-    fence_mbar_init();
-    s_abort = 0;
     ItemIter pre;
     pre.start(a, beg, N);
     for (int k = 0; k < kVStages && k < n_mine; ++k) {
@@ -425,7 +470,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   }
   __syncthreads();
   // The merge kernel may now be scheduled (it waits for this grid to finish).
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_trigger();
 
   // Per-warp online-softmax state of the current run.
   float m_run[RT];
@@ -616,8 +661,9 @@ int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
 #define OC_ASTREAM(RTV)                                                                                   \
   do {                                                                                                    \
     cudaFuncSetAttribute(attn_stream_kernel<D, RTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    attn_stream_kernel<D, RTV><<<grid, kVThreads, smem, st>>>(km, vm, a);                                 \
+    e = launch_pdl(attn_stream_kernel<D, RTV>, dim3(grid), dim3(kVThreads), smem, st, km, vm, a);      \
   } while (0)
+  cudaError_t e = cudaSuccess;
   if (rt == 1) OC_ASTREAM(1);
   else if (rt == 2) OC_ASTREAM(2);
   else if constexpr (D <= 128) {
@@ -626,6 +672,7 @@ int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
   } else
     return set_error(OC_ERR_SHAPE, "attention: row tile %d", rt);
 #undef OC_ASTREAM
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "attn_stream_kernel: %s", cudaGetErrorString(e));
   return check_launch("attn_stream_kernel");
 }
 
@@ -682,9 +729,65 @@ __device__ __forceinline__ uint32_t swz(int t, int c8) {
   return (uint32_t)((c8 >> 3) * (CH * 128) + t * 128 + (((c8 & 7) ^ (t & 7)) << 4));
 }
 
+// Union lists from the scorer's keep mask (the compaction of
+// compaction.py:28-100 folded into the attention prologue): every CTA
+// derives the active-first list of each batch row in shared memory with a
+// ballot scan (active block j goes to the number of active blocks before
+// it), then reads its work from there.  CTA 0 also writes the complete
+// stable permutation (inactive blocks after the active ones, in order) and
+// the counts.  On return a.idx / a.count point at the shared-memory lists.
+template <int NT>
+__device__ void lists_from_keep(AttnArgs& a, int* s_list, int* s_cnt, int* s_scan) {
+  constexpr int NWP = NT / 32;
+  const int nb = a.S / a.bs, H = a.Hkv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool writer = blockIdx.x == 0;
+  for (int pass = 0; pass < (writer ? 2 : 1); ++pass) {
+    for (int b = 0; b < a.B; ++b) {
+      int base = 0;
+      for (int j0 = 0; j0 < nb; j0 += NT) {
+        const int j = j0 + tid;
+        bool act = false;
+        if (j < nb) {
+          const uint8_t* kp = a.keep + ((size_t)b * nb + j) * H;
+          if (H == 8 && (reinterpret_cast<uintptr_t>(kp) & 7) == 0) {
+            act = *reinterpret_cast<const unsigned long long*>(kp) != 0ull;  // one load per block
+          } else {
+            for (int h = 0; h < H; ++h) act |= kp[h] != 0;
+          }
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, act);
+        if (lane == 0) s_scan[warp] = __popc(bal);
+        __syncthreads();
+        int before = 0, tot = 0;
+#pragma unroll
+        for (int w = 0; w < NWP; ++w) {
+          const int v = s_scan[w];
+          before += w < warp ? v : 0;
+          tot += v;
+        }
+        const int rank = base + before + __popc(bal & ((1u << lane) - 1u));  // active blocks before j
+        if (pass == 0 && act) s_list[b * nb + rank] = j;
+        if (pass == 1 && j < nb) a.perm_out[(size_t)b * nb + (act ? rank : s_cnt[b] + j - rank)] = j;
+        __syncthreads();
+        base += tot;
+      }
+      if (pass == 0 && tid == 0) s_cnt[b] = base;
+      if (pass == 1 && tid == 0) const_cast<int32_t*>(a.count)[b] = base;
+    }
+    __syncthreads();
+  }
+  a.idx = s_list;
+  a.count = s_cnt;
+  a.idx_stride = nb;
+  a.idx_hstride = 0;
+  a.cnt_stride = 1;
+  a.cnt_hstride = 0;
+}
+
 template <int D, int RT>
 __global__ void __launch_bounds__(32 * (8192 / D) / 16, 2)
-attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a_in) {
   constexpr int CH = 8192 / D;           // tokens per item
   constexpr int NW = CH / 16;            // warps: 16 tokens each
   constexpr int NT = 32 * NW;
@@ -697,6 +800,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   __shared__ __align__(8) uint64_t full[kMStages];
   __shared__ int s_rel[kMStages];
   __shared__ volatile int s_abort;
+  __shared__ int s_blk[kBlkCache];
   __shared__ float s_wm[NW][RT], s_wl[NW][RT];
   __shared__ float s_wo[NW][RT][D];
 
@@ -704,14 +808,32 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   OC_STAMP(0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;  // MMA fragment coordinates
+  if (tid == 0) {
+    for (int i = 0; i < kMStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
+    fence_mbar_init();
+    s_abort = 0;
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
+  // Launched as a programmatic dependent of the compaction: the lists and
+  // counts (and everything else) are read only after it has finished.
+  pdl_wait();
+  OC_STAMP(5);
+  AttnArgs a = a_in;
+  if (a.keep) {
+    __shared__ int s_scan[NW];
+    int* s_list = reinterpret_cast<int*>(smem + (size_t)kMStages * kMStageBytes);
+    lists_from_keep<NT>(a, s_list, s_list + a.B * (a.S / a.bs), s_scan);
+  }
   const int N = total_items(a);
   const int per = (N + gridDim.x - 1) / gridDim.x;
   const int beg = min(N, (int)blockIdx.x * per), end = min(N, beg + per);
   const int n_mine = end - beg;
+  OC_STAMP(6);
 
   auto issue = [&](int k, const ItemIter& pos) {
     const int slot = pos.item / a.chunks, cc = pos.item - slot * a.chunks;
-    const int blk = a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
+    const int blk = k < kBlkCache ? s_blk[k] : a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
     const int y = (blk < 0 || blk >= a.S / a.bs) ? pos.b * a.S : pos.b * a.S + blk * a.bs + cc * CH;
     uint8_t* dst = smem + (size_t)(k % kMStages) * kMStageBytes;
     uint64_t* bar = &full[k % kMStages];
@@ -723,10 +845,12 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     }
   };
 
+  if (warp == 0) {
+    fill_blk_cache(a, beg, N, n_mine, s_blk, lane);
+    OC_STAMP(7);
+    __syncwarp();
+  }
   if (tid == 0) {
-    for (int i = 0; i < kMStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
-    fence_mbar_init();
-    s_abort = 0;
     ItemIter pre;
     pre.start(a, beg, N);
     for (int k = 0; k < kMStages && k < n_mine; ++k) {
@@ -736,7 +860,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   }
   __syncthreads();
   // The merge kernel may now be scheduled (it waits for this grid to finish).
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_trigger();
 
   // per-warp online-softmax state of the run: rows g and g + 8 of the tile
   float m_run[2], l_acc[2];
@@ -907,6 +1031,10 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   OC_STAMP(3);
 }
 
+// Shared memory for lists built from a keep mask (B rows of nb blocks + B counts).
+constexpr int kKeepListMax = 1024;  // B * nb at most (4 KB)
+int keep_list_bytes(int B, int nb) { return ((B * nb + B) * 4 + 15) / 16 * 16; }
+
 template <int D>
 int launch_attn_mma(const AttnArgs& a, int rt, cudaStream_t st) {
   constexpr int CH = 8192 / D;
@@ -916,30 +1044,43 @@ int launch_attn_mma(const AttnArgs& a, int rt, cudaStream_t st) {
   int rc = encode_map_2d(&km, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, CH, true);
   if (!rc) rc = encode_map_2d(&vm, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, CH, true);
   if (rc) return set_error(OC_ERR_CUDA, "attention: tensor map encode failed (%d)", rc);
-  const int smem = kMStages * kMStageBytes + 1024;
+  // keep mode: the union lists and counts follow the stage ring
+  const int smem = kMStages * kMStageBytes + 1024 + (a.keep ? keep_list_bytes(a.B, a.S / a.bs) : 0);
   const int grid = a.run_grid;
 #define OC_AMMA(RTV)                                                                                   \
   do {                                                                                                 \
     cudaFuncSetAttribute(attn_mma_kernel<D, RTV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    attn_mma_kernel<D, RTV><<<grid, NT, smem, st>>>(km, vm, a);                                        \
+    e = launch_pdl(attn_mma_kernel<D, RTV>, dim3(grid), dim3(NT), smem, st, km, vm, a);               \
   } while (0)
+  cudaError_t e = cudaSuccess;
   if (rt <= 4) OC_AMMA(4);
   else OC_AMMA(8);
 #undef OC_AMMA
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "attn_mma_kernel: %s", cudaGetErrorString(e));
   return check_launch("attn_mma_kernel");
 }
 
-// Combine the items of one (batch, kv head, row): M = max m_i,
+// Combine the partials of one (batch, kv head, row): M = max m_i,
 // L = sum l_i 2^(m_i - M), O = sum o_i 2^(m_i - M).  mode 0 writes O / L in
 // the output dtype at the reference's (Sq, Hq, D) position (zeros when the
 // batch row has no retained block); mode 1 writes (M, L, O) float32 for a
-// later cross-shard merge.
+// later cross-shard merge.  kMergeThreads threads: NQ = kMergeThreads / D
+// groups of D channels, group q taking the partials j = q (mod NQ), so the
+// output loads of a row go out in few rounds; the groups are summed in
+// shared memory at the end.  The code is kept small: it runs once per row
+// and its instructions are fetched cold.
+constexpr int kMergeThreads = 512;
+
 template <typename TO>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kMergeThreads)
 attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode) {
-  __shared__ float s_f[256];
-  __shared__ float s_red[8];
+  __shared__ float s_w[kMergeThreads];            // weights 2^(m_j - M) of the current chunk
+  __shared__ float s_red[kMergeThreads / 32];
+  __shared__ float s_o[kMergeThreads];            // per-group sums
+  pdl_trigger();  // the next kernel may stage its prologue meanwhile
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NQ = kMergeThreads / a.D;
+  const int d = tid % a.D, q = tid / a.D;
   const int r = blockIdx.x % a.R;
   const int h = (blockIdx.x / a.R) % a.Hkv;
   const int b = blockIdx.x / (a.R * a.Hkv);
@@ -967,59 +1108,54 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
     const int last = (s0 + n - 1) / per;                 // last CTA touching the list
     np = 1 + max(0, last - c1 + 1);
   }
-  auto pos = [&](int j) -> int { return (a.run_grid > 0 && j > 0) ? (c1 + j - 1) * per - s0 : j; };
+  auto prow = [&](int j) -> size_t {
+    return p0 + (size_t)((a.run_grid > 0 && j > 0) ? (c1 + j - 1) * per - s0 : j) * stride;
+  };
   // Launched as a programmatic dependent of the stream kernel: wait for it to
   // finish (and its partials to be visible).  A no-op for a plain launch.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_wait();
 
-  // M = max over the partials (in parallel)
-  float M = -INFINITY;
-  for (int j = tid; j < np; j += 256) M = fmaxf(M, a.ws_m[p0 + (size_t)pos(j) * stride]);
+  // M over all partials
+  float mj = -INFINITY, lj = 0.f;  // this thread's partial of the first chunk
+  if (tid < np) { mj = a.ws_m[prow(tid)]; lj = a.ws_l[prow(tid)]; }
+  float M = mj;
+  for (int j = tid + kMergeThreads; j < np; j += kMergeThreads) M = fmaxf(M, a.ws_m[prow(j)]);
   M = warp_max(M);
   if (lane == 0) s_red[warp] = M;
   __syncthreads();
   M = s_red[0];
-  for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
+  for (int w = 1; w < kMergeThreads / 32; ++w) M = fmaxf(M, s_red[w]);
   __syncthreads();
 
-  // Weights f_j = 2^(m_j - M) staged 256 at a time; thread d accumulates O[d].
-  float lpart = 0.f, O = 0.f;
-  const int d = tid;
-  for (int c0 = 0; c0 < np; c0 += 256) {
+  float L = 0.f, O = 0.f;
+  for (int c0 = 0; c0 < np; c0 += kMergeThreads) {
     const int j = c0 + tid;
-    float f = 0.f;
+    float w = 0.f;
     if (j < np) {
-      const size_t p = p0 + (size_t)pos(j) * stride;
-      const float mi = a.ws_m[p];
-      if (mi != -INFINITY) {
-        f = exp2f(mi - M);
-        lpart = fmaf(a.ws_l[p], f, lpart);
+      const float m = c0 == 0 ? mj : a.ws_m[prow(j)];
+      const float l = c0 == 0 ? lj : a.ws_l[prow(j)];
+      if (m != -INFINITY) {
+        w = exp2f(m - M);
+        L = fmaf(l, w, L);
       }
     }
-    s_f[tid] = f;
+    s_w[tid] = w;
     __syncthreads();
-    if (d < a.D) {
-      // Every listed partial holds a written output row (zeros when its max
-      // is -inf), so the loads are unconditional and issue together.
-      const int cn = min(256, np - c0);
-      int jj = 0;
-      for (; jj + 8 <= cn; jj += 8) {
-        float ov[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) ov[u] = a.ws_o[(p0 + (size_t)pos(c0 + jj + u) * stride) * a.D + d];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) O = fmaf(s_f[jj + u], ov[u], O);
-      }
-      for (; jj < cn; ++jj) O = fmaf(s_f[jj], a.ws_o[(p0 + (size_t)pos(c0 + jj) * stride) * a.D + d], O);
-    }
+    // Every listed partial holds a written output row (zeros when its max is
+    // -inf), so the loads are unconditional.
+    const int cn = min(kMergeThreads, np - c0);
+#pragma unroll 8
+    for (int u = q; u < cn; u += NQ) O = fmaf(s_w[u], a.ws_o[prow(c0 + u) * a.D + d], O);
     __syncthreads();
   }
-  lpart = warp_sum(lpart);
-  if (lane == 0) s_red[warp] = lpart;
+  s_o[tid] = O;
+  L = warp_sum(L);
+  if (lane == 0) s_red[warp] = L;
   __syncthreads();
-  float L = 0.f;
-  for (int w = 0; w < 8; ++w) L += s_red[w];
-  if (d < a.D) {
+  if (q == 0) {
+    for (int qq = 1; qq < NQ; ++qq) O += s_o[qq * a.D + d];
+    L = 0.f;
+    for (int w = 0; w < kMergeThreads / 32; ++w) L += s_red[w];
     if (mode == 0) {
       out[orow * a.D + d] = from_f32<TO>(L > 0.f ? O / L : 0.f);
     } else {
@@ -1152,7 +1288,8 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
                   int idx_stride, int idx_hstride, const int32_t* count, int cnt_stride, int cnt_hstride,
                   int B, int Sq, int Hq, int Hkv, int D,
                   int S, int bs, int max_blocks, void* out, int out_dtype, float* pm, float* pl,
-                  float* po, void* ws, size_t ws_bytes, int mode, cudaStream_t st) {
+                  float* po, void* ws, size_t ws_bytes, int mode, cudaStream_t st,
+                  const uint8_t* keep = nullptr, int32_t* perm_out = nullptr) {
   int rc = validate_attn(q, k, v, dtype, idx, idx_stride, idx_hstride, count, B, Sq, Hq, Hkv, D, S, bs,
                          max_blocks);
   if (rc) return rc;
@@ -1191,6 +1328,8 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.out_bf16 = out_dtype == OC_BF16;
   a.pm = pm; a.pl = pl; a.po = po;
   a.mode = mode;
+  a.keep = keep;
+  a.perm_out = perm_out;
   const int64_t rows = (int64_t)B * Hkv * a.R;
   OC_REQUIRE(rows < (1ll << 31), OC_ERR_CAPACITY, "attention: too many rows");
 
@@ -1213,7 +1352,7 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3((unsigned)rows);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kMergeThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -1308,6 +1447,13 @@ extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int d
                            256, 512, tau, zeta_max, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
                            keep, 0, stream);
   if (rc) return rc;
+  if (dtype == OC_BF16 && (head_dim == 64 || head_dim == 128) && batch * nb <= kKeepListMax) {
+    // The compaction runs inside the tensor-core attention kernel.
+    OC_REQUIRE(out, OC_ERR_NULL, "oc_decode_step: out is NULL");
+    return run_attention(q, k, v, dtype, perm, nb, 0, count, 1, 0, batch, q_len, q_heads, kv_heads, head_dim,
+                         seq_len, 512, nb, out, out_dtype, nullptr, nullptr, nullptr, workspace, workspace_bytes, 0,
+                         reinterpret_cast<cudaStream_t>(stream), keep, perm);
+  }
   rc = oc_stream_compact(keep, batch, nb, kv_heads, perm, count, stream);
   if (rc) return rc;
   return oc_indirect_attention(q, k, v, dtype, perm, nb, 0, count, 1, 0, batch, q_len, q_heads, kv_heads, head_dim,

@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(kScanThreads)
 compact_kernel(const uint8_t* __restrict__ keep, int nb, int heads,
                int32_t* __restrict__ perm, int32_t* __restrict__ count) {
   __shared__ int s_warp[33];
+  pdl_trigger();
+  pdl_wait();  // keep comes from the scorer
   const int b = blockIdx.x;
   const uint8_t* kb = keep + (size_t)b * nb * heads;
   int32_t* pb = perm + (size_t)b * nb;
@@ -278,7 +280,9 @@ extern "C" int oc_stream_compact(const uint8_t* keep, int batch, int num_blocks,
   OC_REQUIRE(batch >= 1 && num_blocks >= 0 && heads >= 1, OC_ERR_SHAPE,
              "oc_stream_compact: batch %d, num_blocks %d, heads %d", batch, num_blocks, heads);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  compact_kernel<<<batch, kScanThreads, 0, st>>>(keep, num_blocks, heads, perm, count);
+  const cudaError_t e = launch_pdl(compact_kernel, dim3(batch), dim3(kScanThreads), 0, st, keep, num_blocks, heads,
+                                   perm, count);
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "compact_kernel: %s", cudaGetErrorString(e));
   return check_launch("compact_kernel");
 }
 

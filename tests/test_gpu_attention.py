@@ -185,15 +185,25 @@ def _decode_step_cabi(q, k, v, tau, zmax):
     return keep, perm, count, out
 
 
-@pytest.mark.parametrize("nb,hq,hkv,evict", [(16, 8, 8, 0.5), (128, 32, 8, 0.75), (128, 32, 8, 0.9)])
-def test_decode_step_cabi_vs_oracle(nb, hq, hkv, evict):
-    """Config 0 (8/8 heads, 8K tokens) and config 1 (32/8, 64K tokens) at full size."""
+@pytest.mark.parametrize("nb,hq,hkv,evict,d,sq", [
+    (16, 8, 8, 0.5, 128, 1),     # config 0 (8/8 heads, 8K tokens)
+    (128, 32, 8, 0.75, 128, 1),  # config 1 (32/8, 64K tokens) at full size
+    (128, 32, 8, 0.9, 128, 1),
+    (24, 16, 4, 0.5, 64, 1),     # head_dim 64
+    (20, 16, 4, 0.6, 128, 2),    # two query rows x GQA 4: 8-row tiles
+    (12, 8, 8, 1.0, 128, 1),     # every block evicted: zeros
+    (1100, 2, 1, 0.5, 64, 1),    # more blocks than the in-kernel list holds: separate compaction
+])
+def test_decode_step_cabi_vs_oracle(nb, hq, hkv, evict, d, sq):
+    """The one-call decode step (scorer, compaction fused into the attention
+    prologue, attention, merge) against the oracle's mask, stable permutation,
+    count and attention."""
     from orthocache_b200 import synthetic as syn
     from gpu_util import assert_mask_parity
-    kinds = syn.block_kinds(nb, evict, seed=nb)
-    k = syn.make_keys(nb, hkv, 128, kinds, seed=nb)
-    v = syn.make_values(nb * 512, hkv, 128, seed=nb)
-    q = syn.make_queries(1, hq, 128, seed=nb)
+    kinds = syn.block_kinds(nb, min(evict, 0.99), seed=nb)
+    k = syn.make_keys(nb, hkv, d, kinds, seed=nb)
+    v = syn.make_values(nb * 512, hkv, d, seed=nb)
+    q = syn.make_queries(sq, hq, d, seed=nb)
     kf, qf, vf = host(k), host(q), host(v)
     r0 = O.score_blocks(qf, kf, -1e30, 5.0)
     tau, _ = syn.calibrate_tau(torch.tensor(r0["zeta"]), torch.tensor(r0["bound_max"]), 5.0, evict)
