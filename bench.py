@@ -160,8 +160,10 @@ class Engine:
         self.perm = torch.empty((nb,), dtype=torch.int32, device=device)
         self.count = torch.empty((1,), dtype=torch.int32, device=device)
         self.out = torch.empty((1, HQ, D), dtype=torch.bfloat16, device=device)
-        self.ws_bytes = _lib.query("oc_indirect_attention_workspace_bytes", 1, 1, HQ, HKV, D, 512, nb)
-        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
+        # one workspace for both paths: the decode step's (whose leading
+        # counters must start at zero) covers the partial attention's too
+        self.ws_bytes = _lib.query("oc_decode_step_workspace_bytes", 1, 1, HQ, HKV, D, S_SHARD)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=device)
         rows = HQ
         self.m = torch.empty((rows,), dtype=torch.float32, device=device)
         self.l = torch.empty((rows,), dtype=torch.float32, device=device)

@@ -20,6 +20,7 @@
 // Logits are kept in log2 units: s = (q.k) * log2(e) / sqrt(D), p = 2^(s - m).
 #include "oc_common.cuh"
 #include "oc_tma.cuh"
+#include "oc_mma.cuh"
 
 #include <math.h>
 
@@ -696,38 +697,6 @@ __device__ unsigned long long g_tstamp[4096][8];
 #define OC_STAMP(i) do {} while (0)
 #endif
 
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-// Byte offset of (token t, 16-byte chunk of channels c8) in a swizzled tile of
-// CH rows stored as D/64 boxes of 128-byte rows.
-template <int CH>
-__device__ __forceinline__ uint32_t swz(int t, int c8) {
-  return (uint32_t)((c8 >> 3) * (CH * 128) + t * 128 + (((c8 & 7) ^ (t & 7)) << 4));
-}
 
 // Union lists from the scorer's keep mask (the compaction of
 // compaction.py:28-100 folded into the attention prologue): every CTA
@@ -1430,8 +1399,11 @@ extern "C" int oc_merge_partials(const float* m, const float* l, const float* o,
 
 extern "C" size_t oc_decode_step_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
                                                  int head_dim, int seq_len) {
-  if (seq_len % 512) return 0;
-  return oc_indirect_attention_workspace_bytes(batch, q_len, q_heads, kv_heads, head_dim, 512, seq_len / 512);
+  if (seq_len % 512 || batch < 1 || kv_heads < 1) return 0;
+  // The fused layer's region first (its counters stay zero between calls),
+  // then the scratch of the separate score / attention path.
+  return oc::decode_fused_bytes(batch, seq_len, kv_heads) +
+         oc_indirect_attention_workspace_bytes(batch, q_len, q_heads, kv_heads, head_dim, 512, seq_len / 512);
 }
 
 extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int dtype,
@@ -1442,7 +1414,20 @@ extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int d
                               void* workspace, size_t workspace_bytes, oc_stream_t stream) {
   OC_REQUIRE(keep && perm && count && out, OC_ERR_NULL, "oc_decode_step: null output pointer");
   OC_REQUIRE(seq_len % 512 == 0, OC_ERR_SHAPE, "oc_decode_step: seq_len %d not a multiple of 512", seq_len);
+  OC_REQUIRE(batch >= 1 && kv_heads >= 1, OC_ERR_SHAPE, "oc_decode_step: batch/kv_heads < 1");
   const int nb = seq_len / 512;
+  const size_t fused_bytes = oc::decode_fused_bytes(batch, seq_len, kv_heads);
+  OC_REQUIRE(workspace && workspace_bytes >= fused_bytes, OC_ERR_CAPACITY,
+             "oc_decode_step: workspace of %zu bytes, need at least %zu", workspace_bytes, fused_bytes);
+  if (dtype == OC_BF16 && seq_len > 0) {
+    // One persistent kernel for the whole layer where the shape allows it.
+    const int frc = oc::decode_fused(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max,
+                                     keep, perm, count, out, out_dtype, workspace, fused_bytes,
+                                     reinterpret_cast<cudaStream_t>(stream));
+    if (frc != OC_ERR_UNSUPPORTED) return frc;
+  }
+  workspace = static_cast<uint8_t*>(workspace) + fused_bytes;
+  workspace_bytes -= fused_bytes;
   int rc = oc_score_blocks(k, q, dtype, batch, seq_len, kv_heads, head_dim, q_len, q_heads, 1, 64, 64, 256,
                            256, 512, tau, zeta_max, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
                            keep, 0, stream);

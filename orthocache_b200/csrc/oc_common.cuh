@@ -25,6 +25,17 @@ int device_sm_count();
 int score_status(int* status, int reset);
 int attn_status(int* status, int reset);
 
+// Fused decode layer (score, compact, attend and merge in one persistent
+// kernel; oc_score.cu).  decode_fused_bytes: workspace it needs, whose
+// leading counters must be zero before the first call (every call leaves them
+// zero).  decode_fused returns OC_ERR_UNSUPPORTED, without launching, for
+// shapes it does not cover (head_dim != 128, more than 8 query rows per KV
+// head, batch * kv_heads above the grid, workspace too small).
+size_t decode_fused_bytes(int batch, int seq_len, int kv_heads);
+int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
+                 int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
+                 void* out, int out_dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+
 #define OC_REQUIRE(cond, code, ...)                                   \
   do {                                                                \
     if (!(cond)) return ::oc::set_error((code), __VA_ARGS__);         \

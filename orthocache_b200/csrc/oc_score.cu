@@ -36,6 +36,7 @@
 // One CTA scores one (batch, block, kv-head) tile of 512 x D keys.
 #include "oc_common.cuh"
 #include "oc_tma.cuh"
+#include "oc_mma.cuh"
 
 #include <math.h>
 
@@ -391,15 +392,137 @@ __device__ int g_score_status = 0;
 
 #ifdef OC_TIMING
 // Diagnostic build only: per-CTA time stamps of the pipelined scorer.
-__device__ unsigned long long g_sstamp[1024][16];
+__device__ unsigned long long g_sstamp[1024][20];
 #define OC_SSTAMP(i, v) do { if (blockIdx.x < 1024) g_sstamp[blockIdx.x][i] = (v); } while (0)
 #else
 #define OC_SSTAMP(i, v) do {} while (0)
 #endif
 
-template <int D>
-__global__ void __launch_bounds__(kScoreThreads + kEpiWarps * 32, 1)
-score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_tiles) {
+// ---------------------------------------------------------------------------
+// Fused decode layer (score -> compact -> attend -> merge in one launch).
+//
+// The scorer kernel below, instantiated with FUSED = true, goes on from the
+// keep mask to the attention of pipeline.orthocache_forward(mode='compact')
+// (src/orthocache/pipeline.py:100-149): the union compaction of
+// compaction.py:65,76-82 and the online-softmax attention over the retained
+// blocks of adaptive_attention.py:46-76 / distributed_attention.py:95-128.
+//
+//  * Block decisions.  When the epilogue of tile (b, j, h) has its keep bit,
+//    it adds (1 + keep << 16) to blk_state[b, j].  The epilogue that brings
+//    the head count to H decides block j: if any head kept it, j is appended
+//    to queue[b] (slot = tail[b]++), then decided[b]++.  Blocks therefore
+//    enter the queue while the rest of the keys are still being scored.
+//  * Attention work.  CTA x serves group (b, h) = x mod (B * Hkv); its
+//    producer warp claims units (queue slot, 128-token chunk) from
+//    grp_ctr[group], waits (bounded) until the slot is published, and loads
+//    the chunk's K and V (64 KB) into the stage ring the scorer used.  The
+//    16 compute warps run QK^T and PV with m16n8k16 MMAs (warp = 16 tokens x
+//    64 value channels) and keep one online-softmax state per warp for the
+//    CTA's whole run, so each CTA emits one (m, l, o) partial per group row.
+//  * Merge.  The last CTA of a group to finish combines the group's
+//    partials in log-sum-exp form and writes the output rows.  The last CTA
+//    of the grid writes the stable active-first permutation and the count
+//    from blk_state and returns every counter to zero, so the state region
+//    of the workspace is zero again when the kernel ends.
+// ---------------------------------------------------------------------------
+constexpr int kFusedChunk = 128;           // tokens per attention unit
+constexpr int kFusedMaxRows = 8;           // query rows per KV head (Sq * G)
+constexpr int kFusedMaxGrid = 256;
+constexpr int kMergeRound = 20;            // partials per load round of a group merge
+constexpr int kFusedThreads = kScoreThreads + kEpiWarps * 32;
+
+struct FusedArgs {
+  int* blk_state;   // (B * nb): heads decided | heads kept << 16
+  int* queue;       // (B * nb): 1 + block index, in decision order
+  int* tail;        // (B)
+  int* decided;     // (B)
+  int* grp_ctr;     // (NG) next unit of group (b, h)
+  int* grp_done;    // (NG) CTAs of the group that published their partial
+  int* exit_ctr;    // (1)
+  float* part_m;    // (NG, cpg, kFusedMaxRows)
+  float* part_l;
+  float* part_o;    // (NG, cpg, kFusedMaxRows, D)
+  void* out;        // (B, Sq, Hq, D)
+  int out_bf16;
+  int32_t* perm;    // (B, nb)
+  int32_t* count;   // (B)
+  int NG, cpg, R;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Fused: every warp calls this once, with all 32 lanes, when it has no work
+// left.  The CTA's last warp counts the CTA out of the grid; the grid's last
+// CTA writes the permutation and counts and zeroes the state.
+// fence: order this warp's earlier global writes before the count-out (the
+// epilogue warps' counter updates; the compute warps' partials are already
+// released through the group count).
+__device__ __forceinline__ void fused_finish_warp(const ScoreArgs& a, const FusedArgs& f, int n_tiles,
+                                                  int* s_done_warps, bool fence) {
+  const int lane = threadIdx.x & 31;
+  if (fence) __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0 && atomicAdd(s_done_warps, 1) == kFusedThreads / 32 - 1)
+    last = atom_add_acq_rel(f.exit_ctr, 1) == (int)gridDim.x - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  const int B = n_tiles / (a.H * a.nb);
+  for (int b = 0; b < B; ++b) {
+    // compaction.py:76-82: active blocks ascending, then the others
+    // ascending.  256 blocks per sweep, their states loaded at once.
+    const int* st = f.blk_state + (size_t)b * a.nb;
+    int32_t* pm = f.perm + (size_t)b * a.nb;
+    int n_act = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+      int base = pass == 0 ? 0 : n_act;
+      for (int j0 = 0; j0 < a.nb; j0 += 256) {
+        int v[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int j = j0 + 32 * c + lane;
+          v[c] = j < a.nb ? __ldcg(st + j) : -1;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const bool take = v[c] >= 0 && ((v[c] >> 16) > 0) == (pass == 0);
+          const unsigned m = __ballot_sync(0xffffffffu, take);
+          if (take) pm[base + __popc(m & ((1u << lane) - 1u))] = j0 + 32 * c + lane;
+          base += __popc(m);
+        }
+      }
+      if (pass == 0) {
+        n_act = base;
+        if (lane == 0) f.count[b] = n_act;
+      }
+    }
+  }
+  __syncwarp();
+  for (int i = lane; i < B * a.nb; i += 32) { f.blk_state[i] = 0; f.queue[i] = 0; }
+  for (int i = lane; i < B; i += 32) { f.tail[i] = 0; f.decided[i] = 0; }
+  for (int i = lane; i < f.NG; i += 32) { f.grp_ctr[i] = 0; f.grp_done[i] = 0; }
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) *f.exit_ctr = 0;
+}
+
+template <int D, bool FUSED>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap amap_k,
+                 const __grid_constant__ CUtensorMap amap_v, ScoreArgs a, int n_tiles, FusedArgs f) {
   constexpr int PARTS = D / kSlabC;
   constexpr int kW = kScoreThreads / 32;  // 16 warps
   constexpr int NE = kEpiWarps;           // epilogue warps
@@ -408,6 +531,10 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   // 128-byte swizzled stages must start on a 1024-byte boundary.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full[kStages];
+  __shared__ __align__(8) uint64_t empty[kStages];  // fused: stage free for the producer
+  __shared__ int s_desc[kStages];            // fused: unit in a stage (block * 4 + chunk), -1 = end
+  __shared__ int s_done_warps;               // fused: warps finished (exit protocol)
+  __shared__ int s_merge;                    // fused: this CTA merges its group
   __shared__ int s_rel[kStages];             // warps done with a stage
   __shared__ __align__(8) uint64_t tfull[NBUF], tempty[NBUF];  // tile buffer hand-over
   __shared__ float s_grp[NBUF][kW][8];       // per-warp coefficient-group energies
@@ -454,10 +581,12 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
   };
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
+    for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); s_rel[i] = 0; }
     for (int i = 0; i < NBUF; ++i) { mbar_init(&tfull[i], kW); mbar_init(&tempty[i], 1); }
     fence_mbar_init();
     s_abort = 0;
+    s_done_warps = 0;
+    s_merge = 0;
     OC_SSTAMP(10, globaltimer_ns());
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
   }
@@ -502,10 +631,11 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     }
     for (int tile = e; tile < my_tiles; tile += NE) {
       const int tb = e;
-      if (!mbar_wait(&tfull[tb], (tile / NE) & 1)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[tb], (tile / NE) & 1))) {
         s_abort = 1;
         if (lane == 0) atomicExch(&g_score_status, 1);
-        return;
+        if constexpr (FUSED) break;
+        else return;
       }
       const int t = blockIdx.x + tile * gridDim.x;
       const int h = t % a.H;
@@ -609,12 +739,75 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
         if (a.e_high) a.e_high[cell] = e_hi;
         if (a.zeta) a.zeta[cell] = z;
         if (a.q && a.bound_max) a.bound_max[cell] = bmax;
-        if (a.keep) a.keep[cell] = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
+        const int kp = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
+        if (a.keep) a.keep[cell] = (uint8_t)kp;
+        if constexpr (FUSED) {
+          // Count this head in; the last head of the block decides it.
+          const int bj = b * a.nb + j;
+          const int old = atomicAdd(f.blk_state + bj, 1 + (kp << 16));
+          if ((old & 0xffff) == a.H - 1) {
+            if ((old >> 16) + kp > 0) st_release(f.queue + (size_t)b * a.nb + atomicAdd(f.tail + b, 1), j + 1);
+            __threadfence();
+            atomicAdd(f.decided + b, 1);
+          }
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[tb]);
     }
     if (lane == 0 && e == 0) OC_SSTAMP(4, globaltimer_ns());
+    if constexpr (FUSED) {
+      // The epilogue warp whose last tile comes earliest (tile my_tiles - NE)
+      // becomes the producer of the attention units: lane 0 feeds the stage
+      // ring once the scorer has released each stage for the last time.
+      if (e == my_tiles % NE) {
+        if (lane == 0) {
+          const int grp = blockIdx.x % f.NG, b = grp / a.H, h = grp % a.H;
+          const int* qb = f.queue + (size_t)b * a.nb;
+          // Per stage (bit s): used = a unit was put in the stage and its
+          // release is still to be awaited; phase = parity of that release
+          // on empty[s].
+          uint32_t used = (1u << (n_units < kStages ? n_units : kStages)) - 1u, phase = 0;
+          for (int k = n_units;; ++k) {
+            const int s = k % kStages;
+            if (used >> s & 1u) {
+              if (!mbar_wait(&empty[s], phase >> s & 1u)) { s_abort = 1; atomicExch(&g_score_status, 1); }
+              phase ^= 1u << s;
+            }
+            used |= 1u << s;
+            int desc = -1;
+            if (!s_abort) {
+              const int w = atomicAdd(f.grp_ctr + grp, 1);
+              const int slot = w / (kBlock / kFusedChunk), cc = w % (kBlock / kFusedChunk);
+              const uint64_t t0 = globaltimer_ns();
+              while (slot < a.nb) {
+                const int v = ld_acquire(qb + slot);
+                if (v > 0) { desc = (v - 1) * (kBlock / kFusedChunk) + cc; break; }
+                if (ld_acquire(f.decided + b) == a.nb && slot >= ld_acquire(f.tail + b)) break;
+                if (globaltimer_ns() - t0 > kWaitLimitNs) { s_abort = 1; atomicExch(&g_score_status, 1); break; }
+                __nanosleep(64);
+              }
+            }
+            s_desc[s] = desc;
+            if (k == n_units) OC_SSTAMP(15, globaltimer_ns());
+            if (desc < 0) {
+              mbar_arrive(&full[s]);  // end of the run: the consumers stop at this unit
+              break;
+            }
+            const int j = desc / (kBlock / kFusedChunk), cc = desc % (kBlock / kFusedChunk);
+            uint8_t* dst = smem + (size_t)s * kSlabB;
+            const int y = b * a.S + j * kBlock + cc * kFusedChunk;
+            mbar_expect_tx(&full[s], kSlabB);
+#pragma unroll
+            for (int jb = 0; jb < D / 64; ++jb) {
+              tma_load_2d(dst + jb * (kFusedChunk * 128), &amap_k, &full[s], h * D + jb * 64, y);
+              tma_load_2d(dst + kSlabB / 2 + jb * (kFusedChunk * 128), &amap_v, &full[s], h * D + jb * 64, y);
+            }
+          }
+        }
+      }
+      fused_finish_warp(a, f, n_tiles, &s_done_warps, true);
+    }
     return;
   }
 
@@ -627,25 +820,30 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
                             (uint32_t)((ch ^ (lane & 7)) << 4);
   for (int tile = 0; tile < my_tiles; ++tile) {
     const int tb = tile % NBUF;
-    if (tile >= NBUF && !mbar_wait(&tempty[tb], (tile / NBUF - 1) & 1)) {
+    if (tile >= NBUF && !__all_sync(0xffffffffu, mbar_wait(&tempty[tb], (tile / NBUF - 1) & 1))) {
       s_abort = 1;
       if (lane == 0) atomicExch(&g_score_status, 1);
-      return;
+      if constexpr (FUSED) goto scored;
+      else return;
     }
     float gacc = 0.f;  // this lane's share of the energy of coefficient group g
     for (int part = 0; part < PARTS; ++part) {
       const int k = tile * PARTS + part;
       const int stage = k % kStages;
       // A copy that never completes sets the abort flag: every warp stops
-      // waiting and leaves (there is no barrier left to meet).
-      if (s_abort) return;
+      // waiting and leaves (the fused kernel goes on to its end barriers).
+      if (__any_sync(0xffffffffu, s_abort)) {
+        if constexpr (FUSED) goto scored;
+        else return;
+      }
 #ifdef OC_TIMING
       const unsigned long long tw0 = globaltimer_ns();
 #endif
-      if (!mbar_wait(&full[stage], (k / kStages) & 1)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], (k / kStages) & 1))) {
         s_abort = 1;
         if (lane == 0) atomicExch(&g_score_status, 1);
-        return;
+        if constexpr (FUSED) goto scored;
+        else return;
       }
 #ifdef OC_TIMING
       const unsigned long long tw1 = globaltimer_ns();
@@ -664,12 +862,18 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
       if (lane == 0) {
         if (atomicAdd(&s_rel[stage], 1) == kW - 1) {
           s_rel[stage] = 0;
-          if (k + kStages < n_units && !s_abort) {
-            fence_proxy_async();
-            issue(k + kStages);
+          if (k + kStages < n_units) {
+            if (!s_abort) {
+              fence_proxy_async();
+              issue(k + kStages);
 #ifdef OC_TIMING
-            s_trel += globaltimer_ns() - s_tarr[stage];
+              s_trel += globaltimer_ns() - s_tarr[stage];
 #endif
+            }
+          } else if constexpr (FUSED) {
+            // Last scoring use of this stage: hand it to the producer.
+            fence_proxy_async();
+            mbar_arrive(&empty[stage]);
           }
         }
       }
@@ -729,6 +933,185 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, ScoreArgs a, int n_ti
     OC_SSTAMP(7, n_units);
   }
 #endif
+scored:
+  if constexpr (FUSED) {
+    static_assert(!FUSED || D == 128, "the fused decode layer is built for head_dim 128");
+    // ---- attention over the retained blocks of group (bq, hq) ----
+    const int grp = blockIdx.x % f.NG, bq = grp / a.H, hq = grp % a.H;
+    const int tg = warp & 7;    // tokens 16 tg .. 16 tg + 15 of each unit
+    const int chh = warp >> 3;  // value channels 64 chh .. 64 chh + 63
+    // A fragments of Q: row g of the tile is query row g of KV head hq
+    // (adaptive_attention.py:60-70 with GQA rows s * G + gq); rows 8..15 and
+    // rows >= R are zero.
+    uint32_t qa[D / 16][2];
+    {
+      const uint32_t* qrow = nullptr;
+      if (g < f.R) {
+        const int s = g / a.G, gq = g - s * a.G;
+        qrow = reinterpret_cast<const uint32_t*>(reinterpret_cast<const __nv_bfloat16*>(a.q) +
+                                                 (((size_t)bq * a.Sq + s) * a.Hq + (size_t)hq * a.G + gq) * D);
+      }
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        qa[ks][0] = qrow ? qrow[8 * ks + c4] : 0u;      // channels 16 ks + 2 c4, +1
+        qa[ks][1] = qrow ? qrow[8 * ks + 4 + c4] : 0u;  // channels 16 ks + 8 + 2 c4, +1
+      }
+    }
+    // Online softmax (log2 units) of this warp's tokens, row g:
+    // running max, this lane's share of the sum, output channels
+    // 64 chh + 8 nt + 2 c4, +1.
+    if (tid == 0) OC_SSTAMP(11, globaltimer_ns());
+    float m_run = -INFINITY, l_run = 0.f;
+    float o[8][2];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = 0.f;
+    const int mm = lane >> 3, rr = lane & 7;
+    for (int k = n_units;; ++k) {
+      const int stage = k % kStages;
+      if (__any_sync(0xffffffffu, s_abort)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], (k / kStages) & 1))) {
+        s_abort = 1;
+        if (lane == 0) atomicExch(&g_score_status, 1);
+        break;
+      }
+      if (s_desc[stage] < 0) break;
+      if (tid == 0 && k == n_units) OC_SSTAMP(12, globaltimer_ns());
+      const uint32_t kbase = smem_u32(smem + (size_t)stage * kSlabB), vbase = kbase + kSlabB / 2;
+      // S = Q K^T for tokens 16 tg + (0..7 | 8..15)
+      float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t kb[4];
+        ldsm_x4(kb, kbase + swz<kFusedChunk>(16 * tg + 8 * (mm >> 1) + rr, 2 * ks + (mm & 1)));
+        const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+        mma_bf16_16816(sa[0], af, kb[0], kb[1]);
+        mma_bf16_16816(sa[1], af, kb[2], kb[3]);
+      }
+      // V fragments of the warp's 16 tokens and 64 channels, then release.
+      uint32_t vb[4][4];
+#pragma unroll
+      for (int np = 0; np < 4; ++np)
+        ldsm_x4_t(vb[np], vbase + swz<kFusedChunk>(16 * tg + 8 * (mm & 1) + rr, 2 * (4 * chh + np) + (mm >> 1)));
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0 && atomicAdd(&s_rel[stage], 1) == kW - 1) {
+        s_rel[stage] = 0;
+        fence_proxy_async();
+        mbar_arrive(&empty[stage]);
+      }
+      const float x0 = sa[0][0] * f.scale_log2, x1 = sa[0][1] * f.scale_log2;
+      const float x2 = sa[1][0] * f.scale_log2, x3 = sa[1][1] * f.scale_log2;
+      float mx = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - mn);
+      const float p0 = exp2f(x0 - mn), p1 = exp2f(x1 - mn), p2 = exp2f(x2 - mn), p3 = exp2f(x3 - mn);
+      l_run = fmaf(l_run, alpha, (p0 + p1) + (p2 + p3));
+      m_run = mn;
+      const uint32_t pa[4] = {pack_bf16x2(p0, p1), 0u, pack_bf16x2(p2, p3), 0u};
+#pragma unroll
+      for (int np = 0; np < 4; ++np)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float d[4] = {o[2 * np + e][0] * alpha, o[2 * np + e][1] * alpha, 0.f, 0.f};
+          mma_bf16_16816(d, pa, vb[np][2 * e], vb[np][2 * e + 1]);
+          o[2 * np + e][0] = d[0];
+          o[2 * np + e][1] = d[1];
+        }
+    }
+    if (tid == 0) OC_SSTAMP(13, globaltimer_ns());
+    float l = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    // Combine the 16 warp states into the CTA's partial (the ring is idle:
+    // every issued unit has been consumed and nothing more is issued).
+    asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+    float* cm = reinterpret_cast<float*>(smem);  // [kW][8] max
+    float* cl = cm + kW * 8;                     // [kW][8] sum
+    float* co = cl + kW * 8;                     // [kW][8][64] output
+    if (c4 == 0) { cm[warp * 8 + g] = m_run; cl[warp * 8 + g] = l; }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      co[(warp * 8 + g) * 64 + 8 * nt + 2 * c4] = o[nt][0];
+      co[(warp * 8 + g) * 64 + 8 * nt + 2 * c4 + 1] = o[nt][1];
+    }
+    asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+    const size_t pbase = (size_t)grp * f.cpg + blockIdx.x / f.NG;
+    for (int x = tid; x < f.R * D; x += kScoreThreads) {
+      const int r = x / D, d = x - r * D, hh = d >> 6, dl = d & 63;
+      float M = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) M = fmaxf(M, cm[(hh * 8 + t) * 8 + r]);
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const int w = hh * 8 + t;
+          const float wt = exp2f(cm[w * 8 + r] - M);
+          L = fmaf(cl[w * 8 + r], wt, L);
+          O = fmaf(co[(w * 8 + r) * 64 + dl], wt, O);
+        }
+      f.part_o[(pbase * kFusedMaxRows + r) * D + d] = O;
+      if (d == 0) { f.part_m[pbase * kFusedMaxRows + r] = M; f.part_l[pbase * kFusedMaxRows + r] = L; }
+    }
+    asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+    const int n_grp = ((int)gridDim.x - 1 - grp) / f.NG + 1;  // CTAs serving this group
+    if (tid == 0) {
+      // Release: the CTA's partial (ordered before by the barrier) is
+      // visible to whichever CTA sees the last count.
+      s_merge = atom_add_acq_rel(f.grp_done + grp, 1) == n_grp - 1;
+      OC_SSTAMP(16, s_merge);
+      OC_SSTAMP(17, globaltimer_ns());
+    }
+    asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+    const bool merge = s_merge;
+    // Done with every counter: count the warp out now, so the grid's last
+    // CTA can reset the state while the merges run.
+    fused_finish_warp(a, f, n_tiles, &s_done_warps, false);
+    if (merge) {
+      // Last CTA of the group: log-sum-exp merge of its n_grp partials, o / l
+      // (adaptive_attention.py:72-76; zeros when no block is retained,
+      // indirect_attention.py:150-151).  kMergeRound partials per round,
+      // their loads issued together.
+      const size_t g0 = (size_t)grp * f.cpg;
+      for (int x = tid; x < f.R * D; x += kScoreThreads) {
+        const int r = x / D, d = x - r * D;
+        float M = -INFINITY, L = 0.f, O = 0.f;
+        for (int i0 = 0; i0 < n_grp; i0 += kMergeRound) {
+          float mv[kMergeRound], lv[kMergeRound], ov[kMergeRound];
+#pragma unroll
+          for (int u = 0; u < kMergeRound; ++u) {
+            const size_t pr = (g0 + i0 + u) * kFusedMaxRows + r;
+            const bool in = i0 + u < n_grp;
+            mv[u] = in ? __ldcg(f.part_m + pr) : -INFINITY;
+            lv[u] = in ? __ldcg(f.part_l + pr) : 0.f;
+            ov[u] = in ? __ldcg(f.part_o + pr * D + d) : 0.f;
+          }
+          float mc = M;
+#pragma unroll
+          for (int u = 0; u < kMergeRound; ++u) mc = fmaxf(mc, mv[u]);
+          if (mc != -INFINITY) {
+            const float sc = exp2f(M - mc);
+            L *= sc;
+            O *= sc;
+#pragma unroll
+            for (int u = 0; u < kMergeRound; ++u) {
+              const float w = exp2f(mv[u] - mc);
+              L = fmaf(lv[u], w, L);
+              O = fmaf(ov[u], w, O);
+            }
+            M = mc;
+          }
+        }
+        const float y = L > 0.f ? O / L : 0.f;
+        const int s = r / a.G, gq = r - s * a.G;
+        const size_t orow = ((size_t)bq * a.Sq + s) * a.Hq + (size_t)hq * a.G + gq;
+        if (f.out_bf16) reinterpret_cast<__nv_bfloat16*>(f.out)[orow * D + d] = __float2bfloat16_rn(y);
+        else reinterpret_cast<float*>(f.out)[orow * D + d] = y;
+      }
+    }
+    if (tid == 0) OC_SSTAMP(14, globaltimer_ns());
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -843,25 +1226,46 @@ bool bands_partial_ok(const Bands& bd) {
   return true;
 }
 
+// Keys viewed as (channel, i_hi, i_lo, block) with token = 512 block +
+// 64 i_hi + i_lo, so that a box lands in shared memory i_hi fastest.
+int encode_score_map(CUtensorMap* map, const void* keys, int H, int D, int64_t blocks) {
+  const uint64_t cols = (uint64_t)H * D, row_b = cols * 2;
+  const uint64_t dims[4] = {cols, 8, 64, (uint64_t)blocks};
+  const uint64_t strides[3] = {64 * row_b, row_b, (uint64_t)kBlock * row_b};
+  const uint32_t box[4] = {(uint32_t)kSlabC, 8, 32, 1};
+  return encode_map_4d(map, keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, box, true);
+}
+
 template <int D>
 int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   CUtensorMap map;
-  // Keys viewed as (channel, i_hi, i_lo, block) with token = 512 block +
-  // 64 i_hi + i_lo, so that a box lands in shared memory i_hi fastest.
-  const uint64_t cols = (uint64_t)a.H * D, row_b = cols * 2;
-  const uint64_t blocks = (uint64_t)ntiles / a.H;  // B * nb
-  const uint64_t dims[4] = {cols, 8, 64, blocks};
-  const uint64_t strides[3] = {64 * row_b, row_b, (uint64_t)kBlock * row_b};
-  const uint32_t box[4] = {(uint32_t)kSlabC, 8, 32, 1};
-  int rc = encode_map_4d(&map, a.keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, box, true);
+  int rc = encode_score_map(&map, a.keys, a.H, D, ntiles / a.H);
   if (rc) return set_error(OC_ERR_CUDA, "oc_score_blocks: tensor map encode failed (%d)", rc);
   const int smem = kStages * kSlabB + kQCacheBytes + 1024;
-  cudaFuncSetAttribute(score_tma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(score_tma_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
-  const cudaError_t e = launch_pdl(score_tma_kernel<D>, dim3(grid), dim3(kScoreThreads + kEpiWarps * 32), smem, st,
-                                   map, a, ntiles);
+  const FusedArgs none = {};
+  const cudaError_t e = launch_pdl(score_tma_kernel<D, false>, dim3(grid), dim3(kScoreThreads + kEpiWarps * 32),
+                                   smem, st, map, map, map, a, ntiles, none);
   if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "score_tma_kernel: %s", cudaGetErrorString(e));
   return check_launch("score_tma_kernel");
+}
+
+// Workspace of the fused decode layer: int32 counters (zero between calls),
+// then the per-CTA partials.
+struct FusedLayout {
+  size_t counters, bytes;
+  int NG, cpg;
+};
+FusedLayout fused_layout(int B, int nb, int Hkv) {
+  FusedLayout L;
+  L.NG = B * Hkv;
+  L.cpg = (kFusedMaxGrid + L.NG - 1) / L.NG;
+  const size_t ints = 2 * (size_t)B * nb + 2 * (size_t)B + 2 * (size_t)L.NG + 1;
+  L.counters = (ints * 4 + 255) / 256 * 256;
+  const size_t parts = (size_t)L.NG * L.cpg * kFusedMaxRows;
+  L.bytes = L.counters + ((parts * 2 + parts * 128) * 4 + 255) / 256 * 256;
+  return L;
 }
 
 template <typename T>
@@ -977,6 +1381,69 @@ int score_status(int* status, int reset) {
 
 #ifdef OC_TIMING
 extern "C" int oc_probe_read_score_stamps(unsigned long long* host, int n) {
-  return (int)cudaMemcpyFromSymbol(host, oc::g_sstamp, sizeof(unsigned long long) * 16 * n);
+  return (int)cudaMemcpyFromSymbol(host, oc::g_sstamp, sizeof(unsigned long long) * 20 * n);
 }
 #endif
+
+// ---------------------------------------------------------------------------
+// Fused decode layer: host side.
+// ---------------------------------------------------------------------------
+namespace oc {
+
+size_t decode_fused_bytes(int batch, int seq_len, int kv_heads) {
+  return fused_layout(batch, seq_len / kBlock, kv_heads).bytes;
+}
+
+int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
+                 int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
+                 void* out, int out_dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (head_dim != 128 || !q || q_len < 1 || kv_heads < 1 || q_heads % kv_heads) return OC_ERR_UNSUPPORTED;
+  const int G = q_heads / kv_heads, R = q_len * G, nb = seq_len / kBlock;
+  if (R > kFusedMaxRows || nb < 1 || nb > 0xffff || kv_heads > 0xffff) return OC_ERR_UNSUPPORTED;
+  if (out_dtype != OC_BF16 && out_dtype != OC_F32) return OC_ERR_UNSUPPORTED;
+  const FusedLayout L = fused_layout(batch, nb, kv_heads);
+  const int64_t ntiles = (int64_t)batch * nb * kv_heads;
+  int grid = device_sm_count();
+  if (grid > kFusedMaxGrid) grid = kFusedMaxGrid;
+  if (ntiles < grid) grid = (int)ntiles;
+  if (L.NG > grid || !ws || ws_bytes < L.bytes) return OC_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return OC_ERR_UNSUPPORTED;
+
+  ScoreArgs a = {};
+  a.keys = k; a.q = q; a.S = seq_len; a.H = kv_heads; a.D = head_dim; a.nb = nb;
+  a.Sq = q_len; a.Hq = q_heads; a.G = G;
+  a.bands = Bands{{1, 64, 256}, {64, 256, kBlock}};
+  a.tau = tau; a.zeta_max = zeta_max; a.keep = keep;
+  FusedArgs f = {};
+  int* c = reinterpret_cast<int*>(ws);
+  f.blk_state = c; c += (size_t)batch * nb;
+  f.queue = c; c += (size_t)batch * nb;
+  f.tail = c; c += batch;
+  f.decided = c; c += batch;
+  f.grp_ctr = c; c += L.NG;
+  f.grp_done = c; c += L.NG;
+  f.exit_ctr = c;
+  float* pf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + L.counters);
+  const size_t parts = (size_t)L.NG * L.cpg * kFusedMaxRows;
+  f.part_m = pf; f.part_l = pf + parts; f.part_o = pf + 2 * parts;
+  f.out = out; f.out_bf16 = out_dtype == OC_BF16;
+  f.perm = perm; f.count = count;
+  f.NG = L.NG; f.cpg = L.cpg; f.R = R;
+  f.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+
+  CUtensorMap km, ak, av;
+  int rc = encode_score_map(&km, k, kv_heads, 128, (int64_t)batch * nb);
+  const uint64_t cols = (uint64_t)kv_heads * 128, rows = (uint64_t)batch * seq_len;
+  if (!rc) rc = encode_map_2d(&ak, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true);
+  if (!rc) rc = encode_map_2d(&av, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true);
+  if (rc) return set_error(OC_ERR_CUDA, "oc_decode_step: tensor map encode failed (%d)", rc);
+  const int smem = kStages * kSlabB + kQCacheBytes + 1024;
+  cudaFuncSetAttribute(score_tma_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const cudaError_t e = launch_pdl(score_tma_kernel<128, true>, dim3(grid), dim3(kFusedThreads), smem, st, km, ak,
+                                   av, a, (int)ntiles, f);
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "score_tma_kernel (fused): %s", cudaGetErrorString(e));
+  return check_launch("score_tma_kernel (fused)");
+}
+
+}  // namespace oc

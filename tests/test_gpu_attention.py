@@ -175,7 +175,7 @@ def _decode_step_cabi(q, k, v, tau, zmax):
     count = torch.empty((1,), dtype=torch.int32, device="cuda")
     out = torch.empty((Sq, Hq, D), dtype=torch.bfloat16, device="cuda")
     ws_bytes = lib.oc_decode_step_workspace_bytes(1, Sq, Hq, Hkv, D, S)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")  # zero before first use
     rc = lib.oc_decode_step(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 1, Sq, Hq, Hkv, D, S,
                             ctypes.c_float(tau), ctypes.c_float(zmax), keep.data_ptr(), perm.data_ptr(),
                             count.data_ptr(), out.data_ptr(), 1, ws.data_ptr(), ws_bytes,
