@@ -43,6 +43,10 @@ S_SHARD, HQ, HKV, D = 65536, 32, 8, 128
 ZETA_MAX = 5.0
 LAYERS = 4
 FALLBACK_HBM = 6650.0
+# DRAM bytes read + written by one launch of the fused decode-layer kernel at
+# this workload (75 % eviction), from the ncu capture summarised in
+# profiles/decode_fused_config1.md.
+FUSED_TRAFFIC = 194310144
 
 
 def parse():
@@ -171,9 +175,10 @@ class Engine:
         self.gm = torch.empty((world, rows), dtype=torch.float32, device=device)
         self.gl = torch.empty((world, rows), dtype=torch.float32, device=device)
         self.go = torch.empty((world, rows, D), dtype=torch.float32, device=device)
-        # our kernels per layer: scorer, attention (compaction fused), merge;
-        # sequence-parallel: scorer, compaction, attention, run merge, shard merge
-        self.launches_per_step = 3 if world == 1 else 5
+        # our kernels per layer: one (the fused decode layer: score, block
+        # decisions, attention, merge); sequence-parallel: scorer, compaction,
+        # attention, run merge, shard merge
+        self.launches_per_step = 1 if world == 1 else 5
 
     @property
     def stream(self):
@@ -359,7 +364,10 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         barrier()
     ms = start.elapsed_time(stop) / K
-    # Scorer launch duration (the roofline kernel): CUDA events bracketing
+    # Launch durations: CUDA events bracketing each launch on the launching
+    # stream, eager, inputs rotating past L2.  The scorer alone (oc_score_blocks)
+    # and the whole layer (oc_decode_step: at N = 1 a single launch of the
+    # fused kernel, the roofline kernel).
     # each launch on the launching stream, eager, inputs rotating past L2.
     Kb = max(LAYERS, min(K, 400))
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(Kb)]
@@ -432,10 +440,21 @@ def run_ours(args, rank, world, local_rank):
                                "(%d total), evict=%.2f, zeta_max=5" % (S_SHARD, S_SHARD * world, args.evict),
                    "l2": "inputs > L2: 4 layers of KV (1.07 GB) rotate per step",
                    "parallelism": "single GPU" if world == 1 else f"sequence-parallel x{world}, LSE merge"},
-        "roofline": {"bound": "hbm", "kernel": "score_tma_kernel (fused scorer)",
-                     "achieved": round(score_gbs, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(score_gbs / hbm, 4), "traffic": None, "peak_kind": peak_kind,
-                     "bytes_per_launch": k_bytes},
+        "roofline": ({"bound": "hbm", "kernel": "score_tma_kernel<128,true> (fused decode layer)",
+                      "achieved": round(alg_bytes / (t_step_eager * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                      "frac": round(alg_bytes / (t_step_eager * 1e-3) / 1e9 / hbm, 4),
+                      "traffic": FUSED_TRAFFIC if abs(args.evict - 0.75) < 1e-9 else None,
+                      "peak_kind": peak_kind, "bytes_per_launch": int(alg_bytes),
+                      "how": "algorithmic bytes |K| + kept/nb (|K|+|V|) over the median CUDA-event time of "
+                             "eager oc_decode_step launches; traffic = dram bytes read+written per launch "
+                             "from the ncu capture in profiles/"} if world == 1 else
+                     {"bound": "hbm", "kernel": "score_tma_kernel<128,false> (scorer)",
+                      "achieved": round(score_gbs, 1), "peak": hbm, "unit": "GB/s",
+                      "frac": round(score_gbs / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+                      "bytes_per_launch": k_bytes}),
+        "scorer_roofline": {"kernel": "score_tma_kernel<128,false> (oc_score_blocks alone)",
+                            "achieved": round(score_gbs, 1), "frac": round(score_gbs / hbm, 4),
+                            "bytes_per_launch": k_bytes},
         "step_roofline": {"alg_bytes": int(alg_bytes), "achieved_gbs": round(alg_bytes / (ms * 1e-3) / 1e9, 1),
                           "frac": round(alg_bytes / (ms * 1e-3) / 1e9 / hbm, 4)},
         "kernel_us": {"score": round(t_score * 1e3, 2), "step_eager": round(t_step_eager * 1e3, 2),

@@ -244,6 +244,20 @@ int oc_indirect_attention_noalloc(const void* q, const void* k, const void* v, i
  * copy of compact_and_attend (compaction.py:157-222).
  * Shapes as above; keep (B, nb, Hkv) uint8, perm (B, nb), count (B) are
  * outputs; out (B, Sq, Hq, D) in out_dtype.
+ *
+ * bfloat16 with head_dim 128, Sq * (Hq / Hkv) <= 8 query rows per KV head and
+ * B * Hkv <= the number of SMs runs as ONE persistent kernel: the scorer
+ * decides each block as soon as its Hkv tiles are scored, and the same CTAs
+ * then stream K and V of the retained blocks and merge the attention in
+ * log-sum-exp form.  Other shapes run the scorer, the compaction and the
+ * split-KV attention as separate kernels.
+ *
+ * Workspace: oc_decode_step_workspace_bytes() bytes, 256-byte aligned, and
+ * ZERO-FILLED before its first use (cudaMemset once).  Its leading region
+ * holds an epoch and two counter sets that the one-kernel path keeps
+ * consistent from call to call, so later calls need no clearing.  Calls that
+ * share a workspace must not overlap on the GPU.  If oc_device_status()
+ * reports a wait that gave up, zero the workspace again.
  */
 size_t oc_decode_step_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
                                       int head_dim, int seq_len);

@@ -26,9 +26,9 @@ int score_status(int* status, int reset);
 int attn_status(int* status, int reset);
 
 // Fused decode layer (score, compact, attend and merge in one persistent
-// kernel; oc_score.cu).  decode_fused_bytes: workspace it needs, whose
-// leading counters must be zero before the first call (every call leaves them
-// zero).  decode_fused returns OC_ERR_UNSUPPORTED, without launching, for
+// kernel; oc_score.cu).  decode_fused_bytes: workspace it needs; it must be
+// zero-filled before the first call, after which calls keep its epoch and
+// counter sets consistent.  decode_fused returns OC_ERR_UNSUPPORTED, without launching, for
 // shapes it does not cover (head_dim != 128, more than 8 query rows per KV
 // head, batch * kv_heads above the grid, workspace too small).
 size_t decode_fused_bytes(int batch, int seq_len, int kv_heads);

@@ -420,10 +420,14 @@ __device__ unsigned long long g_sstamp[1024][20];
 //    64 value channels) and keep one online-softmax state per warp for the
 //    CTA's whole run, so each CTA emits one (m, l, o) partial per group row.
 //  * Merge.  The last CTA of a group to finish combines the group's
-//    partials in log-sum-exp form and writes the output rows.  The last CTA
-//    of the grid writes the stable active-first permutation and the count
-//    from blk_state and returns every counter to zero, so the state region
-//    of the workspace is zero again when the kernel ends.
+//    partials in log-sum-exp form and writes the output rows.  The epilogue
+//    that completes a batch row's decisions writes that row's stable
+//    active-first permutation and count from blk_state, long before the
+//    attention ends.
+//  * Counters.  The workspace holds an epoch and two counter sets; a call
+//    uses set (epoch & 1), CTA 0 clears the other set for the next call, and
+//    the last row decision advances the epoch.  No CTA waits for the grid to
+//    finish, so the kernel ends with the last group merge.
 // ---------------------------------------------------------------------------
 constexpr int kFusedChunk = 128;           // tokens per attention unit
 constexpr int kFusedMaxRows = 8;           // query rows per KV head (Sq * G)
@@ -432,13 +436,9 @@ constexpr int kMergeRound = 20;            // partials per load round of a group
 constexpr int kFusedThreads = kScoreThreads + kEpiWarps * 32;
 
 struct FusedArgs {
-  int* blk_state;   // (B * nb): heads decided | heads kept << 16
-  int* queue;       // (B * nb): 1 + block index, in decision order
-  int* tail;        // (B)
-  int* decided;     // (B)
-  int* grp_ctr;     // (NG) next unit of group (b, h)
-  int* grp_done;    // (NG) CTAs of the group that published their partial
-  int* exit_ctr;    // (1)
+  int* epoch;       // calls so far; counter set (epoch & 1) serves this call
+  int* sets;        // two counter sets of set_ints ints (FusedSet layout)
+  int set_ints;
   float* part_m;    // (NG, cpg, kFusedMaxRows)
   float* part_l;
   float* part_o;    // (NG, cpg, kFusedMaxRows, D)
@@ -446,9 +446,33 @@ struct FusedArgs {
   int out_bf16;
   int32_t* perm;    // (B, nb)
   int32_t* count;   // (B)
-  int NG, cpg, R;
+  int B, NG, cpg, R;
   float scale_log2;
 };
+
+// One call's counters.  A call uses set (epoch & 1); CTA 0 zeroes the other
+// set when it starts (the call before, its last user, has completed), so the
+// set is zero when the next call picks it up.
+struct FusedSet {
+  int* blk_state;    // (B * nb): heads decided | heads kept << 16
+  int* queue;        // (B * nb): 1 + block index, in decision order
+  int* row;          // (B) blocks decided | blocks kept (queue tail) << 16
+  int* decided_all;  // (1) batch rows fully decided
+  int* grp_ctr;      // (NG) next unit of group (b, h)
+  int* grp_done;     // (NG) CTAs of the group that published their partial
+};
+__host__ __device__ __forceinline__ int fused_set_ints(int B, int nb, int NG) { return 2 * B * nb + B + 1 + 2 * NG; }
+__device__ __forceinline__ FusedSet fused_set(const FusedArgs& f, int nb, int which) {
+  FusedSet t;
+  int* c = f.sets + (size_t)which * f.set_ints;
+  t.blk_state = c; c += (size_t)f.B * nb;
+  t.queue = c; c += (size_t)f.B * nb;
+  t.row = c; c += f.B;
+  t.decided_all = c; c += 1;
+  t.grp_ctr = c; c += f.NG;
+  t.grp_done = c;
+  return t;
+}
 
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -457,6 +481,11 @@ __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   int old;
   asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
+}
+__device__ __forceinline__ int ld_relaxed(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
@@ -467,56 +496,33 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 // Fused: every warp calls this once, with all 32 lanes, when it has no work
 // left.  The CTA's last warp counts the CTA out of the grid; the grid's last
 // CTA writes the permutation and counts and zeroes the state.
-// fence: order this warp's earlier global writes before the count-out (the
-// epilogue warps' counter updates; the compute warps' partials are already
-// released through the group count).
-__device__ __forceinline__ void fused_finish_warp(const ScoreArgs& a, const FusedArgs& f, int n_tiles,
-                                                  int* s_done_warps, bool fence) {
-  const int lane = threadIdx.x & 31;
-  if (fence) __threadfence();
-  __syncwarp();
-  int last = 0;
-  if (lane == 0 && atomicAdd(s_done_warps, 1) == kFusedThreads / 32 - 1)
-    last = atom_add_acq_rel(f.exit_ctr, 1) == (int)gridDim.x - 1;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
-  const int B = n_tiles / (a.H * a.nb);
-  for (int b = 0; b < B; ++b) {
-    // compaction.py:76-82: active blocks ascending, then the others
-    // ascending.  256 blocks per sweep, their states loaded at once.
-    const int* st = f.blk_state + (size_t)b * a.nb;
-    int32_t* pm = f.perm + (size_t)b * a.nb;
-    int n_act = 0;
-    for (int pass = 0; pass < 2; ++pass) {
-      int base = pass == 0 ? 0 : n_act;
-      for (int j0 = 0; j0 < a.nb; j0 += 256) {
-        int v[8];
+// Stable active-first permutation and count of batch row b from the final
+// block states (compaction.py:76-82: active blocks ascending, then the others
+// ascending); one warp, 256 blocks per sweep with their states loaded at once.
+__device__ __forceinline__ void fused_write_perm(const int* st, int nb, int32_t* perm, int32_t* count, int lane) {
+  int n_act = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    int base = pass == 0 ? 0 : n_act;
+    for (int j0 = 0; j0 < nb; j0 += 256) {
+      int v[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int j = j0 + 32 * c + lane;
-          v[c] = j < a.nb ? __ldcg(st + j) : -1;
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const bool take = v[c] >= 0 && ((v[c] >> 16) > 0) == (pass == 0);
-          const unsigned m = __ballot_sync(0xffffffffu, take);
-          if (take) pm[base + __popc(m & ((1u << lane) - 1u))] = j0 + 32 * c + lane;
-          base += __popc(m);
-        }
+      for (int c = 0; c < 8; ++c) {
+        const int j = j0 + 32 * c + lane;
+        v[c] = j < nb ? __ldcg(st + j) : -1;
       }
-      if (pass == 0) {
-        n_act = base;
-        if (lane == 0) f.count[b] = n_act;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const bool take = v[c] >= 0 && ((v[c] >> 16) > 0) == (pass == 0);
+        const unsigned m = __ballot_sync(0xffffffffu, take);
+        if (take) perm[base + __popc(m & ((1u << lane) - 1u))] = j0 + 32 * c + lane;
+        base += __popc(m);
       }
     }
+    if (pass == 0) {
+      n_act = base;
+      if (lane == 0) *count = n_act;
+    }
   }
-  __syncwarp();
-  for (int i = lane; i < B * a.nb; i += 32) { f.blk_state[i] = 0; f.queue[i] = 0; }
-  for (int i = lane; i < B; i += 32) { f.tail[i] = 0; f.decided[i] = 0; }
-  for (int i = lane; i < f.NG; i += 32) { f.grp_ctr[i] = 0; f.grp_done[i] = 0; }
-  __threadfence();
-  __syncwarp();
-  if (lane == 0) *f.exit_ctr = 0;
 }
 
 template <int D, bool FUSED>
@@ -533,7 +539,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   __shared__ __align__(8) uint64_t full[kStages];
   __shared__ __align__(8) uint64_t empty[kStages];  // fused: stage free for the producer
   __shared__ int s_desc[kStages];            // fused: unit in a stage (block * 4 + chunk), -1 = end
-  __shared__ int s_done_warps;               // fused: warps finished (exit protocol)
+  __shared__ int s_set;                      // fused: counter set of this call
   __shared__ int s_merge;                    // fused: this CTA merges its group
   __shared__ int s_rel[kStages];             // warps done with a stage
   __shared__ __align__(8) uint64_t tfull[NBUF], tempty[NBUF];  // tile buffer hand-over
@@ -585,7 +591,6 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     for (int i = 0; i < NBUF; ++i) { mbar_init(&tfull[i], kW); mbar_init(&tempty[i], 1); }
     fence_mbar_init();
     s_abort = 0;
-    s_done_warps = 0;
     s_merge = 0;
     OC_SSTAMP(10, globaltimer_ns());
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
@@ -596,10 +601,21 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   pdl_wait();
   if (tid == 0) {
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
+    if constexpr (FUSED) s_set = __ldcg(f.epoch) & 1;
     OC_SSTAMP(8, globaltimer_ns());
   }
   __syncthreads();  // the only CTA-wide barrier
   if (tid == 0) OC_SSTAMP(1, globaltimer_ns());
+  FusedSet fs = {};
+  if constexpr (FUSED) {
+    fs = fused_set(f, a.nb, s_set);
+    if (blockIdx.x == 0) {
+      // The other set was last used by the previous call, which has
+      // completed: clear it for the next call.
+      int* other = f.sets + (size_t)(s_set ^ 1) * f.set_ints;
+      for (int i = tid; i < f.set_ints; i += kFusedThreads) other[i] = 0;
+    }
+  }
 #ifdef OC_TIMING
   unsigned long long t_wait = 0;
 #endif
@@ -732,6 +748,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         }
         bmax = warp_max(bound);
       }
+      int row_done = 0;  // fused: this epilogue completed batch row b's decisions
       if (lane == 0) {
         const float z = e_hi / (e_lo + 1e-6f);
         if (a.e_low) a.e_low[cell] = e_lo;
@@ -744,11 +761,28 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         if constexpr (FUSED) {
           // Count this head in; the last head of the block decides it.
           const int bj = b * a.nb + j;
-          const int old = atomicAdd(f.blk_state + bj, 1 + (kp << 16));
+          const int old = atomicAdd(fs.blk_state + bj, 1 + (kp << 16));
           if ((old & 0xffff) == a.H - 1) {
-            if ((old >> 16) + kp > 0) st_release(f.queue + (size_t)b * a.nb + atomicAdd(f.tail + b, 1), j + 1);
+            // One word per batch row counts decided and kept blocks; a kept
+            // block's queue slot is the kept count before it.
+            const bool kept = (old >> 16) + kp > 0;
+            const int rw = atom_add_acq_rel(fs.row + b, kept ? 0x10001 : 1);
+            if (kept) st_release(fs.queue + (size_t)b * a.nb + (rw >> 16), j + 1);
+            row_done = (rw & 0xffff) == a.nb - 1;
+          }
+        }
+      }
+      if constexpr (FUSED) {
+        // The last decision of batch row b: its permutation and count, and,
+        // for the grid's last row, the epoch step that hands the next call
+        // the other counter set (every CTA has read the epoch by now: each
+        // one scored a tile before any row could be complete).
+        if (__shfl_sync(0xffffffffu, row_done, 0)) {
+          fused_write_perm(fs.blk_state + (size_t)b * a.nb, a.nb, f.perm + (size_t)b * a.nb, f.count + b, lane);
+          __syncwarp();
+          if (lane == 0) {
             __threadfence();
-            atomicAdd(f.decided + b, 1);
+            if (atom_add_acq_rel(fs.decided_all, 1) == f.B - 1) atomicAdd(f.epoch, 1);
           }
         }
       }
@@ -763,11 +797,20 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
       if (e == my_tiles % NE) {
         if (lane == 0) {
           const int grp = blockIdx.x % f.NG, b = grp / a.H, h = grp % a.H;
-          const int* qb = f.queue + (size_t)b * a.nb;
+          const int* qb = fs.queue + (size_t)b * a.nb;
           // Per stage (bit s): used = a unit was put in the stage and its
           // release is still to be awaited; phase = parity of that release
           // on empty[s].
           uint32_t used = (1u << (n_units < kStages ? n_units : kStages)) - 1u, phase = 0;
+          constexpr int CPB = kBlock / kFusedChunk;  // units per block
+          // Units are claimed one ahead: the claim's round trip and the first
+          // look at its queue slot overlap the wait for a free stage.  The
+          // queue entry is all that is needed from its publisher (keys and
+          // values are inputs), so relaxed loads poll it; the end-of-queue
+          // test acquires the row word.
+          int w = atomicAdd(fs.grp_ctr + grp, 1);
+          int vq = w / CPB < a.nb ? ld_relaxed(qb + w / CPB) : 0;
+          OC_SSTAMP(9, 0);
           for (int k = n_units;; ++k) {
             const int s = k % kStages;
             if (used >> s & 1u) {
@@ -776,25 +819,31 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
             }
             used |= 1u << s;
             int desc = -1;
+            const uint64_t t0 = globaltimer_ns();
             if (!s_abort) {
-              const int w = atomicAdd(f.grp_ctr + grp, 1);
-              const int slot = w / (kBlock / kFusedChunk), cc = w % (kBlock / kFusedChunk);
-              const uint64_t t0 = globaltimer_ns();
-              while (slot < a.nb) {
-                const int v = ld_acquire(qb + slot);
-                if (v > 0) { desc = (v - 1) * (kBlock / kFusedChunk) + cc; break; }
-                if (ld_acquire(f.decided + b) == a.nb && slot >= ld_acquire(f.tail + b)) break;
+              const int slot = w / CPB;
+              int v = vq;
+              for (int it = 0; slot < a.nb; ++it) {
+                if (v > 0) { desc = (v - 1) * CPB + w % CPB; break; }
+                if ((it & 3) == 3) {
+                  const int rw = ld_acquire(fs.row + b);
+                  if ((rw & 0xffff) == a.nb && slot >= (rw >> 16)) break;  // past the last kept block
+                }
                 if (globaltimer_ns() - t0 > kWaitLimitNs) { s_abort = 1; atomicExch(&g_score_status, 1); break; }
-                __nanosleep(64);
+                __nanosleep(32);
+                v = ld_relaxed(qb + slot);
               }
             }
+#ifdef OC_TIMING
+            g_sstamp[blockIdx.x][9] += globaltimer_ns() - t0;
+#endif
             s_desc[s] = desc;
             if (k == n_units) OC_SSTAMP(15, globaltimer_ns());
             if (desc < 0) {
               mbar_arrive(&full[s]);  // end of the run: the consumers stop at this unit
               break;
             }
-            const int j = desc / (kBlock / kFusedChunk), cc = desc % (kBlock / kFusedChunk);
+            const int j = desc / CPB, cc = desc % CPB;
             uint8_t* dst = smem + (size_t)s * kSlabB;
             const int y = b * a.S + j * kBlock + cc * kFusedChunk;
             mbar_expect_tx(&full[s], kSlabB);
@@ -803,10 +852,11 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
               tma_load_2d(dst + jb * (kFusedChunk * 128), &amap_k, &full[s], h * D + jb * 64, y);
               tma_load_2d(dst + kSlabB / 2 + jb * (kFusedChunk * 128), &amap_v, &full[s], h * D + jb * 64, y);
             }
+            w = atomicAdd(fs.grp_ctr + grp, 1);
+            vq = w / CPB < a.nb ? ld_relaxed(qb + w / CPB) : 0;
           }
         }
       }
-      fused_finish_warp(a, f, n_tiles, &s_done_warps, true);
     }
     return;
   }
@@ -960,7 +1010,7 @@ scored:
     // Online softmax (log2 units) of this warp's tokens, row g:
     // running max, this lane's share of the sum, output channels
     // 64 chh + 8 nt + 2 c4, +1.
-    if (tid == 0) OC_SSTAMP(11, globaltimer_ns());
+    if (tid == 0) { OC_SSTAMP(11, globaltimer_ns()); OC_SSTAMP(18, 0); OC_SSTAMP(19, 0); }
     float m_run = -INFINITY, l_run = 0.f;
     float o[8][2];
 #pragma unroll
@@ -969,11 +1019,17 @@ scored:
     for (int k = n_units;; ++k) {
       const int stage = k % kStages;
       if (__any_sync(0xffffffffu, s_abort)) break;
+#ifdef OC_TIMING
+      const unsigned long long tw0a = globaltimer_ns();
+#endif
       if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], (k / kStages) & 1))) {
         s_abort = 1;
         if (lane == 0) atomicExch(&g_score_status, 1);
         break;
       }
+#ifdef OC_TIMING
+      if (tid == 0) { g_sstamp[blockIdx.x][19] += globaltimer_ns() - tw0a; g_sstamp[blockIdx.x][18] += 1; }
+#endif
       if (s_desc[stage] < 0) break;
       if (tid == 0 && k == n_units) OC_SSTAMP(12, globaltimer_ns());
       const uint32_t kbase = smem_u32(smem + (size_t)stage * kSlabB), vbase = kbase + kSlabB / 2;
@@ -1059,16 +1115,12 @@ scored:
     if (tid == 0) {
       // Release: the CTA's partial (ordered before by the barrier) is
       // visible to whichever CTA sees the last count.
-      s_merge = atom_add_acq_rel(f.grp_done + grp, 1) == n_grp - 1;
+      s_merge = atom_add_acq_rel(fs.grp_done + grp, 1) == n_grp - 1;
       OC_SSTAMP(16, s_merge);
       OC_SSTAMP(17, globaltimer_ns());
     }
     asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
-    const bool merge = s_merge;
-    // Done with every counter: count the warp out now, so the grid's last
-    // CTA can reset the state while the merges run.
-    fused_finish_warp(a, f, n_tiles, &s_done_warps, false);
-    if (merge) {
+    if (s_merge) {
       // Last CTA of the group: log-sum-exp merge of its n_grp partials, o / l
       // (adaptive_attention.py:72-76; zeros when no block is retained,
       // indirect_attention.py:150-151).  kMergeRound partials per round,
@@ -1253,15 +1305,18 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
 
 // Workspace of the fused decode layer: int32 counters (zero between calls),
 // then the per-CTA partials.
+// Workspace of the fused decode layer: the epoch and two counter sets
+// (zero before the first call), then the per-CTA partials.
 struct FusedLayout {
   size_t counters, bytes;
-  int NG, cpg;
+  int NG, cpg, set_ints;
 };
 FusedLayout fused_layout(int B, int nb, int Hkv) {
   FusedLayout L;
   L.NG = B * Hkv;
   L.cpg = (kFusedMaxGrid + L.NG - 1) / L.NG;
-  const size_t ints = 2 * (size_t)B * nb + 2 * (size_t)B + 2 * (size_t)L.NG + 1;
+  L.set_ints = fused_set_ints(B, nb, L.NG);
+  const size_t ints = 1 + 2 * (size_t)L.set_ints;
   L.counters = (ints * 4 + 255) / 256 * 256;
   const size_t parts = (size_t)L.NG * L.cpg * kFusedMaxRows;
   L.bytes = L.counters + ((parts * 2 + parts * 128) * 4 + 255) / 256 * 256;
@@ -1416,20 +1471,15 @@ int decode_fused(const void* q, const void* k, const void* v, int batch, int q_l
   a.bands = Bands{{1, 64, 256}, {64, 256, kBlock}};
   a.tau = tau; a.zeta_max = zeta_max; a.keep = keep;
   FusedArgs f = {};
-  int* c = reinterpret_cast<int*>(ws);
-  f.blk_state = c; c += (size_t)batch * nb;
-  f.queue = c; c += (size_t)batch * nb;
-  f.tail = c; c += batch;
-  f.decided = c; c += batch;
-  f.grp_ctr = c; c += L.NG;
-  f.grp_done = c; c += L.NG;
-  f.exit_ctr = c;
+  f.epoch = reinterpret_cast<int*>(ws);
+  f.sets = f.epoch + 1;
+  f.set_ints = L.set_ints;
   float* pf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + L.counters);
   const size_t parts = (size_t)L.NG * L.cpg * kFusedMaxRows;
   f.part_m = pf; f.part_l = pf + parts; f.part_o = pf + 2 * parts;
   f.out = out; f.out_bf16 = out_dtype == OC_BF16;
   f.perm = perm; f.count = count;
-  f.NG = L.NG; f.cpg = L.cpg; f.R = R;
+  f.B = batch; f.NG = L.NG; f.cpg = L.cpg; f.R = R;
   f.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
 
   CUtensorMap km, ak, av;
