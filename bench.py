@@ -15,11 +15,12 @@ and V blocks.  The KV caches of 4 layers (1.07 GB) rotate across steps, so
 every step reads data that left L2 three steps earlier.
 
 N > 1 (torchrun, one rank per GPU, NCCL): sequence-parallel decode with a
-65,536-token shard per GPU (weak scaling; configuration 3 at N = 8).  Each
-rank scores, compacts and attends over its own shard, producing partial
-(max, sum, output) per query head; the partials (32 x 130 floats per rank)
-are all-gathered over NVLink and merged in log-sum-exp form.  No KV block
-crosses NVLink.
+65,536-token shard per GPU (weak scaling; configuration 3 at N = 8, with
+per-shard eviction drawn from 60-90 %).  Each rank runs the fused decode
+layer on its own shard, producing the partial (max, sum, output) per query
+head; the partials (32 x 130 floats per rank, one packed buffer) are
+all-gathered over NVLink in one call and merged in log-sum-exp form.  No KV
+block crosses NVLink.
 
 Prints one JSON line (rank 0).  The value is µs per decode layer for the
 whole job (lower is better).
@@ -132,27 +133,30 @@ class Layer:
     pass
 
 
-def make_layers(rank, evict, device):
+def make_layers(rank, evict, device, world=1):
     import torch
     from orthocache_b200 import synthetic as syn, score_blocks
     nb = S_SHARD // 512
     layers = []
+    import random
     for l in range(LAYERS):
         seed = 1000 * rank + l
         L = Layer()
-        L.kinds = syn.block_kinds(nb, evict, seed=seed)
+        # configuration 3: uneven per-shard eviction, uniform in 60-90 %
+        L.evict = evict if world == 1 else random.Random(seed).uniform(0.6, 0.9)
+        L.kinds = syn.block_kinds(nb, L.evict, seed=seed)
         L.k = syn.make_keys(nb, HKV, D, L.kinds, seed=seed, device=device)
         L.v = syn.make_values(S_SHARD, HKV, D, seed=seed, device=device)
         L.q = syn.make_queries(1, HQ, D, seed=seed, device=device)
         sc = score_blocks(L.k, L.q, want=("zeta", "bound_max"))
-        L.tau, L.kept = syn.calibrate_tau(sc["zeta"], sc["bound_max"], ZETA_MAX, evict)
+        L.tau, L.kept = syn.calibrate_tau(sc["zeta"], sc["bound_max"], ZETA_MAX, L.evict)
         layers.append(L)
     torch.cuda.synchronize()
     return layers
 
 
 class Engine:
-    """Device buffers and the three C-ABI calls of one decode layer."""
+    """Device buffers and the C-ABI calls of one decode layer."""
 
     def __init__(self, layers, device, world):
         import torch
@@ -168,17 +172,18 @@ class Engine:
         # counters must start at zero) covers the partial attention's too
         self.ws_bytes = _lib.query("oc_decode_step_workspace_bytes", 1, 1, HQ, HKV, D, S_SHARD)
         self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=device)
+        # sequence-parallel: this shard's (m, l, o) partial packed in one
+        # buffer [m (rows) | l (rows) | o (rows, D)], all-gathered in one call
         rows = HQ
-        self.m = torch.empty((rows,), dtype=torch.float32, device=device)
-        self.l = torch.empty((rows,), dtype=torch.float32, device=device)
-        self.o = torch.empty((rows, D), dtype=torch.float32, device=device)
-        self.gm = torch.empty((world, rows), dtype=torch.float32, device=device)
-        self.gl = torch.empty((world, rows), dtype=torch.float32, device=device)
-        self.go = torch.empty((world, rows, D), dtype=torch.float32, device=device)
+        self.rows = rows
+        self.send = torch.empty((rows * (D + 2),), dtype=torch.float32, device=device)
+        self.m, self.l = self.send[:rows], self.send[rows:2 * rows]
+        self.o = self.send[2 * rows:].view(rows, D)
+        self.recv = torch.empty((world * rows * (D + 2),), dtype=torch.float32, device=device)
         # our kernels per layer: one (the fused decode layer: score, block
-        # decisions, attention, merge); sequence-parallel: scorer, compaction,
-        # attention, run merge, shard merge
-        self.launches_per_step = 1 if world == 1 else 5
+        # decisions, attention, merge); sequence-parallel: the fused layer
+        # writing the shard's partial, then the cross-shard merge
+        self.launches_per_step = 1 if world == 1 else 2
 
     @property
     def stream(self):
@@ -191,29 +196,6 @@ class Engine:
                 1, 64, 64, 256, 256, 512, L.tau, ZETA_MAX,
                 None, None, None, None, None, None, None, _l.ptr(self.keep), 0, self.stream)
 
-    def compact(self):
-        _l = self.lib
-        _l.call("oc_stream_compact", _l.ptr(self.keep), 1, self.nb, HKV, _l.ptr(self.perm), _l.ptr(self.count),
-                self.stream)
-
-    def attend(self, L, q=None):
-        _l = self.lib
-        q = L.q if q is None else q
-        if self.world == 1:
-            _l.call("oc_indirect_attention", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, _l.ptr(self.perm), self.nb, 0,
-                    _l.ptr(self.count), 1, 0, 1, 1, HQ, HKV, D, S_SHARD, 512, self.nb, _l.ptr(self.out), 1,
-                    _l.ptr(self.ws), self.ws_bytes, self.stream)
-            return
-        import torch.distributed as dist
-        _l.call("oc_partial_attention", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, _l.ptr(self.perm), self.nb, 0,
-                _l.ptr(self.count), 1, 0, 1, 1, HQ, HKV, D, S_SHARD, 512, self.nb, _l.ptr(self.m), _l.ptr(self.l),
-                _l.ptr(self.o), _l.ptr(self.ws), self.ws_bytes, self.stream)
-        dist.all_gather_into_tensor(self.gm, self.m)
-        dist.all_gather_into_tensor(self.gl, self.l)
-        dist.all_gather_into_tensor(self.go, self.o)
-        _l.call("oc_merge_partials", _l.ptr(self.gm), _l.ptr(self.gl), _l.ptr(self.go), self.world, HQ, D,
-                _l.ptr(self.out), 1, self.stream)
-
     def decode(self, L, q=None):
         """One layer through the one-call C ABI (score -> compact -> attend)."""
         _l = self.lib
@@ -222,13 +204,24 @@ class Engine:
                 _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(self.out), 1,
                 _l.ptr(self.ws), self.ws_bytes, self.stream)
 
+    def decode_sharded(self, L, q=None):
+        """One layer of sequence-parallel decode: the fused kernel writes this
+        shard's partial, one all-gather over NCCL, one merge."""
+        import torch.distributed as dist
+        _l = self.lib
+        q = L.q if q is None else q
+        _l.call("oc_decode_step_partial", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, 1, 1, HQ, HKV, D, S_SHARD,
+                L.tau, ZETA_MAX, _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(self.m),
+                _l.ptr(self.l), _l.ptr(self.o), _l.ptr(self.ws), self.ws_bytes, self.stream)
+        dist.all_gather_into_tensor(self.recv, self.send)
+        _l.call("oc_merge_partials_packed", _l.ptr(self.recv), self.world, self.rows, D, _l.ptr(self.out), 1,
+                self.stream)
+
     def step(self, L, q=None):
         if self.world == 1:
             self.decode(L, q)
-            return
-        self.score(L, q)
-        self.compact()
-        self.attend(L, q)
+        else:
+            self.decode_sharded(L, q)
 
 
 # ---------------------------------------------------------------------------
@@ -301,7 +294,7 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    layers = make_layers(rank, args.evict, device)
+    layers = make_layers(rank, args.evict, device, world)
     eng = Engine(layers, device, world)
     nb = S_SHARD // 512
 
@@ -309,14 +302,26 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
-    # warm-up: at least W steps and at least 0.5 s so clocks settle
+    # warm-up: at least W steps and at least 0.5 s so clocks settle.  With
+    # N > 1 every step is a collective, so all ranks must run the same count:
+    # rank 0's decision to stop is broadcast every 64 steps.
     t_w = time.perf_counter()
     i = 0
-    while i < args.warmup or time.perf_counter() - t_w < 0.5:
+    flag = torch.zeros((1,), dtype=torch.int32, device=device)
+    while True:
         eng.step(layers[i % LAYERS])
         i += 1
-        if i % 64 == 0:
+        if world == 1:
+            if i >= args.warmup and time.perf_counter() - t_w >= 0.5:
+                break
+            if i % 64 == 0:
+                torch.cuda.synchronize()
+        elif i % 64 == 0:
             torch.cuda.synchronize()
+            flag.fill_(int(i >= args.warmup and time.perf_counter() - t_w >= 0.5))
+            dist.broadcast(flag, 0)
+            if int(flag.item()):
+                break
     torch.cuda.synchronize()
 
     K = args.steps
@@ -436,8 +441,10 @@ def run_ours(args, rank, world, local_rank):
         "metric": METRIC, "value": round(ms * 1e3, 3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config1: GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens per GPU "
-                               "(%d total), evict=%.2f, zeta_max=5" % (S_SHARD, S_SHARD * world, args.evict),
+        "config": {"workload": ("config1: GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens, evict=%.2f, "
+                                "zeta_max=5" % (S_SHARD, args.evict)) if world == 1 else
+                               ("config3: sequence-parallel GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens per "
+                                "GPU (%d total), per-shard eviction U[0.6, 0.9], zeta_max=5" % (S_SHARD, S_SHARD * world)),
                    "l2": "inputs > L2: 4 layers of KV (1.07 GB) rotate per step",
                    "parallelism": "single GPU" if world == 1 else f"sequence-parallel x{world}, LSE merge"},
         "roofline": ({"bound": "hbm", "kernel": "score_tma_kernel<128,true> (fused decode layer)",

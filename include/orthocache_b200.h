@@ -268,6 +268,20 @@ int oc_decode_step(const void* q, const void* k, const void* v, int dtype,
                    void* out, int out_dtype,
                    void* workspace, size_t workspace_bytes, oc_stream_t stream);
 
+/* The decode step of one sequence shard, for the log-sum-exp merge across
+ * shards (distributed_attention.py:95-128 applied across devices): as
+ * oc_decode_step, but instead of out it writes the shard's unnormalised
+ * partial per output row in the format of oc_partial_attention — m (rows),
+ * l (rows), o (rows, D) float32, rows = B*Sq*Hq, m in log2 units of the
+ * scaled logits (m = -inf, l = 0, o = 0 when the shard retains nothing).
+ * Same workspace contract as oc_decode_step (zero-filled once). */
+int oc_decode_step_partial(const void* q, const void* k, const void* v, int dtype,
+                           int batch, int q_len, int q_heads, int kv_heads, int head_dim, int seq_len,
+                           float tau, float zeta_max,
+                           uint8_t* keep, int32_t* perm, int32_t* count,
+                           float* m, float* l, float* o,
+                           void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Sequence-parallel exchange helpers (the device-side index math of
  * distributed_attention.py:179-191, alltoallv.py:113-145 and
@@ -293,6 +307,13 @@ int oc_stratified_bucket(int nb_per_device, int gmax);
  * oc_partial_attention; out (rows, D) in out_dtype; rows = B*Sq*Hq. */
 int oc_merge_partials(const float* m, const float* l, const float* o, int parts, int rows,
                       int head_dim, void* out, int out_dtype, oc_stream_t stream);
+
+/* oc_merge_partials on the packed layout that one all-gather of per-shard
+ * partials produces: part p occupies rows * (D + 2) floats at
+ * packed + p * rows * (D + 2), holding m (rows), then l (rows), then
+ * o (rows, D). */
+int oc_merge_partials_packed(const float* packed, int parts, int rows, int head_dim, void* out, int out_dtype,
+                             oc_stream_t stream);
 
 /* Partial (unnormalised) attention of one shard for the LSE merge: same
  * arguments as oc_indirect_attention but writes m (rows), l (rows) and

@@ -1137,19 +1137,21 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
 // Cross-shard merge of (m, l, o) triples (P parts of `rows` rows).
 template <typename TO>
 __global__ void __launch_bounds__(128)
-merge_parts_kernel(const float* m, const float* l, const float* o, int P, int rows, int D, TO* out) {
+merge_parts_kernel(const float* m, const float* l, const float* o, int P, int rows, int D, TO* out,
+                   size_t ml_stride, size_t o_stride) {
+  // part p's m and l at p * ml_stride, its o at p * o_stride (floats)
   const int r = blockIdx.x;
   float M = -INFINITY;
-  for (int p = 0; p < P; ++p) M = fmaxf(M, m[(size_t)p * rows + r]);
+  for (int p = 0; p < P; ++p) M = fmaxf(M, m[(size_t)p * ml_stride + r]);
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
       for (int p = 0; p < P; ++p) {
-        const float mp = m[(size_t)p * rows + r];
+        const float mp = m[(size_t)p * ml_stride + r];
         if (mp == -INFINITY) continue;
         const float f = exp2f(mp - M);
-        L = fmaf(l[(size_t)p * rows + r], f, L);
-        O = fmaf(o[((size_t)p * rows + r) * D + d], f, O);
+        L = fmaf(l[(size_t)p * ml_stride + r], f, L);
+        O = fmaf(o[(size_t)p * o_stride + (size_t)r * D + d], f, O);
       }
     }
     out[(size_t)r * D + d] = from_f32<TO>(L > 0.f ? O / L : 0.f);
@@ -1381,20 +1383,39 @@ extern "C" int oc_partial_attention(const void* q, const void* k, const void* v,
                        reinterpret_cast<cudaStream_t>(stream));
 }
 
+namespace {
+int merge_parts(const float* m, const float* l, const float* o, int parts, int rows, int head_dim, void* out,
+                int out_dtype, size_t ml_stride, size_t o_stride, oc_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (out_dtype == OC_F32)
+    merge_parts_kernel<float><<<rows, 128, 0, st>>>(m, l, o, parts, rows, head_dim, (float*)out, ml_stride,
+                                                    o_stride);
+  else if (out_dtype == OC_BF16)
+    merge_parts_kernel<__nv_bfloat16><<<rows, 128, 0, st>>>(m, l, o, parts, rows, head_dim,
+                                                             (__nv_bfloat16*)out, ml_stride, o_stride);
+  else
+    return set_error(OC_ERR_DTYPE, "oc_merge_partials: out_dtype %d", out_dtype);
+  return check_launch("merge_parts_kernel");
+}
+}  // namespace
+
 extern "C" int oc_merge_partials(const float* m, const float* l, const float* o, int parts, int rows,
                                  int head_dim, void* out, int out_dtype, oc_stream_t stream) {
   OC_REQUIRE(m && l && o && out, OC_ERR_NULL, "oc_merge_partials: null pointer");
   OC_REQUIRE(parts >= 1 && rows >= 0 && head_dim >= 1, OC_ERR_SHAPE, "oc_merge_partials: bad shape");
   if (rows == 0) return OC_OK;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (out_dtype == OC_F32)
-    merge_parts_kernel<float><<<rows, 128, 0, st>>>(m, l, o, parts, rows, head_dim, (float*)out);
-  else if (out_dtype == OC_BF16)
-    merge_parts_kernel<__nv_bfloat16><<<rows, 128, 0, st>>>(m, l, o, parts, rows, head_dim,
-                                                             (__nv_bfloat16*)out);
-  else
-    return set_error(OC_ERR_DTYPE, "oc_merge_partials: out_dtype %d", out_dtype);
-  return check_launch("merge_parts_kernel");
+  return merge_parts(m, l, o, parts, rows, head_dim, out, out_dtype, (size_t)rows, (size_t)rows * head_dim,
+                     stream);
+}
+
+extern "C" int oc_merge_partials_packed(const float* packed, int parts, int rows, int head_dim, void* out,
+                                        int out_dtype, oc_stream_t stream) {
+  OC_REQUIRE(packed && out, OC_ERR_NULL, "oc_merge_partials_packed: null pointer");
+  OC_REQUIRE(parts >= 1 && rows >= 0 && head_dim >= 1, OC_ERR_SHAPE, "oc_merge_partials_packed: bad shape");
+  if (rows == 0) return OC_OK;
+  const size_t part = (size_t)rows * (head_dim + 2);
+  return merge_parts(packed, packed + rows, packed + 2 * (size_t)rows, parts, rows, head_dim, out, out_dtype, part,
+                     part, stream);
 }
 
 extern "C" size_t oc_decode_step_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
@@ -1422,8 +1443,8 @@ extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int d
   if (dtype == OC_BF16 && seq_len > 0) {
     // One persistent kernel for the whole layer where the shape allows it.
     const int frc = oc::decode_fused(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max,
-                                     keep, perm, count, out, out_dtype, workspace, fused_bytes,
-                                     reinterpret_cast<cudaStream_t>(stream));
+                                     keep, perm, count, out, out_dtype, nullptr, nullptr, nullptr, workspace,
+                                     fused_bytes, reinterpret_cast<cudaStream_t>(stream));
     if (frc != OC_ERR_UNSUPPORTED) return frc;
   }
   workspace = static_cast<uint8_t*>(workspace) + fused_bytes;
@@ -1443,6 +1464,38 @@ extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int d
   if (rc) return rc;
   return oc_indirect_attention(q, k, v, dtype, perm, nb, 0, count, 1, 0, batch, q_len, q_heads, kv_heads, head_dim,
                                seq_len, 512, nb, out, out_dtype, workspace, workspace_bytes, stream);
+}
+
+extern "C" int oc_decode_step_partial(const void* q, const void* k, const void* v, int dtype,
+                                      int batch, int q_len, int q_heads, int kv_heads, int head_dim, int seq_len,
+                                      float tau, float zeta_max,
+                                      uint8_t* keep, int32_t* perm, int32_t* count,
+                                      float* m, float* l, float* o,
+                                      void* workspace, size_t workspace_bytes, oc_stream_t stream) {
+  OC_REQUIRE(keep && perm && count && m && l && o, OC_ERR_NULL, "oc_decode_step_partial: null output pointer");
+  OC_REQUIRE(seq_len % 512 == 0, OC_ERR_SHAPE, "oc_decode_step_partial: seq_len %d not a multiple of 512",
+             seq_len);
+  OC_REQUIRE(batch >= 1 && kv_heads >= 1, OC_ERR_SHAPE, "oc_decode_step_partial: batch/kv_heads < 1");
+  const int nb = seq_len / 512;
+  const size_t fused_bytes = oc::decode_fused_bytes(batch, seq_len, kv_heads);
+  OC_REQUIRE(workspace && workspace_bytes >= fused_bytes, OC_ERR_CAPACITY,
+             "oc_decode_step_partial: workspace of %zu bytes, need at least %zu", workspace_bytes, fused_bytes);
+  if (dtype == OC_BF16 && seq_len > 0) {
+    const int frc = oc::decode_fused(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max,
+                                     keep, perm, count, nullptr, OC_F32, m, l, o, workspace, fused_bytes,
+                                     reinterpret_cast<cudaStream_t>(stream));
+    if (frc != OC_ERR_UNSUPPORTED) return frc;
+  }
+  workspace = static_cast<uint8_t*>(workspace) + fused_bytes;
+  workspace_bytes -= fused_bytes;
+  int rc = oc_score_blocks(k, q, dtype, batch, seq_len, kv_heads, head_dim, q_len, q_heads, 1, 64, 64, 256,
+                           256, 512, tau, zeta_max, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                           keep, 0, stream);
+  if (rc) return rc;
+  rc = oc_stream_compact(keep, batch, nb, kv_heads, perm, count, stream);
+  if (rc) return rc;
+  return oc_partial_attention(q, k, v, dtype, perm, nb, 0, count, 1, 0, batch, q_len, q_heads, kv_heads, head_dim,
+                              seq_len, 512, nb, m, l, o, workspace, workspace_bytes, stream);
 }
 
 extern "C" int oc_empty_heads_mean(const void* v, int dtype, const int32_t* count, int count_stride,

@@ -30,11 +30,14 @@ int attn_status(int* status, int reset);
 // zero-filled before the first call, after which calls keep its epoch and
 // counter sets consistent.  decode_fused returns OC_ERR_UNSUPPORTED, without launching, for
 // shapes it does not cover (head_dim != 128, more than 8 query rows per KV
-// head, batch * kv_heads above the grid, workspace too small).
+// head, batch * kv_heads above the grid, workspace too small).  With pm, pl,
+// po non-null it writes the layer's (m, l, o) partials (the format of
+// oc_partial_attention) instead of out.
 size_t decode_fused_bytes(int batch, int seq_len, int kv_heads);
 int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
                  int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
-                 void* out, int out_dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+                 void* out, int out_dtype, float* pm, float* pl, float* po, void* ws, size_t ws_bytes,
+                 cudaStream_t st);
 
 #define OC_REQUIRE(cond, code, ...)                                   \
   do {                                                                \

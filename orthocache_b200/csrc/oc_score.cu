@@ -444,6 +444,9 @@ struct FusedArgs {
   float* part_o;    // (NG, cpg, kFusedMaxRows, D)
   void* out;        // (B, Sq, Hq, D)
   int out_bf16;
+  float* pm;        // non-null: write the layer's (m, l, o) per output row
+  float* pl;        //   instead of out (log2 units, as oc_partial_attention)
+  float* po;
   int32_t* perm;    // (B, nb)
   int32_t* count;   // (B)
   int B, NG, cpg, R;
@@ -1155,11 +1158,17 @@ scored:
             M = mc;
           }
         }
-        const float y = L > 0.f ? O / L : 0.f;
         const int s = r / a.G, gq = r - s * a.G;
         const size_t orow = ((size_t)bq * a.Sq + s) * a.Hq + (size_t)hq * a.G + gq;
-        if (f.out_bf16) reinterpret_cast<__nv_bfloat16*>(f.out)[orow * D + d] = __float2bfloat16_rn(y);
-        else reinterpret_cast<float*>(f.out)[orow * D + d] = y;
+        if (f.pm) {
+          // Unnormalised partial of this shard for a cross-shard merge.
+          f.po[orow * D + d] = O;
+          if (d == 0) { f.pm[orow] = M; f.pl[orow] = L; }
+        } else {
+          const float y = L > 0.f ? O / L : 0.f;
+          if (f.out_bf16) reinterpret_cast<__nv_bfloat16*>(f.out)[orow * D + d] = __float2bfloat16_rn(y);
+          else reinterpret_cast<float*>(f.out)[orow * D + d] = y;
+        }
       }
     }
     if (tid == 0) OC_SSTAMP(14, globaltimer_ns());
@@ -1451,7 +1460,8 @@ size_t decode_fused_bytes(int batch, int seq_len, int kv_heads) {
 
 int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
                  int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
-                 void* out, int out_dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+                 void* out, int out_dtype, float* pm, float* pl, float* po, void* ws, size_t ws_bytes,
+                 cudaStream_t st) {
   if (head_dim != 128 || !q || q_len < 1 || kv_heads < 1 || q_heads % kv_heads) return OC_ERR_UNSUPPORTED;
   const int G = q_heads / kv_heads, R = q_len * G, nb = seq_len / kBlock;
   if (R > kFusedMaxRows || nb < 1 || nb > 0xffff || kv_heads > 0xffff) return OC_ERR_UNSUPPORTED;
@@ -1478,6 +1488,7 @@ int decode_fused(const void* q, const void* k, const void* v, int batch, int q_l
   const size_t parts = (size_t)L.NG * L.cpg * kFusedMaxRows;
   f.part_m = pf; f.part_l = pf + parts; f.part_o = pf + 2 * parts;
   f.out = out; f.out_bf16 = out_dtype == OC_BF16;
+  f.pm = pm; f.pl = pl; f.po = po;
   f.perm = perm; f.count = count;
   f.B = batch; f.NG = L.NG; f.cpg = L.cpg; f.R = R;
   f.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);

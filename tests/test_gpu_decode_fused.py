@@ -164,3 +164,48 @@ def test_fused_decode_in_cuda_graph():
         assert lib.oc_device_status(1) == 0
         check_against_oracle(qbuf, k, v, tau, keep, perm, count, out)
     assert epoch(ws) == e0 + 3
+
+
+@pytest.mark.parametrize("sq,hq,hkv,evicts", [(1, 32, 8, [0.75, 0.6]), (2, 16, 4, [0.9, 0.5, 0.7])])
+def test_fused_shard_partials_and_packed_merge(sq, hq, hkv, evicts):
+    """Sequence-parallel decode on one GPU: each shard runs
+    oc_decode_step_partial into its slice of one packed buffer
+    [m | l | o], oc_merge_partials_packed combines the shards, and the result
+    equals attention over the union of every shard's retained blocks."""
+    lib = _lib()
+    P, nb, d = len(evicts), 20, 128
+    rows = sq * hq
+    shards = [make_batch(1, nb, hq, hkv, d, sq, [ev], seed=400 + 7 * p) for p, ev in enumerate(evicts)]
+    q = shards[0][0]
+    tau = tau_for(q[0], shards[0][1][0], evicts[0])
+    packed = torch.full((P, rows * (d + 2)), float("nan"), dtype=torch.float32, device="cuda")
+    kept_k, kept_v, n_all = [], [], 0
+    for p, (_, k, v) in enumerate(shards):
+        ws = workspace(1, sq, hq, hkv, d, nb * 512)
+        keep = torch.empty((1, nb, hkv), dtype=torch.uint8, device="cuda")
+        perm = torch.empty((1, nb), dtype=torch.int32, device="cuda")
+        count = torch.empty((1,), dtype=torch.int32, device="cuda")
+        buf = packed[p]
+        rc = lib.oc_decode_step_partial(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 1, sq, hq, hkv, d, nb * 512,
+                                        ctypes.c_float(tau), ctypes.c_float(ZMAX), keep.data_ptr(), perm.data_ptr(),
+                                        count.data_ptr(), buf.data_ptr(), buf[rows:].data_ptr(),
+                                        buf[2 * rows:].data_ptr(), ws.data_ptr(), ws.numel(),
+                                        torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, lib.oc_last_error()
+        torch.cuda.synchronize()
+        assert epoch(ws) == 1
+        rp, rn = O.stream_compact_mask(host(keep[0]).astype(bool))
+        assert int(count[0]) == rn and np.array_equal(host(perm[0]), rp)
+        kf, vf = host(k[0]).reshape(nb, 512, hkv, d), host(v[0]).reshape(nb, 512, hkv, d)
+        kept_k.append(kf[rp[:rn]])
+        kept_v.append(vf[rp[:rn]])
+        n_all += rn
+    out = torch.empty((rows, d), dtype=torch.bfloat16, device="cuda")
+    rc = lib.oc_merge_partials_packed(packed.data_ptr(), P, rows, d, out.data_ptr(), 1,
+                                      torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.oc_last_error()
+    torch.cuda.synchronize()
+    kc = np.concatenate(kept_k).reshape(-1, hkv, d)
+    vc = np.concatenate(kept_v).reshape(-1, hkv, d)
+    ref = O.indirect_attention(host(q[0]), kc, vc, np.arange(n_all, dtype=np.int32), n_all)
+    np.testing.assert_allclose(host(out).reshape(ref.shape), ref, rtol=ATT_RTOL, atol=ATT_ATOL)
