@@ -108,6 +108,34 @@ int oc_score_blocks(const void* keys, const void* q, int dtype,
                     int mode, oc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Write-time spectral metadata.  ζ, the DC coefficients and E_AC of a block
+ * do not depend on the query (docs/mathematical_framework.md:244-250 of the
+ * reference: "computed once when the block is written to the KV cache"), so
+ * a cache that keeps them needs to read only them at decode time instead of
+ * every key.
+ *
+ * oc_block_metadata: for keys (B, S, Hkv, D) with the reference's default
+ * bands, write dc (B, nb, Hkv, D) = WHT coefficient 0, e_ac (B, nb, Hkv) =
+ * energy of coefficients 1..511 (spectral_energy.py:159-160) and zeta
+ * (B, nb, Hkv) (spectral_energy.py:109-138); each output nullable.  Values
+ * equal oc_score_blocks' for the same keys.  Run it on a slice of whole
+ * blocks to refresh only the blocks that were (re)written.
+ */
+int oc_block_metadata(const void* keys, int dtype, int batch, int seq_len, int kv_heads, int head_dim,
+                      float* dc, float* e_ac, float* zeta, oc_stream_t stream);
+
+/* oc_score_from_metadata: the two gates of compute_multiband_mask
+ * (spectral_energy.py:199-234) from that metadata and the queries alone:
+ * bound = q·(dc/√512)/√D + ‖q‖·√E_AC/√D per query row (spectral_energy.py:
+ * 150-177, GQA rows as in oc_score_blocks), bound_max (B, nb, Hkv) its max,
+ * bounds (B, Sq, nb, Hq), keep = bound_max >= tau && zeta <= zeta_max; each
+ * output nullable.  q (B, Sq, Hq, D) of q_dtype. */
+int oc_score_from_metadata(const float* dc, const float* e_ac, const float* zeta, const void* q, int q_dtype,
+                           int batch, int num_blocks, int kv_heads, int head_dim, int q_len, int q_heads,
+                           float tau, float zeta_max, float* bound_max, float* bounds, uint8_t* keep,
+                           oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Sum of squared keys per (block, head) — replaces compute_block_energy_jax
  * (spectral_energy.py:21-35).  energy: (B, nb, H) float32.  block_size any
  * divisor of S.

@@ -158,6 +158,35 @@ def query_aware_bounds(q, keys, block_size=BLOCK):
     return (align + resid).reshape(sq, nb, hq).astype(np.float32)
 
 
+def block_metadata(keys, block_size=BLOCK):
+    """Query-independent metadata of every block, computed once when a block
+    is written (the hoisting of ``docs/mathematical_framework.md:244-250``):
+    dc (nb, H, D) = WHT coefficient 0, e_ac (nb, H) = energy of coefficients
+    1..511 (``spectral_energy.py:159-160``), zeta (nb, H)
+    (``spectral_energy.py:109-138``).  float32."""
+    spec = spectral_coefficients(keys, block_size)
+    dc = spec[:, 0].astype(np.float64)
+    ac = spec[:, 1:].astype(np.float64)
+    e_ac = np.einsum("bkhd,bkhd->bh", ac, ac)
+    return dc.astype(np.float32), e_ac.astype(np.float32), spectral_decay_ratio(keys, block_size)
+
+
+def bounds_from_metadata(q, dc, e_ac):
+    """``compute_query_aware_bounds`` (``spectral_energy.py:141-177``) from the
+    cached dc and E_AC instead of the keys: (Sq, nb, Hq)."""
+    q64 = np.asarray(q, np.float64)
+    dc = np.asarray(dc, np.float64)
+    e_ac = np.asarray(e_ac, np.float64)
+    nb, hkv, d = dc.shape
+    sq, hq, _ = q64.shape
+    g = _group(hq, hkv)
+    q64 = q64.reshape(sq, hkv, g, d)
+    align = np.einsum("qhgd,bhd->qbhg", q64, dc / math.sqrt(BLOCK)) / math.sqrt(d)
+    qn = np.sqrt(np.einsum("qhgd,qhgd->qhg", q64, q64))
+    resid = qn[:, None, :, :] * np.sqrt(e_ac)[None, :, :, None] / math.sqrt(d)
+    return (align + resid).reshape(sq, nb, hq).astype(np.float32)
+
+
 def max_bounds(q, keys, block_size=BLOCK):
     """Max over the query axis (and the G heads of each group): (nb, Hkv).
 

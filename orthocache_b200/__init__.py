@@ -25,6 +25,7 @@ from .compaction import stream_compact, stream_decompact, compact_and_attend
 from .pipeline import orthocache_forward
 from .indirect_attention import indirect_attention, compile_indirect_attention
 from .adaptive_attention import orthocache_attention, orthocache_attention_batched
+from .metadata_cache import SpectralMetadataCache
 
 __all__ = [
     "fwht_512", "compute_block_energy_jax", "generate_threshold_mask", "compute_query_aware_bounds",
@@ -32,5 +33,5 @@ __all__ = [
     "compute_multiband_mask", "score_blocks", "jax_block_sparse_attention",
     "compile_pallas_sparse_attention", "stream_compact", "stream_decompact", "compact_and_attend",
     "orthocache_forward", "indirect_attention", "compile_indirect_attention", "orthocache_attention",
-    "orthocache_attention_batched",
+    "orthocache_attention_batched", "SpectralMetadataCache",
 ]

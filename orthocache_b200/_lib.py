@@ -35,6 +35,8 @@ SIGNATURES = {
     "oc_score_blocks": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _f,
                              _p, _p, _p, _p, _p, _p, _p, _p, _i, _p]),
     "oc_block_energy": (_i, [_p, _i, _i, _i, _i, _i, _i, _p, _p]),
+    "oc_block_metadata": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p]),
+    "oc_score_from_metadata": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p, _p, _p]),
     "oc_stream_compact": (_i, [_p, _i, _i, _i, _p, _p, _p]),
     "oc_gather_blocks": (_i, [_p, _i, _i, _i, _i64, _p, _i, _p, _p, _i, _i, _p]),
     "oc_scatter_blocks": (_i, [_p, _i, _i, _i, _i64, _p, _i, _p, _p, _i, _p]),

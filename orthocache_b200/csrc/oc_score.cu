@@ -65,6 +65,7 @@ struct ScoreArgs {
   float* zeta;
   float* bound_max;
   float* bounds;  // (B, Sq, nb, Hq) or null
+  float* e_ac;    // (B, nb, H) energy of coefficients 1..511, or null
   uint8_t* keep;
 };
 
@@ -133,6 +134,7 @@ __device__ void score_epilogue(const ScoreArgs& a, int b, int j, int h,
     if (a.e_mid) a.e_mid[cell] = band[1];
     if (a.e_high) a.e_high[cell] = band[2];
     if (a.zeta) a.zeta[cell] = z;
+    if (a.e_ac) a.e_ac[cell] = band[3];
     if (a.q && a.bound_max) a.bound_max[cell] = bmax;
     if (a.keep) {
       const bool gate1 = a.q ? (bmax >= a.tau) : true;
@@ -597,13 +599,17 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     s_merge = 0;
     OC_SSTAMP(10, globaltimer_ns());
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
+    // The first slabs are requested before the previous kernel in the stream
+    // has finished: a kernel only starts early behind one of this library's
+    // scorer, compaction or attention kernels, and none of them writes keys.
+    for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
   }
   // Launched as a programmatic dependent: everything above overlaps the
-  // previous kernel; keys, queries and outputs are touched only after it.
+  // previous kernel; queries, outputs and the workspace are touched only
+  // after it.
   pdl_trigger();
   pdl_wait();
   if (tid == 0) {
-    for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
     if constexpr (FUSED) s_set = __ldcg(f.epoch) & 1;
     OC_SSTAMP(8, globaltimer_ns());
   }
@@ -758,6 +764,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         if (a.e_mid) a.e_mid[cell] = e_mi;
         if (a.e_high) a.e_high[cell] = e_hi;
         if (a.zeta) a.zeta[cell] = z;
+        if (a.e_ac) a.e_ac[cell] = e_ac;
         if (a.q && a.bound_max) a.bound_max[cell] = bmax;
         const int kp = ((a.q ? bmax >= a.tau : true) && z <= a.zeta_max) ? 1 : 0;
         if (a.keep) a.keep[cell] = (uint8_t)kp;
@@ -1385,6 +1392,13 @@ extern "C" int oc_fwht512(const void* x, int x_dtype, int64_t ncols, float* y, o
   return check_launch("fwht512_kernel");
 }
 
+namespace oc {
+int score_blocks_impl(const void* keys, const void* q, int dtype, int batch, int seq_len, int kv_heads,
+                      int head_dim, int q_len, int q_heads, int bl0, int bl1, int bm0, int bm1, int bh0, int bh1,
+                      float tau, float zeta_max, float* dc, float* e_low, float* e_mid, float* e_high, float* zeta,
+                      float* bound_max, float* bounds, uint8_t* keep, float* e_ac, int mode, oc_stream_t stream);
+}  // namespace oc
+
 extern "C" int oc_score_blocks(const void* keys, const void* q, int dtype,
                                int batch, int seq_len, int kv_heads, int head_dim,
                                int q_len, int q_heads,
@@ -1393,6 +1407,24 @@ extern "C" int oc_score_blocks(const void* keys, const void* q, int dtype,
                                float* dc, float* e_low, float* e_mid, float* e_high,
                                float* zeta, float* bound_max, float* bounds, uint8_t* keep,
                                int mode, oc_stream_t stream) {
+  return score_blocks_impl(keys, q, dtype, batch, seq_len, kv_heads, head_dim, q_len, q_heads, bl0, bl1, bm0, bm1,
+                           bh0, bh1, tau, zeta_max, dc, e_low, e_mid, e_high, zeta, bound_max, bounds, keep,
+                           nullptr, mode, stream);
+}
+
+extern "C" int oc_block_metadata(const void* keys, int dtype, int batch, int seq_len, int kv_heads, int head_dim,
+                                 float* dc, float* e_ac, float* zeta, oc_stream_t stream) {
+  OC_REQUIRE(dc || e_ac || zeta, OC_ERR_NULL, "oc_block_metadata: no output");
+  return score_blocks_impl(keys, nullptr, dtype, batch, seq_len, kv_heads, head_dim, 0, 0, 1, 64, 64, 256, 256,
+                           512, 0.f, 0.f, dc, nullptr, nullptr, nullptr, zeta, nullptr, nullptr, nullptr, e_ac, 0,
+                           stream);
+}
+
+namespace oc {
+int score_blocks_impl(const void* keys, const void* q, int dtype, int batch, int seq_len, int kv_heads,
+                      int head_dim, int q_len, int q_heads, int bl0, int bl1, int bm0, int bm1, int bh0, int bh1,
+                      float tau, float zeta_max, float* dc, float* e_low, float* e_mid, float* e_high, float* zeta,
+                      float* bound_max, float* bounds, uint8_t* keep, float* e_ac, int mode, oc_stream_t stream) {
   OC_REQUIRE(keys, OC_ERR_NULL, "oc_score_blocks: keys is NULL");
   OC_REQUIRE(batch >= 1 && kv_heads >= 1, OC_ERR_SHAPE, "oc_score_blocks: batch/kv_heads < 1");
   OC_REQUIRE(seq_len >= 0 && seq_len % kBlock == 0, OC_ERR_SHAPE,
@@ -1419,15 +1451,92 @@ extern "C" int oc_score_blocks(const void* keys, const void* q, int dtype,
   const int64_t ncta = (int64_t)batch * nb * kv_heads;
   if (ncta == 0) return OC_OK;
   OC_REQUIRE(ncta < (1ll << 31), OC_ERR_CAPACITY, "oc_score_blocks: too many blocks");
-  ScoreArgs a;
+  ScoreArgs a = {};
   a.keys = keys; a.q = q; a.S = seq_len; a.H = kv_heads; a.D = head_dim; a.nb = nb;
   a.Sq = q ? q_len : 0; a.Hq = q ? q_heads : 0; a.G = q ? q_heads / kv_heads : 1;
   a.bands = bd; a.tau = tau; a.zeta_max = zeta_max;
   a.dc = dc; a.e_low = e_low; a.e_mid = e_mid; a.e_high = e_high; a.zeta = zeta;
-  a.bound_max = bound_max; a.bounds = q ? bounds : nullptr; a.keep = keep;
+  a.bound_max = bound_max; a.bounds = q ? bounds : nullptr; a.keep = keep; a.e_ac = e_ac;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == OC_F32) return launch_score<float>(a, mode, (int)ncta, st);
   return launch_score<__nv_bfloat16>(a, mode, (int)ncta, st);
+}
+}  // namespace oc
+
+// ---------------------------------------------------------------------------
+// The two gates from write-time metadata (no key is read): one warp per
+// (batch, block, kv head) cell computes the bound of every query row of the
+// group from the cached DC coefficients and E_AC (spectral_energy.py:150-177),
+// its max (:195), and the keep bit with the cached zeta (:196, :231-234).
+// ---------------------------------------------------------------------------
+namespace oc {
+namespace {
+template <typename T>
+__global__ void __launch_bounds__(256)
+meta_gates_kernel(const float* __restrict__ dc, const float* __restrict__ e_ac, const float* __restrict__ zeta,
+                  const T* __restrict__ q, int nb, int H, int D, int Sq, int Hq, int G, int64_t cells, float tau,
+                  float zeta_max, float* bound_max, float* bounds, uint8_t* keep) {
+  const int lane = threadIdx.x & 31;
+  const int64_t cell = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (cell >= cells) return;
+  const int h = (int)(cell % H);
+  const int j = (int)((cell / H) % nb);
+  const int b = (int)(cell / ((int64_t)H * nb));
+  const float sqrt_d = sqrtf((float)D);
+  const float resid_scale = sqrtf(e_ac[cell]);
+  const float* dcc = dc + cell * D;
+  float bmax = -INFINITY;
+  const int rows = Sq * G;
+  for (int r = 0; r < rows; ++r) {
+    const int s = r / G, gq = r - s * G;
+    const size_t qrow = ((size_t)b * Sq + s) * Hq + (size_t)h * G + gq;
+    const T* qr = q + qrow * D;
+    float dot = 0.f, nrm = 0.f;
+    for (int c = lane; c < D; c += 32) {
+      const float qv = to_f32<T>(qr[c]);
+      dot = fmaf(qv, dcc[c] / kNorm, dot);  // block mean = DC / sqrt(512)
+      nrm = fmaf(qv, qv, nrm);
+    }
+    dot = warp_sum(dot);
+    nrm = warp_sum(nrm);
+    const float bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
+    if (bounds && lane == 0) bounds[(((size_t)b * Sq + s) * nb + j) * Hq + (size_t)h * G + gq] = bound;
+    bmax = fmaxf(bmax, bound);
+  }
+  if (lane == 0) {
+    if (bound_max) bound_max[cell] = bmax;
+    if (keep) keep[cell] = (bmax >= tau && zeta[cell] <= zeta_max) ? 1 : 0;
+  }
+}
+}  // namespace
+}  // namespace oc
+
+extern "C" int oc_score_from_metadata(const float* dc, const float* e_ac, const float* zeta, const void* q,
+                                      int q_dtype, int batch, int num_blocks, int kv_heads, int head_dim,
+                                      int q_len, int q_heads, float tau, float zeta_max, float* bound_max,
+                                      float* bounds, uint8_t* keep, oc_stream_t stream) {
+  OC_REQUIRE(dc && e_ac && zeta && q, OC_ERR_NULL, "oc_score_from_metadata: null input");
+  OC_REQUIRE(bound_max || bounds || keep, OC_ERR_NULL, "oc_score_from_metadata: no output");
+  OC_REQUIRE(batch >= 1 && num_blocks >= 0 && kv_heads >= 1 && head_dim >= 1 && q_len >= 1 &&
+                 q_heads >= 1 && q_heads % kv_heads == 0,
+             OC_ERR_SHAPE, "oc_score_from_metadata: bad shape");
+  const int64_t cells = (int64_t)batch * num_blocks * kv_heads;
+  if (cells == 0) return OC_OK;
+  const int64_t grid = (cells + 7) / 8;
+  OC_REQUIRE(grid < (1ll << 31), OC_ERR_CAPACITY, "oc_score_from_metadata: too many blocks");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int G = q_heads / kv_heads;
+  if (q_dtype == OC_F32)
+    meta_gates_kernel<float><<<(unsigned)grid, 256, 0, st>>>(dc, e_ac, zeta, (const float*)q, num_blocks, kv_heads,
+                                                             head_dim, q_len, q_heads, G, cells, tau, zeta_max,
+                                                             bound_max, bounds, keep);
+  else if (q_dtype == OC_BF16)
+    meta_gates_kernel<__nv_bfloat16><<<(unsigned)grid, 256, 0, st>>>(
+        dc, e_ac, zeta, (const __nv_bfloat16*)q, num_blocks, kv_heads, head_dim, q_len, q_heads, G, cells, tau,
+        zeta_max, bound_max, bounds, keep);
+  else
+    return set_error(OC_ERR_DTYPE, "oc_score_from_metadata: q dtype %d", q_dtype);
+  return check_launch("meta_gates_kernel");
 }
 
 namespace oc {

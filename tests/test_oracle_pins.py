@@ -168,3 +168,10 @@ def test_sparse_attention_equals_indirect_on_union_mask():  # test_compaction.py
     a = O.indirect_attention(q, k, v, perm, n, block_size=64)
     b = O.block_sparse_attention(q, k, v, np.repeat(m[:, None], 2, 1), block_size=64)
     np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-6)
+
+
+def test_bounds_from_write_time_metadata_match_reference():  # test_energy.py:33-52
+    """The bound rebuilt from cached (dc, E_AC) equals the reference's bound."""
+    dc, e_ac, _ = O.block_metadata(X["bounds_keys"])
+    np.testing.assert_allclose(O.bounds_from_metadata(X["bounds_q"], dc, e_ac), GOLD["bounds"],
+                               rtol=1e-5, atol=1e-5)
