@@ -1573,7 +1573,9 @@ int decode_fused(const void* q, const void* k, const void* v, int batch, int q_l
                  cudaStream_t st) {
   if (head_dim != 128 || !q || q_len < 1 || kv_heads < 1 || q_heads % kv_heads) return OC_ERR_UNSUPPORTED;
   const int G = q_heads / kv_heads, R = q_len * G, nb = seq_len / kBlock;
-  if (R > kFusedMaxRows || nb < 1 || nb > 0xffff || kv_heads > 0xffff) return OC_ERR_UNSUPPORTED;
+  // Counts share an int32 with 16 bits each (blk_state, the row word): at
+  // most 32767 blocks per row and 32767 KV heads keep them non-negative.
+  if (R > kFusedMaxRows || nb < 1 || nb > 0x7fff || kv_heads > 0x7fff) return OC_ERR_UNSUPPORTED;
   if (out_dtype != OC_BF16 && out_dtype != OC_F32) return OC_ERR_UNSUPPORTED;
   const FusedLayout L = fused_layout(batch, nb, kv_heads);
   const int64_t ntiles = (int64_t)batch * nb * kv_heads;
