@@ -1579,6 +1579,7 @@ int decode_fused(const void* q, const void* k, const void* v, int batch, int q_l
   if (out_dtype != OC_BF16 && out_dtype != OC_F32) return OC_ERR_UNSUPPORTED;
   const FusedLayout L = fused_layout(batch, nb, kv_heads);
   const int64_t ntiles = (int64_t)batch * nb * kv_heads;
+  if (ntiles >= (1ll << 31)) return OC_ERR_UNSUPPORTED;
   int grid = device_sm_count();
   if (grid > kFusedMaxGrid) grid = kFusedMaxGrid;
   if (ntiles < grid) grid = (int)ntiles;
