@@ -286,6 +286,34 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def warmup_steps(step, min_steps, min_seconds, world, sync, device):
+    """Run step(i) for i = 0, 1, ... until at least min_steps steps and
+    min_seconds of wall time have passed; returns the number of steps.
+
+    With world > 1 every step is a collective, so every rank must run the same
+    number of steps whatever its own clock says: rank 0 decides, and its
+    decision is broadcast every 64 steps."""
+    import torch
+    import torch.distributed as dist
+    t0 = time.perf_counter()
+    flag = torch.zeros((1,), dtype=torch.int32, device=device)
+    i = 0
+    while True:
+        step(i)
+        i += 1
+        if world == 1:
+            if i >= min_steps and time.perf_counter() - t0 >= min_seconds:
+                return i
+            if i % 64 == 0:
+                sync()
+        elif i % 64 == 0:
+            sync()
+            flag.fill_(int(i >= min_steps and time.perf_counter() - t0 >= min_seconds))
+            dist.broadcast(flag, 0)
+            if int(flag.item()):
+                return i
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -302,26 +330,8 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
-    # warm-up: at least W steps and at least 0.5 s so clocks settle.  With
-    # N > 1 every step is a collective, so all ranks must run the same count:
-    # rank 0's decision to stop is broadcast every 64 steps.
-    t_w = time.perf_counter()
-    i = 0
-    flag = torch.zeros((1,), dtype=torch.int32, device=device)
-    while True:
-        eng.step(layers[i % LAYERS])
-        i += 1
-        if world == 1:
-            if i >= args.warmup and time.perf_counter() - t_w >= 0.5:
-                break
-            if i % 64 == 0:
-                torch.cuda.synchronize()
-        elif i % 64 == 0:
-            torch.cuda.synchronize()
-            flag.fill_(int(i >= args.warmup and time.perf_counter() - t_w >= 0.5))
-            dist.broadcast(flag, 0)
-            if int(flag.item()):
-                break
+    warmup_steps(lambda i: eng.step(layers[i % LAYERS]), args.warmup, 0.5, world, torch.cuda.synchronize,
+                 device)
     torch.cuda.synchronize()
 
     K = args.steps

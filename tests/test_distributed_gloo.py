@@ -3,6 +3,7 @@ count sync, offsets, the packed-buffer exchange, the receive-side layout and
 the stratified bucket consensus, each checked against the oracle."""
 import os
 import socket
+from pathlib import Path
 import sys
 
 import pytest
@@ -54,3 +55,37 @@ def test_block_data_paths_fail_without_gpu():
     with pytest.raises(Exception):
         ocd.pack_active_blocks(torch.zeros(1024, 1, 8), torch.arange(2, dtype=torch.int32),
                                torch.tensor([1]), 2)
+
+
+def _warmup_entry(rank, world, port, result_dir):
+    """Ranks whose steps take different times must still agree on the number
+    of warm-up steps (each step of the sequence-parallel bench is a
+    collective)."""
+    import time
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.dirname(HERE))
+    import bench
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        t = torch.zeros(1)
+
+        def step(i):
+            time.sleep(0.0005 * (rank + 1))  # rank 1 is twice as slow
+            dist.all_reduce(t)
+
+        n = bench.warmup_steps(step, 5, 0.2, world, lambda: None, torch.device("cpu"))
+        got = torch.tensor([n])
+        dist.all_reduce(got, op=dist.ReduceOp.MAX)
+        assert int(got) == n and n % 64 == 0 and n >= 64
+        (Path(result_dir) / f"warm{rank}").write_text(str(n))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_bench_warmup_step_count_agrees_across_ranks(tmp_path):
+    world = 2
+    mp.spawn(_warmup_entry, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    counts = {(tmp_path / f"warm{r}").read_text() for r in range(world)}
+    assert len(counts) == 1
