@@ -249,7 +249,9 @@ int oc_empty_heads_mean(const void* v, int dtype, const int32_t* count, int coun
  *     with OC_ERR_CAPACITY.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The address is cached for the life of the
+ *     process: a device reset (cudaDeviceReset) or a torn-down primary
+ *     context is not supported afterwards.
  *   - All calls on a device share the one array: calls whose kernels overlap
  *     on the GPU (different streams, or other threads) race and corrupt each
  *     other's results.  Serialise them.  Nothing in the array needs to start

@@ -1350,7 +1350,8 @@ using namespace oc;
 
 extern "C" size_t oc_indirect_attention_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
                                                         int head_dim, int block_size, int max_blocks) {
-  if (batch < 1 || q_len < 1 || kv_heads < 1 || q_heads % kv_heads || block_size < 64 || block_size % 64)
+  if (batch < 1 || q_len < 1 || kv_heads < 1 || q_heads % kv_heads || block_size < 64 || block_size % 64 ||
+      (head_dim != 64 && head_dim != 128 && head_dim != 256) || max_blocks < 0)
     return 0;
   return attn_ws_bytes(batch, q_len, q_heads, kv_heads, head_dim, block_size, max_blocks);
 }
@@ -1420,7 +1421,9 @@ extern "C" int oc_merge_partials_packed(const float* packed, int parts, int rows
 
 extern "C" size_t oc_decode_step_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
                                                  int head_dim, int seq_len) {
-  if (seq_len % 512 || batch < 1 || kv_heads < 1) return 0;
+  if (seq_len % 512 || seq_len < 512 || batch < 1 || kv_heads < 1 || q_len < 1 || q_heads % kv_heads ||
+      (head_dim != 64 && head_dim != 128 && head_dim != 256))
+    return 0;
   // The fused layer's region first (its counters stay zero between calls),
   // then the scratch of the separate score / attention path.
   return oc::decode_fused_bytes(batch, seq_len, kv_heads) +
@@ -1586,8 +1589,9 @@ extern "C" int oc_indirect_attention_noalloc(const void* q, const void* k, const
                                              void* out, int out_dtype, oc_stream_t stream) {
   OC_REQUIRE(out, OC_ERR_NULL, "oc_indirect_attention_noalloc: out is NULL");
   OC_REQUIRE(batch >= 1 && q_len >= 1 && kv_heads >= 1 && q_heads >= kv_heads && q_heads % kv_heads == 0 &&
-                 block_size >= 64 && block_size % 64 == 0 && max_blocks >= 0,
-             OC_ERR_SHAPE, "oc_indirect_attention_noalloc: bad shape");
+                 block_size >= 64 && block_size % 64 == 0 && max_blocks >= 0 &&
+                 (head_dim == 64 || head_dim == 128 || head_dim == 256),
+             OC_ERR_SHAPE, "oc_indirect_attention_noalloc: bad shape (head_dim must be 64, 128 or 256)");
   const size_t need = oc::attn_ws_bytes(batch, q_len, q_heads, kv_heads, head_dim, block_size, max_blocks);
   OC_REQUIRE(need <= oc::kNoAllocScratchBytes, OC_ERR_CAPACITY,
              "oc_indirect_attention_noalloc: this shape needs %zu bytes of scratch, above the fixed %zu-byte "

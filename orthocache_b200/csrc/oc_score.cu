@@ -1319,8 +1319,6 @@ int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   return check_launch("score_tma_kernel");
 }
 
-// Workspace of the fused decode layer: int32 counters (zero between calls),
-// then the per-CTA partials.
 // Workspace of the fused decode layer: the epoch and two counter sets
 // (zero before the first call), then the per-CTA partials.
 struct FusedLayout {

@@ -55,3 +55,10 @@ def test_host_side_validation_without_gpu():
     assert lib.oc_stratified_bucket(16, 0) == 4
     assert lib.oc_stratified_bucket(1, 1) == 1
     assert lib.oc_indirect_attention_workspace_bytes(1, 1, 32, 8, 128, 512, 128) > 0
+    # an unsupported head_dim is an error code, never a host-side crash
+    assert lib.oc_indirect_attention_workspace_bytes(1, 1, 32, 8, 0, 512, 4) == 0
+    assert lib.oc_indirect_attention_workspace_bytes(1, 1, 32, 8, 16384, 512, 4) == 0
+    assert lib.oc_decode_step_workspace_bytes(1, 1, 32, 8, 0, 65536) == 0
+    rc = lib.oc_indirect_attention_noalloc(None, None, None, 1, None, 4, 0, None, 1, 0, 1, 1, 32, 8, 0,
+                                           2048, 512, 4, ctypes.c_void_p(16), 1, None)
+    assert rc == -2 and b"head_dim" in lib.oc_last_error()
