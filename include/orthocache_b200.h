@@ -55,7 +55,8 @@ const char* oc_last_error(void);
 
 /* Device-side status of the pipelined kernels: nonzero if a bounded wait on
  * an asynchronous copy gave up (the kernel then skipped its remaining work
- * instead of hanging).  Synchronises the current device; reset != 0 clears it.
+ * instead of hanging).  Bit 0: scorer / fused decode layer; bit 1: split-KV
+ * attention; bit 2: chunked-prefill attention.  Synchronises the current device; reset != 0 clears it.
  * Returns the status (>= 0) or an OC_ERR_* code. */
 int oc_device_status(int reset);
 
@@ -264,6 +265,31 @@ int oc_indirect_attention_noalloc(const void* q, const void* k, const void* v, i
                                   int batch, int q_len, int q_heads, int kv_heads, int head_dim,
                                   int seq_len, int block_size, int max_blocks,
                                   void* out, int out_dtype, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Chunked-prefill indirect attention on the tensor cores (tcgen05 + tensor
+ * memory) — replaces indirect_attention / _multihead_loop
+ * (src/orthocache/indirect_attention.py:29-83, :127-170;
+ * adaptive_attention.py:90-120) when the query chunk is long: every query row
+ * attends to the tokens of blocks idx[0 .. count) (count clipped to
+ * max_blocks), online softmax in float32, o / l; count == 0 gives zeros.
+ * Same index / count conventions as oc_indirect_attention (per-row lists with
+ * idx_head_stride = count_head_stride = 0, per-KV-head lists otherwise).
+ *
+ * bfloat16 q (B, Sq, Hq, D), k / v (B, S, Hkv, D) with head_dim 128;
+ * block_size a multiple of 128 dividing seq_len; out (B, Sq, Hq, D) in
+ * out_dtype (OC_BF16 or OC_F32).  Any q_len >= 1 (query rows are processed in
+ * tiles of 128; the last tile of a chunk is partial).  P is rounded to
+ * bfloat16 for the P.V product, as in FlashAttention-style kernels.  Needs no
+ * workspace.  One persistent CTA per SM holding 224 KB of shared memory and
+ * all 512 tensor-memory columns of its SM.
+ */
+int oc_prefill_attention(const void* q, const void* k, const void* v, int dtype,
+                         const int32_t* idx, int idx_stride, int idx_head_stride,
+                         const int32_t* count, int count_stride, int count_head_stride,
+                         int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                         int seq_len, int block_size, int max_blocks,
+                         void* out, int out_dtype, oc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * One decode step of the OrthoCache pipeline on the device: score (two-gate

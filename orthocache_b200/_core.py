@@ -87,9 +87,24 @@ def batched_qkv(q, k, v, dtype=None):
     return q.contiguous(), k.contiguous(), v.contiguous(), batched
 
 
+PREFILL_MIN_Q = 64
+
+
+def prefill_applies(q, block_size):
+    """Long query chunks (chunked prefill) go to the tensor-core kernel
+    ``oc_prefill_attention``: bfloat16, head_dim 128, blocks of a multiple of
+    128 tokens and at least ``PREFILL_MIN_Q`` query positions (its row tiles
+    are 128 positions of one query head, so shorter chunks would be mostly
+    padding and stay on the split-KV decode kernel)."""
+    return (q.dtype == torch.bfloat16 and q.shape[-1] == 128 and block_size % 128 == 0
+            and q.shape[1] >= PREFILL_MIN_Q)
+
+
 def attend(q, k, v, idx, count, block_size, max_blocks=None, idx_stride=None, idx_head_stride=0,
            count_stride=1, count_head_stride=0, out_dtype=None):
-    """Indirect block attention (``oc_indirect_attention``) on 4-D tensors.
+    """Indirect block attention on 4-D tensors: ``oc_prefill_attention`` for
+    long bfloat16 query chunks (``prefill_applies``), ``oc_indirect_attention``
+    (split-KV) otherwise.
 
     q (B, Sq, Hq, D); k, v (B, S, Hkv, D); idx int32 index lists, count int32.
     Returns (B, Sq, Hq, D) in ``out_dtype`` (default q.dtype).
@@ -103,6 +118,12 @@ def attend(q, k, v, idx, count, block_size, max_blocks=None, idx_stride=None, id
         idx_stride = idx.shape[-1] if idx.dim() >= 1 else 0
     out_dtype = out_dtype or q.dtype
     out = torch.empty((B, Sq, Hq, D), dtype=out_dtype, device=q.device)
+    if prefill_applies(q, block_size):
+        _lib.call("oc_prefill_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(q),
+                  _lib.ptr(idx), int(idx_stride), int(idx_head_stride), _lib.ptr(count), int(count_stride),
+                  int(count_head_stride), B, Sq, Hq, Hkv, D, S, block_size, max_blocks,
+                  _lib.ptr(out), _lib.dtype_code(out), _lib.stream_ptr(q.device))
+        return out
     ws_bytes = _lib.query("oc_indirect_attention_workspace_bytes", B, Sq, Hq, Hkv, D, block_size, max_blocks)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
     _lib.call("oc_indirect_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(q),

@@ -45,6 +45,8 @@ SIGNATURES = {
     "oc_indirect_attention_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
     "oc_indirect_attention": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
                                    _i, _p, _i, _p, _sz, _p]),
+    "oc_prefill_attention": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+                                  _i, _p, _i, _p]),
     "oc_indirect_attention_noalloc_max_scratch_bytes": (_sz, []),
     "oc_indirect_attention_noalloc": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
                                            _i, _p, _i, _p]),

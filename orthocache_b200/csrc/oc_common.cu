@@ -84,6 +84,20 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+int encode_map_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t dims[3],
+                  const uint64_t strides[2], const uint32_t box[3], bool swizzle128) {
+  auto fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t s[2] = {strides[0], strides[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), d, s, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return (int)r;
+}
+
 int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
                   uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
   auto fn = encode_fn();
@@ -120,5 +134,8 @@ extern "C" int oc_device_status(int reset) {
   if (rc) return rc;
   rc = oc::attn_status(&s2, reset);
   if (rc) return rc;
-  return s1 | (s2 << 1);
+  int s3 = 0;
+  rc = oc::prefill_status(&s3, reset);
+  if (rc) return rc;
+  return s1 | (s2 << 1) | (s3 << 2);
 }

@@ -24,6 +24,7 @@ int device_sm_count();
 // copies it to *status (0 = none) and clears it if reset.  Synchronous.
 int score_status(int* status, int reset);
 int attn_status(int* status, int reset);
+int prefill_status(int* status, int reset);
 
 // Fused decode layer (score, compact, attend and merge in one persistent
 // kernel; oc_score.cu).  decode_fused_bytes: workspace it needs; it must be

@@ -1,0 +1,601 @@
+// Chunked-prefill indirect block attention on the 5th-generation tensor cores
+// (tcgen05 + tensor memory), for query chunks long enough to make attention
+// compute-bound: every query row of a chunk attends to the tokens of the
+// retained blocks idx[0 .. count) of its batch row (and KV head, for per-head
+// lists), with a streaming (online) softmax.
+//
+// Semantics: the per-block loop of indirect_attention / _multihead_loop
+// (src/orthocache/indirect_attention.py:29-83, adaptive_attention.py:90-120)
+// for any seq_len_q: logits = q.k / sqrt(D) in float32, softmax over all
+// retained tokens, output o / l cast to the output dtype; count == 0 gives
+// zeros (indirect_attention.py:150-151).  GQA: query head hq reads KV head
+// hq / (Hq / Hkv).  No causal mask (the reference has none).
+//
+// Design (one persistent CTA per SM, 320 threads):
+//   * a work unit is (batch row b, KV head h, two row tiles of 128 query rows
+//     each); the two tiles share every K and V tile the unit streams, so the
+//     tensor pipe alternates between them while the other tile's softmax runs;
+//   * warp 8 is the TMA producer: the unit's two query tiles (32 KB each,
+//     128B-swizzled boxes of 128 rows x 64 channels), then K_0, V_0, K_1,
+//     V_1, ... (128 tokens x 128 channels, 32 KB each) into a 3-slot ring;
+//   * warp 9 allocates 512 tensor-memory columns (per tile: S = 128 fp32
+//     columns, O = 128 fp32 columns) and one of its threads issues every
+//     tcgen05.mma: S_t = Q_t K_j^T (A and B K-major) and O_t += P_t V_j
+//     (P K-major from shared memory, V MN-major), 8 instructions of
+//     M128 N128 K16 each, with tcgen05.commit to mbarriers;
+//   * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / 1: each thread
+//     owns one query row (tensor-memory lane), loads its 128 logits with
+//     tcgen05.ld, keeps the running max and sum, writes P in bf16 into a
+//     128B-swizzled shared-memory tile, and rescales O in tensor memory only
+//     when its row max grows by more than 2^8 (the stale max stays exact: the
+//     final o / l uses the same max for both);
+//   * the issue order per KV tile j is PV_0(j-1), S_0(j), PV_1(j-1), S_1(j):
+//     the commit that publishes S_t(j) also covers PV_t(j-1), so a softmax
+//     warpgroup that sees S_t(j) may rescale O_t and overwrite P_t.
+// Every mbarrier wait is bounded; a wait that gives up sets g_prefill_status
+// and an abort flag so that all warps leave their loops and the CTA frees its
+// tensor memory.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "oc_common.cuh"
+#include "oc_mma.cuh"
+#include "oc_tma.cuh"
+
+namespace oc {
+
+__device__ int g_prefill_status = 0;
+
+namespace {
+
+constexpr int kPfRows = 128;        // query rows per tile (UMMA M)
+constexpr int kPfTok = 128;         // tokens per K/V tile (UMMA N of QK^T, K of PV)
+constexpr int kPfD = 128;           // head_dim
+constexpr int kPfSlots = 3;         // K/V ring slots
+constexpr int kPfTileBytes = kPfRows * kPfD * 2;  // 32 KB, every tile in the kernel
+constexpr int kPfBoxBytes = kPfTileBytes / 2;     // one 128 x 64 box
+constexpr int kPfThreads = 320;
+constexpr int kPfProducerWarp = 8;
+constexpr int kPfMmaWarp = 9;
+constexpr int kPfTmemCols = 512;
+
+struct PfSmem {
+  // tiles first, each 1024-byte aligned (the 128B swizzle repeats every 1024 B)
+  unsigned char q[2][kPfTileBytes];
+  unsigned char p[2][kPfTileBytes];
+  unsigned char kv[kPfSlots][kPfTileBytes];
+  uint64_t kv_full[kPfSlots], kv_empty[kPfSlots];
+  uint64_t q_full, q_empty;
+  uint64_t s_full[2], p_full[2], o_free[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t kPfSmemBytes = sizeof(PfSmem) + 1024;  // + alignment slack
+
+struct PfArgs {
+  const int32_t* idx;
+  const int32_t* count;
+  void* out;
+  int out_dtype;
+  int B, Sq, Hq, Hkv, S, bs, max_blocks;
+  int idx_stride, idx_hstride, count_stride, count_hstride;
+  int G, nqt, tiles_per_head, npairs, units;
+  float scale_log2;  // log2(e) / sqrt(D)
+};
+
+// ---- tcgen05 helpers (inline PTX, sm_100a) --------------------------------
+
+// Shared-memory matrix descriptor: start address, leading / stride byte
+// offsets (16-byte units), descriptor version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr & 0x3ffff) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: f32 accumulator, bf16 A and B, A
+// K-major, B K-major (b_mn = 0) or MN-major (b_mn = 1), M = 128, N = 128.
+__host__ __device__ constexpr uint32_t idesc_bf16(int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(kPfTok >> 3) << 17) |
+         ((uint32_t)(kPfRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, int acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive once on bar when every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's lane (warp w reads lanes
+// 32*(w%4) .. +31), loaded and waited for in one asm statement so that no
+// use of the registers can be scheduled before tcgen05.wait::ld.
+__device__ __forceinline__ void tmem_ld32_wait(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 64 consecutive fp32 columns of this thread's lane, loaded and waited for
+// in one asm statement.
+__device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64 + 32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+        "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]),
+        "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
+        "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ float fast_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---- work decomposition ---------------------------------------------------
+
+struct PfUnit {
+  int b, h, n;        // batch row, KV head, K/V tiles to stream (count * bs / 128)
+  int ntile;          // row tiles in this unit (1 or 2)
+  int hq[2], q0[2];   // query head and first query position of each tile
+  const int32_t* idx;
+};
+
+__device__ __forceinline__ PfUnit pf_unit(const PfArgs& a, int u) {
+  PfUnit w;
+  const int pair = u % a.npairs;
+  const int bh = u / a.npairs;
+  w.h = bh % a.Hkv;
+  w.b = bh / a.Hkv;
+  const int r0 = 2 * pair;
+  w.ntile = (r0 + 1 < a.tiles_per_head) ? 2 : 1;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int r = r0 + t;  // row tile r: query head g = r % G of the group, position tile r / G
+    w.hq[t] = w.h * a.G + r % a.G;
+    w.q0[t] = (r / a.G) * kPfRows;
+  }
+  int c = a.count[(size_t)w.b * a.count_stride + (size_t)w.h * a.count_hstride];
+  c = c < 0 ? 0 : (c > a.max_blocks ? a.max_blocks : c);
+  w.n = c * (a.bs / kPfTok);
+  w.idx = a.idx + (size_t)w.b * a.idx_stride + (size_t)w.h * a.idx_hstride;
+  return w;
+}
+
+// First token (row of the (B*S, Hkv, D) view) of K/V tile j of a unit.
+__device__ __forceinline__ int pf_token(const PfArgs& a, const PfUnit& w, int j) {
+  const int tpb = a.bs / kPfTok;
+  const int blk = w.idx[j / tpb];
+  return w.b * a.S + blk * a.bs + (j % tpb) * kPfTok;
+}
+
+__device__ __forceinline__ bool pf_wait(PfSmem& sm, uint64_t* bar, uint32_t parity) {
+  if (mbar_wait(bar, parity)) return true;
+  atomicExch(&g_prefill_status, 1);
+  *(volatile int*)&sm.abort = 1;
+  return false;
+}
+__device__ __forceinline__ bool pf_aborted(PfSmem& sm) { return *(volatile int*)&sm.abort != 0; }
+
+// Store one finished output row (128 channels) of this thread.
+template <typename TO>
+__device__ __forceinline__ void pf_store_row(TO* dst, const float* v, float inv_l);
+template <>
+__device__ __forceinline__ void pf_store_row<__nv_bfloat16>(__nv_bfloat16* dst, const float* v, float inv_l) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * c + 0] * inv_l, v[8 * c + 1] * inv_l);
+    w.y = pack_bf16x2(v[8 * c + 2] * inv_l, v[8 * c + 3] * inv_l);
+    w.z = pack_bf16x2(v[8 * c + 4] * inv_l, v[8 * c + 5] * inv_l);
+    w.w = pack_bf16x2(v[8 * c + 6] * inv_l, v[8 * c + 7] * inv_l);
+    d[c] = w;
+  }
+}
+template <>
+__device__ __forceinline__ void pf_store_row<float>(float* dst, const float* v, float inv_l) {
+  float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    d[c] = make_float4(v[4 * c] * inv_l, v[4 * c + 1] * inv_l, v[4 * c + 2] * inv_l, v[4 * c + 3] * inv_l);
+}
+
+template <typename TO>
+__device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
+  const int row = threadIdx.x & 127;           // query row of the tile == TMEM lane
+  const int warp_lane0 = (threadIdx.x & 96);   // first TMEM lane of this warp
+  const uint32_t t_s = tmem + ((uint32_t)warp_lane0 << 16) + t * 256;
+  const uint32_t t_o = t_s + 128;
+  unsigned char* pt = sm.p[t];
+  const uint32_t sw = row & 7;
+  uint32_t s_ph = 0;
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+    const PfUnit w = pf_unit(a, u);
+    if (t >= w.ntile) continue;
+    const int qpos = (t ? w.q0[1] : w.q0[0]) + row;
+    const int hq = t ? w.hq[1] : w.hq[0];
+    TO* orow = reinterpret_cast<TO*>(a.out) + (((size_t)w.b * a.Sq + qpos) * a.Hq + hq) * kPfD;
+    if (w.n == 0) {
+      if (qpos < a.Sq) {
+        float z[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) z[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) pf_store_row<TO>(orow + 32 * c, z, 0.f);
+      }
+      continue;
+    }
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < w.n; ++j) {
+      if (pf_aborted(sm) || !pf_wait(sm, &sm.s_full[t], s_ph)) { ok = false; break; }
+      s_ph ^= 1;
+      tc_fence_after();
+      // Row max in two halves (64 columns each, to stay within the register
+      // budget of 3 warps per SM sub-partition); the second half stays in
+      // registers for the exponentials, the first is read again.
+      float s[64];
+      tmem_ld64_wait(t_s, s);
+      float mx = s[0];
+#pragma unroll
+      for (int i = 1; i < 64; ++i) mx = fmaxf(mx, s[i]);
+      tmem_ld64_wait(t_s + 64, s);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
+      mx *= a.scale_log2;
+      const bool need = mx > m_used + 8.f;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_new = need ? mx : m_used;
+        const float alpha = fast_ex2(m_used - m_new);  // 0 on the first tile (m_used = -inf)
+        if (j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32_wait(t_o + 32 * c, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(t_o + 32 * c, o);
+          }
+          tc_wait_st();
+        }
+        l *= alpha;
+        m_used = m_new;
+      }
+      // P = exp2(s * scale - m) in bf16, K-major 128B-swizzled: tokens 0-63
+      // in the first 16 KB box, 64-127 in the second.
+      float rs = 0.f;
+#pragma unroll
+      for (int half = 1; half >= 0; --half) {
+        if (half == 0) tmem_ld64_wait(t_s, s);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float p[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            p[i] = fast_ex2(fmaf(s[8 * c + i], a.scale_log2, -m_used));
+            rs += p[i];
+          }
+          uint4 v;
+          v.x = pack_bf16x2(p[0], p[1]);
+          v.y = pack_bf16x2(p[2], p[3]);
+          v.z = pack_bf16x2(p[4], p[5]);
+          v.w = pack_bf16x2(p[6], p[7]);
+          *reinterpret_cast<uint4*>(pt + half * kPfBoxBytes + row * 128 + ((c ^ sw) << 4)) = v;
+        }
+      }
+      l += rs;
+      fence_proxy_async();  // P (generic-proxy writes) is read by the tensor core
+      tc_fence_before();
+      mbar_arrive(&sm.p_full[t]);
+    }
+    if (!ok) break;
+    // the last commit of the unit covers the final PV: O is complete
+    if (pf_aborted(sm) || !pf_wait(sm, &sm.s_full[t], s_ph)) break;
+    s_ph ^= 1;
+    tc_fence_after();
+    const float inv_l = 1.f / l;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      tmem_ld32_wait(t_o + 32 * c, o);
+      if (qpos < a.Sq) pf_store_row<TO>(orow + 32 * c, o, inv_l);
+    }
+    // O of this tile is read: the next unit's first S_t may be committed
+    // (without this hand-over two phases of s_full[t] could complete between
+    // two polls of this warpgroup).
+    tc_fence_before();
+    mbar_arrive(&sm.o_free[t]);
+  }
+}
+
+__device__ void pf_producer(PfSmem& sm, const PfArgs& a, const CUtensorMap* mq, const CUtensorMap* mk,
+                            const CUtensorMap* mv) {
+  uint32_t q_ph = 0;
+  uint32_t L = 0;  // running K/V load index: slot L % 3, use L / 3
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+    const PfUnit w = pf_unit(a, u);
+    if (w.n == 0) continue;
+    if (pf_aborted(sm) || !pf_wait(sm, &sm.q_empty, q_ph ^ 1)) return;
+    q_ph ^= 1;
+    mbar_expect_tx(&sm.q_full, (uint32_t)(w.ntile * kPfTileBytes));
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      if (t < w.ntile) {
+        const int y = w.hq[t], z = w.b * a.Sq + w.q0[t];
+        tma_load_3d(sm.q[t], mq, &sm.q_full, 0, y, z);
+        tma_load_3d(sm.q[t] + kPfBoxBytes, mq, &sm.q_full, 64, y, z);
+      }
+    }
+    for (int j = 0; j < w.n; ++j) {
+      const int tok = pf_token(a, w, j);
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv, ++L) {
+        const uint32_t slot = L % kPfSlots, use = L / kPfSlots;
+        if (pf_aborted(sm) || !pf_wait(sm, &sm.kv_empty[slot], (use & 1) ^ 1)) return;
+        mbar_expect_tx(&sm.kv_full[slot], kPfTileBytes);
+        const CUtensorMap* m = kv ? mv : mk;
+        tma_load_3d(sm.kv[slot], m, &sm.kv_full[slot], 0, w.h, tok);
+        tma_load_3d(sm.kv[slot] + kPfBoxBytes, m, &sm.kv_full[slot], 64, w.h, tok);
+      }
+    }
+  }
+}
+
+__device__ void pf_mma(PfSmem& sm, const PfArgs& a, uint32_t tmem) {
+  constexpr uint32_t kIdQK = idesc_bf16(0), kIdPV = idesc_bf16(1);
+  uint32_t q_ph = 0, p_ph = 0, o_ph = 0;  // bit t: phase of p_full[t] / o_free[t]
+  uint32_t L = 0;
+  for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+    const PfUnit w = pf_unit(a, u);
+    if (w.n == 0) continue;
+    if (pf_aborted(sm) || !pf_wait(sm, &sm.q_full, q_ph)) return;
+    q_ph ^= 1;
+    tc_fence_after();
+    uint32_t vslot_prev = 0;
+    for (int j = 0; j <= w.n; ++j) {
+      uint32_t kslot = 0;
+      if (j < w.n) {
+        kslot = L % kPfSlots;
+        if (pf_aborted(sm) || !pf_wait(sm, &sm.kv_full[kslot], (L / kPfSlots) & 1)) return;
+        tc_fence_after();
+      }
+      if (j > 0) {  // V_{j-1} is load L - 1
+        if (pf_aborted(sm) || !pf_wait(sm, &sm.kv_full[vslot_prev], ((L - 1) / kPfSlots) & 1)) return;
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t >= w.ntile) break;
+        const uint32_t d_s = tmem + t * 256, d_o = d_s + 128;
+        const uint32_t qa = smem_u32(sm.q[t]), pa = smem_u32(sm.p[t]);
+        if (j > 0) {
+          if (pf_aborted(sm) || !pf_wait(sm, &sm.p_full[t], (p_ph >> t) & 1)) return;
+          p_ph ^= 1u << t;
+          tc_fence_after();
+          const uint32_t vb = smem_u32(sm.kv[vslot_prev]);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = sdesc(pa + (kk >> 2) * kPfBoxBytes + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sdesc(vb + kk * 2048, kPfBoxBytes, 1024);
+            umma_bf16(d_o, ad, bd, kIdPV, (j > 1 || kk > 0) ? 1 : 0);
+          }
+          if (t == w.ntile - 1) umma_commit(&sm.kv_empty[vslot_prev]);
+        }
+        if (j == 0) {  // the softmax warpgroup has read the previous unit's O_t
+          if (pf_aborted(sm) || !pf_wait(sm, &sm.o_free[t], ((o_ph >> t) & 1) ^ 1)) return;
+          o_ph ^= 1u << t;
+          tc_fence_after();
+        }
+        if (j < w.n) {
+          const uint32_t kb = smem_u32(sm.kv[kslot]);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = sdesc(qa + (kk >> 2) * kPfBoxBytes + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sdesc(kb + (kk >> 2) * kPfBoxBytes + (kk & 3) * 32, 16, 1024);
+            umma_bf16(d_s, ad, bd, kIdQK, kk > 0 ? 1 : 0);
+          }
+        }
+        umma_commit(&sm.s_full[t]);
+        if (j < w.n && t == w.ntile - 1) {
+          umma_commit(&sm.kv_empty[kslot]);
+          if (j == w.n - 1) umma_commit(&sm.q_empty);
+        }
+      }
+      if (j < w.n) {
+        vslot_prev = (L + 1) % kPfSlots;
+        L += 2;
+      }
+    }
+  }
+}
+
+template <typename TO>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                        const __grid_constant__ CUtensorMap mv, const PfArgs a) {
+  extern __shared__ unsigned char pf_raw[];
+  PfSmem& sm = *reinterpret_cast<PfSmem*>((reinterpret_cast<uintptr_t>(pf_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPfSlots; ++i) {
+      mbar_init(&sm.kv_full[i], 1);
+      mbar_init(&sm.kv_empty[i], 1);
+    }
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], 128);
+      mbar_init(&sm.o_free[t], 128);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kPfMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem_base)),
+                 "r"(kPfTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp < 8) {
+    pf_softmax<TO>(sm, a, warp >> 2, tmem);
+  } else if (warp == kPfProducerWarp) {
+    if ((threadIdx.x & 31) == 0) pf_producer(sm, a, &mq, &mk, &mv);
+  } else {
+    if ((threadIdx.x & 31) == 0) {
+      pf_mma(sm, a, tmem);
+      // wait (bounded) for every MMA still in flight before the memory is freed
+      umma_commit(&sm.drain);
+      if (!mbar_wait(&sm.drain, 0)) atomicExch(&g_prefill_status, 1);
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kPfMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols) : "memory");
+  }
+}
+
+int pf_map(CUtensorMap* m, const void* base, int inner_heads, int64_t rows, const char* what) {
+  const uint64_t dims[3] = {(uint64_t)kPfD, (uint64_t)inner_heads, (uint64_t)rows};
+  const uint64_t strides[2] = {(uint64_t)kPfD * 2, (uint64_t)inner_heads * kPfD * 2};
+  const uint32_t box[3] = {64, 1, (uint32_t)kPfRows};
+  const int r = encode_map_3d(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, box, true);
+  if (r) return set_error(OC_ERR_CUDA, "oc_prefill_attention: tensor map for %s failed (CUresult %d)", what, r);
+  return OC_OK;
+}
+
+}  // namespace
+
+int prefill_status(int* status, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_prefill_status, sizeof(int));
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_prefill_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  }
+  return OC_OK;
+}
+
+}  // namespace oc
+
+using namespace oc;
+
+extern "C" int oc_prefill_attention(const void* q, const void* k, const void* v, int dtype,
+                                    const int32_t* idx, int idx_stride, int idx_head_stride,
+                                    const int32_t* count, int count_stride, int count_head_stride,
+                                    int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                    int seq_len, int block_size, int max_blocks,
+                                    void* out, int out_dtype, oc_stream_t stream) {
+  OC_REQUIRE(q && k && v && idx && count && out, OC_ERR_NULL, "oc_prefill_attention: NULL pointer");
+  OC_REQUIRE(dtype == OC_BF16, OC_ERR_DTYPE, "oc_prefill_attention: inputs must be bfloat16");
+  OC_REQUIRE(out_dtype == OC_BF16 || out_dtype == OC_F32, OC_ERR_DTYPE, "oc_prefill_attention: bad out dtype");
+  OC_REQUIRE(head_dim == kPfD, OC_ERR_SHAPE, "oc_prefill_attention: head_dim must be 128");
+  OC_REQUIRE(batch >= 1 && q_len >= 1 && kv_heads >= 1 && q_heads >= kv_heads && q_heads % kv_heads == 0,
+             OC_ERR_SHAPE, "oc_prefill_attention: bad batch / heads");
+  OC_REQUIRE(block_size >= kPfTok && block_size % kPfTok == 0, OC_ERR_SHAPE,
+             "oc_prefill_attention: block_size must be a multiple of 128");
+  OC_REQUIRE(seq_len >= block_size && seq_len % block_size == 0, OC_ERR_SHAPE,
+             "oc_prefill_attention: seq_len must be a multiple of block_size");
+  OC_REQUIRE(max_blocks >= 0 && max_blocks <= seq_len / block_size, OC_ERR_SHAPE,
+             "oc_prefill_attention: max_blocks out of range");
+  OC_REQUIRE(idx_stride >= 0 && idx_head_stride >= 0 && count_stride >= 0 && count_head_stride >= 0, OC_ERR_SHAPE,
+             "oc_prefill_attention: negative stride");
+  OC_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out), OC_ERR_ALIGN,
+             "oc_prefill_attention: q/k/v/out must be 16-byte aligned");
+  OC_REQUIRE((int64_t)batch * seq_len < INT32_MAX && (int64_t)batch * q_len < INT32_MAX, OC_ERR_SHAPE,
+             "oc_prefill_attention: too many rows");
+
+  PfArgs a;
+  a.idx = idx;
+  a.count = count;
+  a.out = out;
+  a.out_dtype = out_dtype;
+  a.B = batch;
+  a.Sq = q_len;
+  a.Hq = q_heads;
+  a.Hkv = kv_heads;
+  a.S = seq_len;
+  a.bs = block_size;
+  a.max_blocks = max_blocks;
+  a.idx_stride = idx_stride;
+  a.idx_hstride = idx_head_stride;
+  a.count_stride = count_stride;
+  a.count_hstride = count_head_stride;
+  a.G = q_heads / kv_heads;
+  a.nqt = (q_len + kPfRows - 1) / kPfRows;
+  a.tiles_per_head = a.G * a.nqt;
+  a.npairs = (a.tiles_per_head + 1) / 2;
+  const int64_t units = (int64_t)batch * kv_heads * a.npairs;
+  OC_REQUIRE(units < INT32_MAX, OC_ERR_SHAPE, "oc_prefill_attention: too many work units");
+  a.units = (int)units;
+  a.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+
+  CUtensorMap mq, mk, mv;
+  int rc = pf_map(&mq, q, q_heads, (int64_t)batch * q_len, "q");
+  if (!rc) rc = pf_map(&mk, k, kv_heads, (int64_t)batch * seq_len, "k");
+  if (!rc) rc = pf_map(&mv, v, kv_heads, (int64_t)batch * seq_len, "v");
+  if (rc) return rc;
+
+  auto kern = out_dtype == OC_BF16 ? prefill_attn_kernel<__nv_bfloat16> : prefill_attn_kernel<float>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfSmemBytes);
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_prefill_attention: %s", cudaGetErrorString(e));
+  const int sms = device_sm_count();
+  const int grid = (int)(units < sms ? units : sms);
+  kern<<<grid, kPfThreads, kPfSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, a);
+  return check_launch("prefill_attn_kernel");
+}

@@ -105,6 +105,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
                   uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128 = false);
 
+// Host: encode a 3-D tensor map (dims[0] innermost, byte strides of dims 1
+// and 2).  Returns 0 or a CUresult.
+int encode_map_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, const uint64_t dims[3],
+                  const uint64_t strides[2], const uint32_t box[3], bool swizzle128);
+
 // Host: encode a 4-D tensor map; dims[0] is innermost (contiguous), strides
 // are the byte strides of dims 1..3 in any order of size (a box is laid out
 // in shared memory dim 0 fastest, then 1, 2, 3).  Returns 0 or a CUresult.
