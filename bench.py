@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--evict", type=float, default=0.75)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--config", type=int, choices=[1, 2], default=1,
+                   help="1: decode layer (the headline metric); 2: chunked prefill on the tensor cores")
     return p.parse_args()
 
 
@@ -493,6 +495,181 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# configuration 2: chunked prefill (tensor-bound attention)
+# ---------------------------------------------------------------------------
+P_B, P_SQ, P_S = 4, 2048, 32768
+P_LAYERS = 2
+
+
+def run_prefill(args, rank, world, local_rank):
+    """Configuration 2: batch 4, 2048-query chunks against a 32,768-token
+    cache, 32/8 heads, D 128, bf16, keys of the 30/40/30 smooth / mid-band /
+    noise mixture, 75 % union eviction per batch row.  A step is one layer:
+    the fused scorer over all keys (bounds of all 8192 query rows of each KV
+    head), the compaction, and the tensor-core attention (oc_prefill_attention)
+    over the retained blocks.  With N > 1 every rank runs its own batch
+    (replicas: the chunked prefill does not shard across GPUs here)."""
+    import torch
+    import torch.distributed as dist
+    from orthocache_b200 import synthetic as syn, score_blocks, _lib
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    nb = P_S // 512
+    layers = []
+    for li in range(P_LAYERS):
+        L = Layer()
+        ks, vs, qs, taus, kept = [], [], [], [], []
+        for b in range(P_B):
+            seed = 10000 * rank + 100 * li + b
+            kinds = syn.block_kinds(nb, 0.3, 0.4, seed=seed)
+            ks.append(syn.make_keys(nb, HKV, D, kinds, seed=seed, device=device))
+            vs.append(syn.make_values(P_S, HKV, D, seed=seed, device=device))
+            qs.append(syn.make_queries(P_SQ, HQ, D, seed=seed, device=device))
+        L.k, L.v, L.q = torch.stack(ks), torch.stack(vs), torch.stack(qs)
+        del ks, vs, qs
+        sc = score_blocks(L.k, L.q, want=("zeta", "bound_max"))
+        for b in range(P_B):
+            t, kp = syn.calibrate_tau(sc["zeta"][b], sc["bound_max"][b], ZETA_MAX, args.evict)
+            taus.append(t)
+            kept.append(kp)
+        # τ is calibrated per batch row (the reference has no batch
+        # dimension) and the scorer takes one τ per call: one call per row
+        L.taus, L.kept = taus, kept
+        layers.append(L)
+    torch.cuda.synchronize()
+    keep = torch.empty((P_B, nb, HKV), dtype=torch.uint8, device=device)
+    perm = torch.empty((P_B, nb), dtype=torch.int32, device=device)
+    count = torch.empty((P_B,), dtype=torch.int32, device=device)
+    out = torch.empty((P_B, P_SQ, HQ, D), dtype=torch.bfloat16, device=device)
+    st = lambda: torch.cuda.current_stream().cuda_stream
+    rows_b = P_SQ * HQ * D * 2
+    kv_b = P_S * HKV * D * 2
+
+    f32 = dict(dtype=torch.float32, device=device)
+    dc = torch.empty((P_B, nb, HKV, D), **f32)
+    e_ac, zeta, bmax = (torch.empty((P_B, nb, HKV), **f32) for _ in range(3))
+    cells = nb * HKV
+
+    def score(L):
+        # one pass over all keys for the query-independent block metadata
+        # (DC, E_AC, zeta), the bounds of all 8192 query rows per KV head as a
+        # tiled GEMM, then the two gates with each batch row's own τ (the
+        # reference has no batch dimension; the synthetic rows are calibrated
+        # one by one)
+        _lib.call("oc_block_metadata", L.k.data_ptr(), 1, P_B, P_S, HKV, D, dc.data_ptr(), e_ac.data_ptr(),
+                  zeta.data_ptr(), st())
+        _lib.call("oc_score_from_metadata", dc.data_ptr(), e_ac.data_ptr(), zeta.data_ptr(), L.q.data_ptr(), 1, P_B,
+                  nb, HKV, D, P_SQ, HQ, -math.inf, ZETA_MAX, bmax.data_ptr(), None, None, st())
+        for b in range(P_B):
+            _lib.call("oc_apply_gates", bmax.data_ptr() + 4 * b * cells, zeta.data_ptr() + 4 * b * cells, cells,
+                      None, L.taus[b], ZETA_MAX, keep.data_ptr() + b * cells, st())
+
+    def compact():
+        _lib.call("oc_stream_compact", keep.data_ptr(), P_B, nb, HKV, perm.data_ptr(), count.data_ptr(), st())
+
+    def attend(L, q=None):
+        q = L.q if q is None else q
+        _lib.call("oc_prefill_attention", q.data_ptr(), L.k.data_ptr(), L.v.data_ptr(), 1, perm.data_ptr(), nb, 0,
+                  count.data_ptr(), 1, 0, P_B, P_SQ, HQ, HKV, D, P_S, 512, nb, out.data_ptr(), 1, st())
+
+    def step(L, q=None):
+        score(L)
+        compact()
+        attend(L, q)
+
+    for i in range(max(args.warmup, 3)):
+        step(layers[i % P_LAYERS])
+    torch.cuda.synchronize()
+    assert [int(c) for c in count.cpu()] == layers[(max(args.warmup, 3) - 1) % P_LAYERS].kept
+    K = max(4, min(args.steps, 200))
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, n):
+        a, b = ev(), ev()
+        torch.cuda.synchronize()
+        a.record()
+        for i in range(n):
+            fn(i)
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    with Clocks(local_rank) as clk:
+        if world > 1:
+            dist.barrier()
+        ms = timed(lambda i: step(layers[i % P_LAYERS]), K)
+        if world > 1:
+            dist.barrier()
+    # per-kernel launch durations (CUDA events on the launching stream); the
+    # retained lists of the last step stay in perm / count for the attention
+    ms_score = timed(lambda i: score(layers[i % P_LAYERS]), K)
+    step(layers[0])
+    ms_attn = timed(lambda i: attend(layers[0]), K)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # end to end: the chunk's queries from pinned host memory, the output back
+    q_host = [L.q.cpu().pin_memory() for L in layers]
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_dev = torch.empty_like(layers[0].q)
+    Ke = max(4, min(K, 50))
+
+    def e2e_step(i):
+        q_dev.copy_(q_host[i % P_LAYERS], non_blocking=True)
+        L = layers[i % P_LAYERS]
+        score(L)
+        compact()
+        attend(L, q_dev)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_step(0)
+    e2e_ms = timed(e2e_step, Ke)
+    if rank != 0:
+        return
+    kept = statistics.mean(statistics.mean(L.kept) for L in layers)
+    flops = 4.0 * P_B * HQ * P_SQ * (kept * 512) * D
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        tf_peak, tf_kind = float(pk["bf16_tflops"]), "measured (burst: the kernel is timed on its own)"
+    except Exception:
+        tf_peak, tf_kind = 1590.0, "fallback"
+    hbm, _ = peaks()
+    attn_tf = flops / (ms_attn * 1e-3) / 1e12
+    score_bytes = P_B * kv_b + P_B * rows_b
+    line = {
+        "metric": "chunked-prefill layer ms @32K ctx 75% evict (incl. scoring); attention TFLOP/s vs peak",
+        "value": round(ms, 4), "unit": "ms/layer", "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config2: chunked prefill B=4, Sq=2048, Hq=32/Hkv=8, D=128, bf16, 32768 tokens, "
+                               "30/40/30 smooth/mid/noise keys, evict=%.2f per batch row, zeta_max=5" % args.evict,
+                   "l2": "inputs > L2: 2 layers of KV (2 x 537 MB) alternate per step",
+                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"},
+        "roofline": {"bound": "tensor", "kernel": "prefill_attn_kernel (tcgen05, TMEM accumulators)",
+                     "achieved": round(attn_tf, 1), "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": round(attn_tf / tf_peak, 4), "traffic": None, "peak_kind": tf_kind,
+                     "flops_per_launch": flops, "launch_ms": round(ms_attn, 4),
+                     "how": "4*B*Hq*Sq*(retained tokens)*D FLOPs over the median-free average launch time of K "
+                            "back-to-back launches bracketed by CUDA events"},
+        "scorer": {"launch_ms": round(ms_score, 4), "bytes": score_bytes,
+                   "achieved_gbs": round(score_bytes / (ms_score * 1e-3) / 1e9, 1),
+                   "frac": round(score_bytes / (ms_score * 1e-3) / 1e9 / hbm, 4),
+                   "note": "oc_block_metadata over all keys + bound GEMM (oc_score_from_metadata) + per-row gates; "
+                           "bytes = keys + queries"},
+        "cpu_baseline": None,
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms/layer", "h2d_bytes_per_step": P_B * rows_b,
+                "d2h_bytes_per_step": P_B * rows_b,
+                "note": "queries of the chunk from pinned host memory, attention output back; KV cache resident"},
+        "gpu_launches": K * (1 + 3 + P_B + 1 + 1),
+        "clocks": clk.summary(),
+        "retained_blocks": kept,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -507,7 +684,10 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.config == 2:
+            run_prefill(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             dist.destroy_process_group()

@@ -43,7 +43,8 @@ enum oc_status {
   OC_ERR_CAPACITY = -4,    /* workspace too small / size above a limit */
   OC_ERR_DTYPE = -5,       /* unsupported dtype */
   OC_ERR_CUDA = -6,        /* CUDA runtime error (message has details) */
-  OC_ERR_UNSUPPORTED = -7  /* valid request this build does not implement */
+  OC_ERR_UNSUPPORTED = -7, /* valid request this build does not implement */
+  OC_ERR_COMM = -8         /* NCCL error (message has details) */
 };
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -59,6 +60,12 @@ const char* oc_last_error(void);
  * attention; bit 2: chunked-prefill attention.  Synchronises the current device; reset != 0 clears it.
  * Returns the status (>= 0) or an OC_ERR_* code. */
 int oc_device_status(int reset);
+
+/* Limit of every bounded wait in the kernels of the current device (default
+ * 2 s; 1 us .. 60 s): after it a wait gives up, the kernel records the status
+ * above and returns.  Meant for tests and watchdogs that want a failure to
+ * surface fast; no counterpart in the reference (JAX has no device waits). */
+int oc_set_wait_limit_ns(uint64_t ns);
 
 /* ---------------------------------------------------------------------------
  * fwht_512 — replaces `fwht_512(x)` (src/orthocache/fwht.py:4-65).
@@ -382,6 +389,80 @@ int oc_partial_attention(const void* q, const void* k, const void* v, int dtype,
                          int seq_len, int block_size, int max_blocks,
                          float* m, float* l, float* o,
                          void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Sequence-parallel exchange over NCCL (one rank per GPU).  `comm` is an
+ * ncclComm_t created by the caller (any NCCL 2.x: the library resolves NCCL
+ * at run time, preferring the copy already loaded in the process, else
+ * libnccl.so.2 or the path in the environment variable OC_NCCL_LIBRARY) or
+ * by oc_comm_init.  The reference's pmap axis (axis_name) becomes this
+ * communicator.  Calls are collective: every rank makes the same call in the
+ * same order.
+ */
+/* NCCL_VERSION_CODE of the NCCL in use, or OC_ERR_UNSUPPORTED. */
+int oc_nccl_version(void);
+/* A 128-byte ncclUniqueId (rank 0), to be shared with the other ranks. */
+int oc_comm_unique_id(void* id_out);
+/* ncclCommInitRank on the current device. */
+int oc_comm_init(void** comm_out, const void* id, int nranks, int rank);
+int oc_comm_destroy(void* comm);
+/* Host-side failure detection: OC_ERR_COMM (with NCCL's message) if the
+ * communicator holds an asynchronous error (a peer failed or aborted), else 0.
+ * A watchdog polls it and calls oc_comm_abort to release blocked ranks. */
+int oc_comm_check(void* comm);
+int oc_comm_abort(void* comm);
+
+/* Workspace of oc_exchange_stratified / oc_alltoallv_heads: the packed K
+ * and V send buffers of one shard of num_blocks blocks. */
+size_t oc_exchange_workspace_bytes(int num_blocks, int kv_heads, int head_dim, int dtype, int block_size);
+
+/* Stratified all-gather of the retained blocks — replaces build_stratified
+ * (benchmarks/phase_e_stratified.py:164-273) and the exchange of
+ * distributed_orthocache_attention (distributed_attention.py:156-191).
+ * k, v: this shard (num_blocks * block_size, kv_heads, head_dim); idx, count:
+ * its compaction (oc_stream_compact).  Gathers every rank's count into
+ * all_counts (P, device), reads them on the host (the one synchronisation:
+ * the bucket sizes the collective), picks bucket = oc_stratified_bucket(
+ * num_blocks, max count), packs this rank's first `bucket` retained blocks
+ * (zero tail) and all-gathers them: k_recv / v_recv (P * num_blocks *
+ * block_size, kv_heads, head_dim) hold P chunks of `bucket` blocks in rank
+ * order (capacity for the largest bucket, num_blocks).  order / total: the
+ * valid-slot index of oc_exchange_index over the P * bucket gathered slots,
+ * ready for oc_indirect_attention.  *bucket_out (nullable) = bucket.  Blocks
+ * are bit-exact copies. */
+int oc_exchange_stratified(void* comm, const void* k, const void* v, int dtype, const int32_t* idx,
+                           const int32_t* count, int num_blocks, int kv_heads, int head_dim, int block_size,
+                           void* k_recv, void* v_recv, int32_t* all_counts, int32_t* order, int32_t* total,
+                           int* bucket_out, void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
+/* AllToAllv of the retained blocks by KV head — the exchange of
+ * alltoallv_kv_exchange (alltoallv.py:217-259, 340-440) with each rank
+ * receiving only the KV heads it owns (rank r: heads r*H/P .. (r+1)*H/P - 1;
+ * kv_heads % P == 0) instead of every head: grouped ncclSend / ncclRecv with
+ * per-peer sizes from the count all-gather (read on the host).  k_recv /
+ * v_recv: (P * num_blocks * block_size, kv_heads / P, head_dim) capacity;
+ * the first total blocks are every rank's retained blocks of this rank's
+ * heads in rank order (the layout unpack_received_blocks leaves), so they
+ * are attended to with idx = 0, 1, ..., total - 1.  *total_out (nullable) =
+ * total.  Bit-exact copies. */
+int oc_alltoallv_heads(void* comm, const void* k, const void* v, int dtype, const int32_t* idx,
+                       const int32_t* count, int num_blocks, int kv_heads, int head_dim, int block_size,
+                       void* k_recv, void* v_recv, int32_t* all_counts, int* total_out, void* workspace,
+                       size_t workspace_bytes, oc_stream_t stream);
+
+/* One decode layer of sequence-parallel attention through NCCL: the fused
+ * layer of this rank's shard writes its (m, l, o) partial
+ * (oc_decode_step_partial), the P packed partials are all-gathered, and the
+ * log-sum-exp merge writes out on every rank — attention over the union of
+ * all shards' retained blocks (distributed_attention.py:95-128 across
+ * devices).  No KV block crosses NVLink.  Workspace: the size below,
+ * zero-filled once (its leading region is oc_decode_step's). */
+size_t oc_decode_step_sharded_workspace_bytes(int nranks, int batch, int q_len, int q_heads, int kv_heads,
+                                              int head_dim, int seq_len);
+int oc_decode_step_sharded(void* comm, const void* q, const void* k, const void* v, int dtype, int batch,
+                           int q_len, int q_heads, int kv_heads, int head_dim, int seq_len, float tau,
+                           float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count, void* out, int out_dtype,
+                           void* workspace, size_t workspace_bytes, oc_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -31,6 +31,7 @@ SIGNATURES = {
     "oc_status_string": (C.c_char_p, [_i]),
     "oc_last_error": (C.c_char_p, []),
     "oc_device_status": (_i, [_i]),
+    "oc_set_wait_limit_ns": (_i, [C.c_uint64]),
     "oc_fwht512": (_i, [_p, _i, _i64, _p, _p]),
     "oc_score_blocks": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _f, _f,
                              _p, _p, _p, _p, _p, _p, _p, _p, _i, _p]),
@@ -43,6 +44,19 @@ SIGNATURES = {
     "oc_bucket_count": (_i, [_p, _i, _i, _p, _p]),
     "oc_apply_gates": (_i, [_p, _p, _i64, _p, _f, _f, _p, _p]),
     "oc_indirect_attention_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
+    "oc_nccl_version": (_i, []),
+    "oc_comm_unique_id": (_i, [_p]),
+    "oc_comm_init": (_i, [C.POINTER(_p), _p, _i, _i]),
+    "oc_comm_destroy": (_i, [_p]),
+    "oc_comm_check": (_i, [_p]),
+    "oc_comm_abort": (_i, [_p]),
+    "oc_exchange_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "oc_exchange_stratified": (_i, [_p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, C.POINTER(_i),
+                                    _p, _sz, _p]),
+    "oc_alltoallv_heads": (_i, [_p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _p, _p, _p, C.POINTER(_i), _p, _sz, _p]),
+    "oc_decode_step_sharded_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
+    "oc_decode_step_sharded": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p, _p, _p, _i, _p, _sz,
+                                    _p]),
     "oc_indirect_attention": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
                                    _i, _p, _i, _p, _sz, _p]),
     "oc_prefill_attention": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,

@@ -1522,6 +1522,7 @@ extern "C" int oc_empty_heads_mean(const void* v, int dtype, const int32_t* coun
 }
 
 namespace oc {
+int wait_limit_attn(unsigned long long ns) { return set_wait_limit_here(ns); }
 int attn_status(int* status, int reset) {
   cudaError_t e = cudaMemcpyFromSymbol(status, g_attn_status, sizeof(int));
   if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));

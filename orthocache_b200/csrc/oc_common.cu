@@ -1,5 +1,10 @@
 // Error state, status strings and small host utilities shared by all entry points.
 #include "oc_common.cuh"
+#include "oc_tma.cuh"
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
 
 #include <stdarg.h>
 #include <stdio.h>
@@ -24,10 +29,57 @@ int check_launch(const char* what) {
 }
 
 int device_sm_count() {
+  static std::atomic<int> cache[kMaxCachedDevices] = {};
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
-  return n > 0 ? n : 148;
+  if (dev >= 0 && dev < kMaxCachedDevices && (n = cache[dev].load(std::memory_order_relaxed)) > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  if (dev >= 0 && dev < kMaxCachedDevices) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+bool first_on_device(std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxCachedDevices) return true;
+  const uint64_t bit = 1ull << dev;
+  if (done.load(std::memory_order_acquire) & bit) return false;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
+}
+
+// Encoded tensor maps by (kind, base address, shape): encoding goes through
+// the driver and costs microseconds per map, and decode loops pass the same
+// few buffers every call.  A map depends only on the address and the shape,
+// so an entry stays valid whatever happens to the memory behind it.
+namespace {
+struct MapEntry {
+  uint64_t key[4];
+  CUtensorMap map;
+  bool used;
+};
+constexpr int kMapCache = 64;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+std::mutex g_map_mu;
+}  // namespace
+
+bool map_cache_get(const uint64_t key[4], CUtensorMap* out) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  for (int i = 0; i < kMapCache; ++i)
+    if (g_maps[i].used && !memcmp(g_maps[i].key, key, sizeof(g_maps[i].key))) {
+      *out = g_maps[i].map;
+      return true;
+    }
+  return false;
+}
+
+void map_cache_put(const uint64_t key[4], const CUtensorMap& map) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  MapEntry& e = g_maps[g_map_next];
+  g_map_next = (g_map_next + 1) % kMapCache;
+  memcpy(e.key, key, sizeof(e.key));
+  e.map = map;
+  e.used = true;
 }
 
 }  // namespace oc
@@ -46,6 +98,7 @@ const char* oc_status_string(int s) {
     case OC_ERR_DTYPE: return "unsupported dtype";
     case OC_ERR_CUDA: return "CUDA error";
     case OC_ERR_UNSUPPORTED: return "unsupported";
+    case OC_ERR_COMM: return "NCCL error";
     default: return "unknown status";
   }
 }
@@ -127,6 +180,16 @@ int encode_map_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, co
 }
 
 }  // namespace oc
+
+extern "C" int oc_set_wait_limit_ns(uint64_t ns) {
+  OC_REQUIRE(ns >= 1000 && ns <= 60000000000ull, OC_ERR_SHAPE, "oc_set_wait_limit_ns: %llu ns outside [1 us, 60 s]",
+             (unsigned long long)ns);
+  int e = oc::wait_limit_score(ns);
+  if (!e) e = oc::wait_limit_attn(ns);
+  if (!e) e = oc::wait_limit_prefill(ns);
+  if (e) return oc::set_error(OC_ERR_CUDA, "oc_set_wait_limit_ns: %s", cudaGetErrorString((cudaError_t)e));
+  return OC_OK;
+}
 
 extern "C" int oc_device_status(int reset) {
   int s1 = 0, s2 = 0;

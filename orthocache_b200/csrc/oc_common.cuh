@@ -6,6 +6,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <stddef.h>
+#include <atomic>
 #include <utility>
 
 #include "../../include/orthocache_b200.h"
@@ -19,12 +20,20 @@ namespace oc {
 // ---------------------------------------------------------------------------
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
-int device_sm_count();
+int device_sm_count();  // cached per device
+constexpr int kMaxCachedDevices = 64;
+// True the first time it is called for the current device (per `done`
+// mask): per-device set-up such as cudaFuncSetAttribute runs once.
+bool first_on_device(std::atomic<uint64_t>& done);
 // Device-side error status of the pipelined kernels (a bounded wait gave up):
 // copies it to *status (0 = none) and clears it if reset.  Synchronous.
 int score_status(int* status, int reset);
 int attn_status(int* status, int reset);
 int prefill_status(int* status, int reset);
+// Set the bounded-wait limit of the kernels of each translation unit.
+int wait_limit_score(unsigned long long ns);
+int wait_limit_attn(unsigned long long ns);
+int wait_limit_prefill(unsigned long long ns);
 
 // Fused decode layer (score, compact, attend and merge in one persistent
 // kernel; oc_score.cu).  decode_fused_bytes: workspace it needs; it must be

@@ -17,21 +17,24 @@
 //     tensor pipe alternates between them while the other tile's softmax runs;
 //   * warp 8 is the TMA producer: the unit's two query tiles (32 KB each,
 //     128B-swizzled boxes of 128 rows x 64 channels), then K_0, V_0, K_1,
-//     V_1, ... (128 tokens x 128 channels, 32 KB each) into a 3-slot ring;
+//     V_1, ... (128 tokens x 128 channels, 32 KB each) into a 5-slot ring;
 //   * warp 9 allocates 512 tensor-memory columns (per tile: S = 128 fp32
 //     columns, O = 128 fp32 columns) and one of its threads issues every
-//     tcgen05.mma: S_t = Q_t K_j^T (A and B K-major) and O_t += P_t V_j
-//     (P K-major from shared memory, V MN-major), 8 instructions of
-//     M128 N128 K16 each, with tcgen05.commit to mbarriers;
+//     tcgen05.mma: S_t = Q_t K_j^T (A and B K-major in shared memory) and
+//     O_t += P_t V_j (P from tensor memory, V MN-major in shared memory),
+//     8 instructions of M128 N128 K16 each, with tcgen05.commit to mbarriers;
 //   * warps 0-3 / 4-7 are the softmax warpgroups of tile 0 / 1: each thread
 //     owns one query row (tensor-memory lane), loads its 128 logits with
-//     tcgen05.ld, keeps the running max and sum, writes P in bf16 into a
-//     128B-swizzled shared-memory tile, and rescales O in tensor memory only
-//     when its row max grows by more than 2^8 (the stale max stays exact: the
-//     final o / l uses the same max for both);
+//     tcgen05.ld, keeps the running max and sum, writes P as bfloat16 pairs
+//     over the logits in tensor memory (tcgen05.st), and rescales O in tensor
+//     memory only when its row max grows by more than 2^8 (the stale max
+//     stays exact: the final o / l uses the same max for both); a quarter of
+//     the exponentials run as a polynomial on the FMA pipe to unload MUFU;
 //   * the issue order per KV tile j is PV_0(j-1), S_0(j), PV_1(j-1), S_1(j):
 //     the commit that publishes S_t(j) also covers PV_t(j-1), so a softmax
-//     warpgroup that sees S_t(j) may rescale O_t and overwrite P_t.
+//     warpgroup that sees S_t(j) may rescale O_t and overwrite P_t, and
+//     tensor-core operations of one thread run in issue order, so S_t(j+1)
+//     overwrites P_t(j) only after PV_t(j) has read it.
 // Every mbarrier wait is bounded; a wait that gives up sets g_prefill_status
 // and an abort flag so that all warps leave their loops and the CTA frees its
 // tensor memory.
@@ -53,7 +56,7 @@ namespace {
 constexpr int kPfRows = 128;        // query rows per tile (UMMA M)
 constexpr int kPfTok = 128;         // tokens per K/V tile (UMMA N of QK^T, K of PV)
 constexpr int kPfD = 128;           // head_dim
-constexpr int kPfSlots = 3;         // K/V ring slots
+constexpr int kPfSlots = 5;         // K/V ring slots
 constexpr int kPfTileBytes = kPfRows * kPfD * 2;  // 32 KB, every tile in the kernel
 constexpr int kPfBoxBytes = kPfTileBytes / 2;     // one 128 x 64 box
 constexpr int kPfThreads = 320;
@@ -64,7 +67,6 @@ constexpr int kPfTmemCols = 512;
 struct PfSmem {
   // tiles first, each 1024-byte aligned (the 128B swizzle repeats every 1024 B)
   unsigned char q[2][kPfTileBytes];
-  unsigned char p[2][kPfTileBytes];
   unsigned char kv[kPfSlots][kPfTileBytes];
   uint64_t kv_full[kPfSlots], kv_empty[kPfSlots];
   uint64_t q_full, q_empty;
@@ -108,6 +110,17 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t 
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Same with A read from tensor memory (128 lanes = rows, K packed two bf16
+// per 32-bit column).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, int acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 
@@ -161,6 +174,29 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
         "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
         "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
       : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+        "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+        "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// 2^x on the FMA pipe, for the share of the exponentials taken off the MUFU
+// unit: x = n + f with n = floor(x), 2^f by the cubic through the four
+// Chebyshev nodes of [0, 1) (relative error < 1e-4, below the bfloat16
+// rounding that P gets), 2^n added to the exponent field.  x >= -127.
+__device__ __forceinline__ float poly_ex2(float x) {
+  x = fmaxf(x, -127.f);
+  const float n = floorf(x);
+  const float f = x - n;
+  const float p = fmaf(fmaf(fmaf(0.0789672570f, f, 0.2246931558f), f, 0.6963247711f), f, 0.9999002882f);
+  return __int_as_float(__float_as_int(p) + ((int)n << 23));
 }
 
 __device__ __forceinline__ float fast_ex2(float x) {
@@ -251,8 +287,6 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
   const int warp_lane0 = (threadIdx.x & 96);   // first TMEM lane of this warp
   const uint32_t t_s = tmem + ((uint32_t)warp_lane0 << 16) + t * 256;
   const uint32_t t_o = t_s + 128;
-  unsigned char* pt = sm.p[t];
-  const uint32_t sw = row & 7;
   uint32_t s_ph = 0;
   for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
     const PfUnit w = pf_unit(a, u);
@@ -276,15 +310,15 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
       if (pf_aborted(sm) || !pf_wait(sm, &sm.s_full[t], s_ph)) { ok = false; break; }
       s_ph ^= 1;
       tc_fence_after();
-      // Row max in two halves (64 columns each, to stay within the register
-      // budget of 3 warps per SM sub-partition); the second half stays in
-      // registers for the exponentials, the first is read again.
+      // Row max over the 128 logits in two halves of 64 columns (the register
+      // budget is that of 3 warps per SM sub-partition); the first half stays
+      // in registers for its exponentials, the second is read again.
       float s[64];
-      tmem_ld64_wait(t_s, s);
+      tmem_ld64_wait(t_s + 64, s);
       float mx = s[0];
 #pragma unroll
       for (int i = 1; i < 64; ++i) mx = fmaxf(mx, s[i]);
-      tmem_ld64_wait(t_s + 64, s);
+      tmem_ld64_wait(t_s, s);
 #pragma unroll
       for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
       mx *= a.scale_log2;
@@ -301,35 +335,37 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
             tmem_st32(t_o + 32 * c, o);
           }
-          tc_wait_st();
         }
         l *= alpha;
         m_used = m_new;
       }
-      // P = exp2(s * scale - m) in bf16, K-major 128B-swizzled: tokens 0-63
-      // in the first 16 KB box, 64-127 in the second.
+      // P = exp2(s * scale - m) as bfloat16 pairs written over S in tensor
+      // memory (column c holds tokens 2c, 2c + 1), the A operand of P.V.
+      // Tokens 0-63 go to columns 0-31, whose logits are already in
+      // registers; tokens 64-127 to columns 32-63, after their logits (columns
+      // 64-127, untouched so far) have been read.  One chunk of 8 in 4 takes
+      // its exponentials on the FMA pipe.
       float rs = 0.f;
 #pragma unroll
-      for (int half = 1; half >= 0; --half) {
-        if (half == 0) tmem_ld64_wait(t_s, s);
+      for (int half = 0; half < 2; ++half) {
+        if (half == 1) tmem_ld64_wait(t_s + 64, s);
+        uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           float p[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            p[i] = fast_ex2(fmaf(s[8 * c + i], a.scale_log2, -m_used));
+            const float x = fmaf(s[8 * c + i], a.scale_log2, -m_used);
+            p[i] = (c & 3) == 3 ? poly_ex2(x) : fast_ex2(x);
             rs += p[i];
           }
-          uint4 v;
-          v.x = pack_bf16x2(p[0], p[1]);
-          v.y = pack_bf16x2(p[2], p[3]);
-          v.z = pack_bf16x2(p[4], p[5]);
-          v.w = pack_bf16x2(p[6], p[7]);
-          *reinterpret_cast<uint4*>(pt + half * kPfBoxBytes + row * 128 + ((c ^ sw) << 4)) = v;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pk[4 * c + i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
         }
+        tmem_st32u(t_s + 32 * half, pk);
       }
+      tc_wait_st();  // P and any rescaled O are in tensor memory
       l += rs;
-      fence_proxy_async();  // P (generic-proxy writes) is read by the tensor core
       tc_fence_before();
       mbar_arrive(&sm.p_full[t]);
     }
@@ -356,7 +392,7 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
 __device__ void pf_producer(PfSmem& sm, const PfArgs& a, const CUtensorMap* mq, const CUtensorMap* mk,
                             const CUtensorMap* mv) {
   uint32_t q_ph = 0;
-  uint32_t L = 0;  // running K/V load index: slot L % 3, use L / 3
+  uint32_t L = 0;  // running K/V load index: slot L % kPfSlots, use L / kPfSlots
   for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
     const PfUnit w = pf_unit(a, u);
     if (w.n == 0) continue;
@@ -412,7 +448,7 @@ __device__ void pf_mma(PfSmem& sm, const PfArgs& a, uint32_t tmem) {
       for (int t = 0; t < 2; ++t) {
         if (t >= w.ntile) break;
         const uint32_t d_s = tmem + t * 256, d_o = d_s + 128;
-        const uint32_t qa = smem_u32(sm.q[t]), pa = smem_u32(sm.p[t]);
+        const uint32_t qa = smem_u32(sm.q[t]);
         if (j > 0) {
           if (pf_aborted(sm) || !pf_wait(sm, &sm.p_full[t], (p_ph >> t) & 1)) return;
           p_ph ^= 1u << t;
@@ -420,9 +456,8 @@ __device__ void pf_mma(PfSmem& sm, const PfArgs& a, uint32_t tmem) {
           const uint32_t vb = smem_u32(sm.kv[vslot_prev]);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = sdesc(pa + (kk >> 2) * kPfBoxBytes + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = sdesc(vb + kk * 2048, kPfBoxBytes, 1024);
-            umma_bf16(d_o, ad, bd, kIdPV, (j > 1 || kk > 0) ? 1 : 0);
+            umma_bf16_ts(d_o, d_s + kk * 8, bd, kIdPV, (j > 1 || kk > 0) ? 1 : 0);
           }
           if (t == w.ntile - 1) umma_commit(&sm.kv_empty[vslot_prev]);
         }
@@ -513,13 +548,17 @@ int pf_map(CUtensorMap* m, const void* base, int inner_heads, int64_t rows, cons
   const uint64_t dims[3] = {(uint64_t)kPfD, (uint64_t)inner_heads, (uint64_t)rows};
   const uint64_t strides[2] = {(uint64_t)kPfD * 2, (uint64_t)inner_heads * kPfD * 2};
   const uint32_t box[3] = {64, 1, (uint32_t)kPfRows};
+  const uint64_t key[4] = {3, (uint64_t)base, (uint64_t)inner_heads, (uint64_t)rows};
+  if (map_cache_get(key, m)) return OC_OK;
   const int r = encode_map_3d(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, box, true);
   if (r) return set_error(OC_ERR_CUDA, "oc_prefill_attention: tensor map for %s failed (CUresult %d)", what, r);
+  map_cache_put(key, *m);
   return OC_OK;
 }
 
 }  // namespace
 
+int wait_limit_prefill(unsigned long long ns) { return set_wait_limit_here(ns); }
 int prefill_status(int* status, int reset) {
   cudaError_t e = cudaMemcpyFromSymbol(status, g_prefill_status, sizeof(int));
   if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
@@ -592,8 +631,11 @@ extern "C" int oc_prefill_attention(const void* q, const void* k, const void* v,
   if (rc) return rc;
 
   auto kern = out_dtype == OC_BF16 ? prefill_attn_kernel<__nv_bfloat16> : prefill_attn_kernel<float>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfSmemBytes);
-  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_prefill_attention: %s", cudaGetErrorString(e));
+  static std::atomic<uint64_t> s_setup[2] = {{0}, {0}};
+  if (first_on_device(s_setup[out_dtype == OC_BF16])) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfSmemBytes);
+    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_prefill_attention: %s", cudaGetErrorString(e));
+  }
   const int sms = device_sm_count();
   const int grid = (int)(units < sms ? units : sms);
   kern<<<grid, kPfThreads, kPfSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, a);

@@ -545,6 +545,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   __shared__ __align__(8) uint64_t empty[kStages];  // fused: stage free for the producer
   __shared__ int s_desc[kStages];            // fused: unit in a stage (block * 4 + chunk), -1 = end
   __shared__ int s_set;                      // fused: counter set of this call
+  __shared__ __align__(8) uint64_t setbar;   // fused: s_set is known (after the previous kernel)
   __shared__ int s_merge;                    // fused: this CTA merges its group
   __shared__ int s_rel[kStages];             // warps done with a stage
   __shared__ __align__(8) uint64_t tfull[NBUF], tempty[NBUF];  // tile buffer hand-over
@@ -594,6 +595,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); s_rel[i] = 0; }
     for (int i = 0; i < NBUF; ++i) { mbar_init(&tfull[i], kW); mbar_init(&tempty[i], 1); }
+    mbar_init(&setbar, 1);
     fence_mbar_init();
     s_abort = 0;
     s_merge = 0;
@@ -604,27 +606,17 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     // scorer, compaction or attention kernels, and none of them writes keys.
     for (int k = 0; k < kStages && k < n_units; ++k) issue(k);
   }
-  // Launched as a programmatic dependent: everything above overlaps the
-  // previous kernel; queries, outputs and the workspace are touched only
-  // after it.
+  // Launched as a programmatic dependent: the kernel may start while the one
+  // before it in the stream (one of this library's, which write no keys and
+  // no queries) is still running.  Streaming and transforming the keys and
+  // staging the queries only read inputs, so they start at once; the
+  // epilogue warps wait for the previous kernel (pdl_wait) before the first
+  // write of an output or of the workspace, the compute warps before the
+  // attention phase.
   pdl_trigger();
-  pdl_wait();
-  if (tid == 0) {
-    if constexpr (FUSED) s_set = __ldcg(f.epoch) & 1;
-    OC_SSTAMP(8, globaltimer_ns());
-  }
-  __syncthreads();  // the only CTA-wide barrier
+  __syncthreads();  // barrier initialisation is visible; the only CTA-wide barrier
   if (tid == 0) OC_SSTAMP(1, globaltimer_ns());
   FusedSet fs = {};
-  if constexpr (FUSED) {
-    fs = fused_set(f, a.nb, s_set);
-    if (blockIdx.x == 0) {
-      // The other set was last used by the previous call, which has
-      // completed: clear it for the next call.
-      int* other = f.sets + (size_t)(s_set ^ 1) * f.set_ints;
-      for (int i = tid; i < f.set_ints; i += kFusedThreads) other[i] = 0;
-    }
-  }
 #ifdef OC_TIMING
   unsigned long long t_wait = 0;
 #endif
@@ -653,6 +645,23 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         if (lane == 0) s_qn[r] = nrm;
       }
       asm volatile("bar.sync 1, %0;" ::"r"(NE * 32) : "memory");
+    }
+    // Outputs and the workspace are written from here on.
+    pdl_wait();
+    if constexpr (FUSED) {
+      if (e == 0 && lane == 0) {
+        s_set = __ldcg(f.epoch) & 1;
+        OC_SSTAMP(8, globaltimer_ns());
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(NE * 32) : "memory");
+      fs = fused_set(f, a.nb, s_set);
+      if (blockIdx.x == 0) {
+        // The other set was last used by the previous call, which has
+        // completed: clear it for the next call.
+        int* other = f.sets + (size_t)(s_set ^ 1) * f.set_ints;
+        for (int i = e * 32 + lane; i < f.set_ints; i += NE * 32) other[i] = 0;
+      }
+      if (e == 0 && lane == 0) mbar_arrive(&setbar);  // the compute warps may read s_set
     }
     for (int tile = e; tile < my_tiles; tile += NE) {
       const int tb = e;
@@ -839,7 +848,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                   const int rw = ld_acquire(fs.row + b);
                   if ((rw & 0xffff) == a.nb && slot >= (rw >> 16)) break;  // past the last kept block
                 }
-                if (globaltimer_ns() - t0 > kWaitLimitNs) { s_abort = 1; atomicExch(&g_score_status, 1); break; }
+                if (globaltimer_ns() - t0 > g_wait_limit_ns) { s_abort = 1; atomicExch(&g_score_status, 1); break; }
                 __nanosleep(32);
                 v = ld_relaxed(qb + slot);
               }
@@ -996,6 +1005,14 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
 scored:
   if constexpr (FUSED) {
     static_assert(!FUSED || D == 128, "the fused decode layer is built for head_dim 128");
+    // The attention phase writes partials into the workspace: after the
+    // previous kernel, with this call's counter set.
+    if (!__all_sync(0xffffffffu, mbar_wait(&setbar, 0))) {
+      s_abort = 1;
+      if (lane == 0) atomicExch(&g_score_status, 1);
+    }
+    pdl_wait();
+    fs = fused_set(f, a.nb, s_set);
     // ---- attention over the retained blocks of group (bq, hq) ----
     const int grp = blockIdx.x % f.NG, bq = grp / a.H, hq = grp % a.H;
     const int tg = warp & 7;    // tokens 16 tg .. 16 tg + 15 of each unit
@@ -1307,10 +1324,15 @@ int encode_score_map(CUtensorMap* map, const void* keys, int H, int D, int64_t b
 template <int D>
 int launch_tma(const ScoreArgs& a, int ntiles, cudaStream_t st) {
   CUtensorMap map;
-  int rc = encode_score_map(&map, a.keys, a.H, D, ntiles / a.H);
+  const uint64_t key[4] = {1, (uint64_t)a.keys, (uint64_t)a.H | ((uint64_t)D << 32), (uint64_t)(ntiles / a.H) * kBlock};
+  int rc = 0;
+  if (!map_cache_get(key, &map) && !(rc = encode_score_map(&map, a.keys, a.H, D, ntiles / a.H)))
+    map_cache_put(key, map);
   if (rc) return set_error(OC_ERR_CUDA, "oc_score_blocks: tensor map encode failed (%d)", rc);
   const int smem = kStages * kSlabB + kQCacheBytes + 1024;
-  cudaFuncSetAttribute(score_tma_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  static std::atomic<uint64_t> s_setup{0};
+  if (first_on_device(s_setup))
+    cudaFuncSetAttribute(score_tma_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int grid = ntiles < device_sm_count() ? ntiles : device_sm_count();
   const FusedArgs none = {};
   const cudaError_t e = launch_pdl(score_tma_kernel<D, false>, dim3(grid), dim3(kScoreThreads + kEpiWarps * 32),
@@ -1509,6 +1531,155 @@ meta_gates_kernel(const float* __restrict__ dc, const float* __restrict__ e_ac, 
 }  // namespace
 }  // namespace oc
 
+namespace oc {
+namespace {
+// ---------------------------------------------------------------------------
+// The same gates for long query chunks (chunked prefill: thousands of query
+// rows per KV head).  The bounds of all rows against all blocks are a small
+// float32 GEMM (rows x D) . (D x blocks) per (batch, KV head), tiled so that
+// every query row is read once per 64 blocks instead of once per block:
+//   meta_bound_init_kernel  bound_max <- ordered key of -inf
+//   meta_bound_gemm_kernel  CTA = 128 rows x 64 blocks of one (b, h); each
+//                           thread 8 rows x 4 blocks; row norms on the way;
+//                           bound per (row, block) (optionally stored), max
+//                           over the CTA's rows, atomicMax of the ordered
+//                           integer key into bound_max
+//   meta_bound_gates_kernel key -> float, keep = bound >= tau && zeta <= zeta_max
+// The per-term arithmetic is the warp kernel's: mean = DC / sqrt(512) in
+// float32, dot in float32, bound = dot / sqrt(D) + sqrt(|q|^2) sqrt(E_AC) / sqrt(D).
+// ---------------------------------------------------------------------------
+// Monotone map of float32 onto int32 (for atomicMax over floats of any sign).
+__device__ __forceinline__ int f2key(float f) {
+  const int i = __float_as_int(f);
+  return i >= 0 ? i : i ^ 0x7fffffff;
+}
+__device__ __forceinline__ float key2f(int k) { return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff); }
+
+__global__ void meta_bound_init_kernel(int* key, int64_t cells) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < cells) key[i] = f2key(-INFINITY);
+}
+
+constexpr int kMbRows = 128, kMbBlk = 64, kMbK = 32;
+constexpr int kMetaGemmMinRows = 32;  // query rows per KV head above which the GEMM form is used
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+meta_bound_gemm_kernel(const float* __restrict__ dc, const float* __restrict__ e_ac, const T* __restrict__ q,
+                       int nb, int H, int D, int Sq, int Hq, int G, int* key, float* bounds) {
+  __shared__ float qs[kMbK][kMbRows + 4];
+  __shared__ float ds[kMbK][kMbBlk + 4];
+  __shared__ float s_nrm[kMbRows];
+  __shared__ float s_max[16][kMbBlk];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int bh = blockIdx.y, h = bh % H, b = bh / H;
+  const int r0 = blockIdx.x * kMbRows, j0 = blockIdx.z * kMbBlk;
+  const int rows = Sq * G;
+  // loader roles: q row lr (two threads per row, 16 dims each), dc block ld
+  const int lr = tid >> 1, lhalf = tid & 1;
+  const int grow = r0 + lr;
+  const T* qrow = nullptr;
+  if (grow < rows) {
+    const int s = grow / G, g = grow - s * G;
+    qrow = q + (((size_t)b * Sq + s) * Hq + (size_t)h * G + g) * D;
+  }
+  const int lb = tid >> 2, lq = tid & 3;  // dc: block lb, 8 dims at lq*8
+  const float* dcrow = (j0 + lb < nb) ? dc + (((size_t)b * nb + j0 + lb) * H + h) * D : nullptr;
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[i][c] = 0.f;
+  float nrm = 0.f;
+  for (int k0 = 0; k0 < D; k0 += kMbK) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int k = lhalf * 16 + e;
+      const float v = qrow ? to_f32<T>(qrow[k0 + k]) : 0.f;
+      nrm = fmaf(v, v, nrm);
+      qs[k][lr] = v;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ds[lq * 8 + e][lb] = dcrow ? dcrow[k0 + lq * 8 + e] / kNorm : 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kMbK; ++k) {
+      float a[8], bv[4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = qs[k][ty * 8 + i];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) bv[c] = ds[k][tx * 4 + c];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[i][c] = fmaf(a[i], bv[c], acc[i][c]);
+    }
+    __syncthreads();
+  }
+  nrm += __shfl_xor_sync(0xffffffffu, nrm, 1);
+  if (lhalf == 0) s_nrm[lr] = nrm;
+  __syncthreads();
+  const float sqrt_d = sqrtf((float)D);
+  float bm[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int j = j0 + tx * 4 + c;
+    const float rs = j < nb ? sqrtf(e_ac[((size_t)b * nb + j) * H + h]) : 0.f;
+    bm[c] = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = r0 + ty * 8 + i;
+      if (r < rows && j < nb) {
+        const float bound = acc[i][c] / sqrt_d + (sqrtf(s_nrm[ty * 8 + i]) * rs) / sqrt_d;
+        if (bounds) {
+          const int s = r / G, g = r - s * G;
+          bounds[(((size_t)b * Sq + s) * nb + j) * Hq + (size_t)h * G + g] = bound;
+        }
+        bm[c] = fmaxf(bm[c], bound);
+      }
+    }
+    s_max[ty][tx * 4 + c] = bm[c];
+  }
+  __syncthreads();
+  if (tid < kMbBlk && j0 + tid < nb) {
+    float m = s_max[0][tid];
+#pragma unroll
+    for (int y = 1; y < 16; ++y) m = fmaxf(m, s_max[y][tid]);
+    atomicMax(&key[((size_t)b * nb + j0 + tid) * H + h], f2key(m));
+  }
+}
+
+__global__ void meta_bound_gates_kernel(float* bound_max, const float* __restrict__ zeta, int64_t cells, float tau,
+                                        float zeta_max, uint8_t* keep) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= cells) return;
+  const float bm = key2f(reinterpret_cast<int*>(bound_max)[i]);
+  bound_max[i] = bm;
+  if (keep) keep[i] = (bm >= tau && zeta[i] <= zeta_max) ? 1 : 0;
+}
+
+template <typename T>
+int launch_meta_bound_gemm(const float* dc, const float* e_ac, const float* zeta, const T* q, int B, int nb, int H,
+                           int D, int Sq, int Hq, float tau, float zeta_max, float* bound_max, float* bounds,
+                           uint8_t* keep, cudaStream_t st) {
+  const int64_t cells = (int64_t)B * nb * H;
+  const int G = Hq / H;
+  const int64_t rows = (int64_t)Sq * G;
+  const int64_t gx = (rows + kMbRows - 1) / kMbRows;
+  OC_REQUIRE(gx < (1ll << 31) && (int64_t)B * H < 65536 && (nb + kMbBlk - 1) / kMbBlk < 65536, OC_ERR_CAPACITY,
+             "oc_score_from_metadata: grid too large");
+  const unsigned g1 = (unsigned)((cells + 255) / 256);
+  int* key = reinterpret_cast<int*>(bound_max);
+  meta_bound_init_kernel<<<g1, 256, 0, st>>>(key, cells);
+  dim3 grid((unsigned)gx, (unsigned)(B * H), (unsigned)((nb + kMbBlk - 1) / kMbBlk));
+  meta_bound_gemm_kernel<T><<<grid, 256, 0, st>>>(dc, e_ac, q, nb, H, D, Sq, Hq, G, key, bounds);
+  meta_bound_gates_kernel<<<g1, 256, 0, st>>>(bound_max, zeta, cells, tau, zeta_max, keep);
+  return check_launch("meta_bound_gemm_kernel");
+}
+
+}  // namespace
+}  // namespace oc
+
 extern "C" int oc_score_from_metadata(const float* dc, const float* e_ac, const float* zeta, const void* q,
                                       int q_dtype, int batch, int num_blocks, int kv_heads, int head_dim,
                                       int q_len, int q_heads, float tau, float zeta_max, float* bound_max,
@@ -1524,6 +1695,17 @@ extern "C" int oc_score_from_metadata(const float* dc, const float* e_ac, const 
   OC_REQUIRE(grid < (1ll << 31), OC_ERR_CAPACITY, "oc_score_from_metadata: too many blocks");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int G = q_heads / kv_heads;
+  // Long query chunks: the tiled bound GEMM (bound_max doubles as its
+  // atomic-max scratch, so it must be given).
+  if ((int64_t)q_len * G > kMetaGemmMinRows && bound_max && head_dim % kMbK == 0) {
+    if (q_dtype == OC_F32)
+      return launch_meta_bound_gemm<float>(dc, e_ac, zeta, (const float*)q, batch, num_blocks, kv_heads, head_dim,
+                                           q_len, q_heads, tau, zeta_max, bound_max, bounds, keep, st);
+    if (q_dtype == OC_BF16)
+      return launch_meta_bound_gemm<__nv_bfloat16>(dc, e_ac, zeta, (const __nv_bfloat16*)q, batch, num_blocks,
+                                                   kv_heads, head_dim, q_len, q_heads, tau, zeta_max, bound_max,
+                                                   bounds, keep, st);
+  }
   if (q_dtype == OC_F32)
     meta_gates_kernel<float><<<(unsigned)grid, 256, 0, st>>>(dc, e_ac, zeta, (const float*)q, num_blocks, kv_heads,
                                                              head_dim, q_len, q_heads, G, cells, tau, zeta_max,
@@ -1538,6 +1720,7 @@ extern "C" int oc_score_from_metadata(const float* dc, const float* e_ac, const 
 }
 
 namespace oc {
+int wait_limit_score(unsigned long long ns) { return set_wait_limit_here(ns); }
 int score_status(int* status, int reset) {
   cudaError_t e = cudaMemcpyFromSymbol(status, g_score_status, sizeof(int));
   if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
@@ -1604,13 +1787,40 @@ int decode_fused(const void* q, const void* k, const void* v, int batch, int q_l
   f.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
 
   CUtensorMap km, ak, av;
-  int rc = encode_score_map(&km, k, kv_heads, 128, (int64_t)batch * nb);
   const uint64_t cols = (uint64_t)kv_heads * 128, rows = (uint64_t)batch * seq_len;
-  if (!rc) rc = encode_map_2d(&ak, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true);
-  if (!rc) rc = encode_map_2d(&av, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true);
+  int rc = 0;
+  const uint64_t kk[4] = {1, (uint64_t)k, (uint64_t)kv_heads | (128ull << 32), rows};
+  const uint64_t ka[4] = {2, (uint64_t)k, cols, rows};
+  const uint64_t kv[4] = {2, (uint64_t)v, cols, rows};
+  if (!map_cache_get(kk, &km) && !(rc = encode_score_map(&km, k, kv_heads, 128, (int64_t)batch * nb)))
+    map_cache_put(kk, km);
+  if (!rc && !map_cache_get(ka, &ak) &&
+      !(rc = encode_map_2d(&ak, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true)))
+    map_cache_put(ka, ak);
+  if (!rc && !map_cache_get(kv, &av) &&
+      !(rc = encode_map_2d(&av, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true)))
+    map_cache_put(kv, av);
   if (rc) return set_error(OC_ERR_CUDA, "oc_decode_step: tensor map encode failed (%d)", rc);
   const int smem = kStages * kSlabB + kQCacheBytes + 1024;
-  cudaFuncSetAttribute(score_tma_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // Once per device: the shared-memory opt-in, and the check that a CTA of
+  // this size fits on every SM (the persistent grid relies on all its CTAs
+  // being resident at once; with less room the separate kernels run instead).
+  static std::atomic<uint64_t> s_setup{0}, s_fits{0};
+  if (first_on_device(s_setup)) {
+    cudaFuncSetAttribute(score_tma_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int per_sm = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_tma_kernel<128, true>, kFusedThreads, smem) ==
+            cudaSuccess &&
+        per_sm >= 1 && dev < kMaxCachedDevices)
+      s_fits.fetch_or(1ull << dev);
+  }
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= kMaxCachedDevices || !(s_fits.load() & (1ull << dev))) return OC_ERR_UNSUPPORTED;
+  }
   const cudaError_t e = launch_pdl(score_tma_kernel<128, true>, dim3(grid), dim3(kFusedThreads), smem, st, km, ak,
                                    av, a, (int)ntiles, f);
   if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "score_tma_kernel (fused): %s", cudaGetErrorString(e));

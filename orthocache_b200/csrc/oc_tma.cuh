@@ -2,7 +2,7 @@
 // host-side tensor-map encoder (driver entry point fetched through the
 // runtime, so the library needs no link against libcuda).
 //
-// Every wait is bounded: after kWaitLimitNs of %globaltimer time a wait gives
+// Every wait is bounded: after g_wait_limit_ns of %globaltimer time a wait gives
 // up and reports failure, and the kernel records an error status instead of
 // spinning forever.
 #pragma once
@@ -14,7 +14,14 @@
 
 namespace oc {
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, the default
+
+// The limit in force, one copy per translation unit (set from the host by
+// oc_set_wait_limit_ns through set_wait_limit_here of every unit).
+static __device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+static inline int set_wait_limit_here(unsigned long long ns) {
+  return (int)cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -60,12 +67,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Wait for the phase with the given parity; false if kWaitLimitNs passed.
+// Wait for the phase with the given parity; false once the wait limit
+// (g_wait_limit_ns, 2 s by default) has passed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = g_wait_limit_ns;
   while (!mbar_try_wait(bar, parity))
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit) return false;
   return true;
 }
 
@@ -104,6 +113,11 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // each 1024-byte group of 8 rows (needs box_cols * elem_bytes == 128).
 int encode_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t cols,
                   uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128 = false);
+
+// Host: a process-wide cache of encoded tensor maps keyed by four words
+// (kind, base address, shape digest); see oc_common.cu.
+bool map_cache_get(const uint64_t key[4], CUtensorMap* out);
+void map_cache_put(const uint64_t key[4], const CUtensorMap& map);
 
 // Host: encode a 3-D tensor map (dims[0] innermost, byte strides of dims 1
 // and 2).  Returns 0 or a CUresult.

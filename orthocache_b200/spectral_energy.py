@@ -40,6 +40,9 @@ def _as_batched(x, name):
     raise ValueError(f"{name} must be (S, H, D) or (B, S, H, D), got {tuple(x.shape)}")
 
 
+LONG_CHUNK_ROWS = 32  # query rows per KV head above which the bounds run as a GEMM
+
+
 def score_blocks(keys, q=None, tau=-math.inf, zeta_max=math.inf, block_size=BLOCK,
                  band_low=BAND_LOW, band_mid=BAND_MID, band_high=BAND_HIGH,
                  want=("keep",), mode=0):
@@ -83,14 +86,29 @@ def score_blocks(keys, q=None, tau=-math.inf, zeta_max=math.inf, block_size=BLOC
         if keep is not None:
             out["keep"] = keep.bool()
         return out if batched else {n: t[0] for n, t in out.items()}
-    _lib.call("oc_score_blocks", _lib.ptr(k), _lib.ptr(qq), _lib.dtype_code(k),
-              B, S, H, D, Sq, Hq,
-              int(band_low[0]), int(band_low[1]), int(band_mid[0]), int(band_mid[1]),
-              int(band_high[0]), int(band_high[1]),
-              float(tau), float(zeta_max),
-              _lib.ptr(out.get("dc")), _lib.ptr(out.get("e_low")), _lib.ptr(out.get("e_mid")),
-              _lib.ptr(out.get("e_high")), _lib.ptr(out.get("zeta")), _lib.ptr(out.get("bound_max")),
-              _lib.ptr(out.get("bounds")), _lib.ptr(keep), int(mode), _lib.stream_ptr(dev))
+    if (qq is not None and Sq * (Hq // H) > LONG_CHUNK_ROWS and int(mode) == 0
+            and (tuple(band_low), tuple(band_mid), tuple(band_high)) == (BAND_LOW, BAND_MID, BAND_HIGH)
+            and set(want) <= {"dc", "zeta", "bound_max", "bounds", "keep"}):
+        # Long query chunks: the query-independent block metadata in one pass
+        # over the keys, then the bounds of all rows as a tiled GEMM.
+        dc = out.get("dc", torch.empty((B, nb, H, D), **f32))
+        zeta = out.get("zeta", torch.empty((B, nb, H), **f32))
+        bmax = out.get("bound_max", torch.empty((B, nb, H), **f32))
+        e_ac = torch.empty((B, nb, H), **f32)
+        _lib.call("oc_block_metadata", _lib.ptr(k), _lib.dtype_code(k), B, S, H, D, _lib.ptr(dc), _lib.ptr(e_ac),
+                  _lib.ptr(zeta), _lib.stream_ptr(dev))
+        _lib.call("oc_score_from_metadata", _lib.ptr(dc), _lib.ptr(e_ac), _lib.ptr(zeta), _lib.ptr(qq),
+                  _lib.dtype_code(qq), B, nb, H, D, Sq, Hq, float(tau), float(zeta_max), _lib.ptr(bmax),
+                  _lib.ptr(out.get("bounds")), _lib.ptr(keep), _lib.stream_ptr(dev))
+    else:
+        _lib.call("oc_score_blocks", _lib.ptr(k), _lib.ptr(qq), _lib.dtype_code(k),
+                  B, S, H, D, Sq, Hq,
+                  int(band_low[0]), int(band_low[1]), int(band_mid[0]), int(band_mid[1]),
+                  int(band_high[0]), int(band_high[1]),
+                  float(tau), float(zeta_max),
+                  _lib.ptr(out.get("dc")), _lib.ptr(out.get("e_low")), _lib.ptr(out.get("e_mid")),
+                  _lib.ptr(out.get("e_high")), _lib.ptr(out.get("zeta")), _lib.ptr(out.get("bound_max")),
+                  _lib.ptr(out.get("bounds")), _lib.ptr(keep), int(mode), _lib.stream_ptr(dev))
     if keep is not None:
         out["keep"] = keep.bool()
     if not batched:

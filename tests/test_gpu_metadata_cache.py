@@ -18,6 +18,10 @@ pytestmark = pytest.mark.gpu
     (24, 16, 4, 128, 1, torch.bfloat16),
     (128, 32, 8, 128, 1, torch.bfloat16),   # config 1 size
     (10, 8, 2, 64, 3, torch.float32),
+    # long query chunks: the bounds run as the tiled GEMM (rows per KV head > 32)
+    (16, 8, 2, 128, 100, torch.bfloat16),
+    (12, 8, 4, 64, 40, torch.float32),
+    (70, 32, 8, 128, 256, torch.bfloat16),   # two block tiles of 64, 1024 rows per KV head
 ])
 def test_metadata_cache_vs_oracle(nb, hq, hkv, d, sq, dtype):
     import orthocache_b200 as oc
