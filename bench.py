@@ -45,9 +45,11 @@ ZETA_MAX = 5.0
 LAYERS = 4
 FALLBACK_HBM = 6650.0
 # DRAM bytes read + written by one launch of the fused decode-layer kernel at
-# this workload (75 % eviction), from the ncu capture summarised in
-# profiles/decode_fused_config1.md.
+# this workload (75 % eviction): not measured by this script but taken from the
+# ncu capture summarised in profiles/decode_fused_config1.md (reported with
+# that source in the JSON line; null at other evictions).
 FUSED_TRAFFIC = 194310144
+FUSED_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/decode_fused_config1.md"
 
 
 def parse():
@@ -58,8 +60,10 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--evict", type=float, default=0.75)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--config", type=int, choices=[1, 2], default=1,
-                   help="1: decode layer (the headline metric); 2: chunked prefill on the tensor cores")
+    p.add_argument("--no-parity", action="store_true", help="N > 1: skip the oracle check of the merged output")
+    p.add_argument("--config", type=int, choices=[1, 2, 4], default=1,
+                   help="1: decode layer (the headline metric); 2: chunked prefill on the tensor cores; "
+                        "4: the 60-layer decode stack (sliding-window + global layers, D 256)")
     return p.parse_args()
 
 
@@ -149,7 +153,8 @@ def make_layers(rank, evict, device, world=1):
         L.kinds = syn.block_kinds(nb, L.evict, seed=seed)
         L.k = syn.make_keys(nb, HKV, D, L.kinds, seed=seed, device=device)
         L.v = syn.make_values(S_SHARD, HKV, D, seed=seed, device=device)
-        L.q = syn.make_queries(1, HQ, D, seed=seed, device=device)
+        # the query is the same on every rank (it attends across all shards)
+        L.q = syn.make_queries(1, HQ, D, seed=l, device=device)
         sc = score_blocks(L.k, L.q, want=("zeta", "bound_max"))
         L.tau, L.kept = syn.calibrate_tau(sc["zeta"], sc["bound_max"], ZETA_MAX, L.evict)
         layers.append(L)
@@ -174,18 +179,24 @@ class Engine:
         # counters must start at zero) covers the partial attention's too
         self.ws_bytes = _lib.query("oc_decode_step_workspace_bytes", 1, 1, HQ, HKV, D, S_SHARD)
         self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=device)
-        # sequence-parallel: this shard's (m, l, o) partial packed in one
-        # buffer [m (rows) | l (rows) | o (rows, D)], all-gathered in one call
-        rows = HQ
-        self.rows = rows
-        self.send = torch.empty((rows * (D + 2),), dtype=torch.float32, device=device)
-        self.m, self.l = self.send[:rows], self.send[rows:2 * rows]
-        self.o = self.send[2 * rows:].view(rows, D)
-        self.recv = torch.empty((world * rows * (D + 2),), dtype=torch.float32, device=device)
         # our kernels per layer: one (the fused decode layer: score, block
-        # decisions, attention, merge); sequence-parallel: the fused layer
-        # writing the shard's partial, then the cross-shard merge
-        self.launches_per_step = 1 if world == 1 else 2
+        # decisions, attention, merge)
+        self.launches_per_step = 1
+        self.dec = None
+        if world > 1:
+            # sequence-parallel: oc_decode_step_sharded over an NCCL
+            # communicator; with the exchange regions mapped across the ranks
+            # (oc_sharded_connect) each layer is still one kernel, whose group
+            # merges exchange the shards' (m, l, o) partials by NVLink peer
+            # stores; otherwise the fused kernel, an NCCL all-gather and a
+            # merge kernel
+            from orthocache_b200.comm import NcclComm
+            from orthocache_b200.distributed import ShardedDecoder
+            self.comm = NcclComm(device=device)
+            self.dec = ShardedDecoder(self.comm, HQ, HKV, D, S_SHARD, peer=True)
+            self.keep, self.perm, self.count, self.out = self.dec.keep[0], self.dec.perm[0], self.dec.count, \
+                self.dec.out
+            self.launches_per_step = 1 if self.dec.peer else 2
 
     @property
     def stream(self):
@@ -207,17 +218,8 @@ class Engine:
                 _l.ptr(self.ws), self.ws_bytes, self.stream)
 
     def decode_sharded(self, L, q=None):
-        """One layer of sequence-parallel decode: the fused kernel writes this
-        shard's partial, one all-gather over NCCL, one merge."""
-        import torch.distributed as dist
-        _l = self.lib
-        q = L.q if q is None else q
-        _l.call("oc_decode_step_partial", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, 1, 1, HQ, HKV, D, S_SHARD,
-                L.tau, ZETA_MAX, _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(self.m),
-                _l.ptr(self.l), _l.ptr(self.o), _l.ptr(self.ws), self.ws_bytes, self.stream)
-        dist.all_gather_into_tensor(self.recv, self.send)
-        _l.call("oc_merge_partials_packed", _l.ptr(self.recv), self.world, self.rows, D, _l.ptr(self.out), 1,
-                self.stream)
+        """One layer of sequence-parallel decode through oc_decode_step_sharded."""
+        self.dec(L.q if q is None else q, L.k, L.v, L.tau, ZETA_MAX)
 
     def step(self, L, q=None):
         if self.world == 1:
@@ -229,6 +231,17 @@ class Engine:
 # ---------------------------------------------------------------------------
 # CPU port of the reference path (baseline leg and --impl reference)
 # ---------------------------------------------------------------------------
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_port_time(L, min_seconds=10.0, max_reps=20):
     """Time the reference's decode layer on the host cores (oracle/oc_port.c,
     OpenMP on all cores) on a full layer; returns (median µs, threads, reps)."""
@@ -247,42 +260,81 @@ def cpu_port_time(L, min_seconds=10.0, max_reps=20):
     return statistics.median(ts) * 1e6, port.threads(), len(ts)
 
 
+def workload_config(world, evict):
+    """The config dict of the JSON line, shared by both arms."""
+    return {"workload": ("config1: GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens, evict=%.2f, "
+                         "zeta_max=5" % (S_SHARD, evict)) if world == 1 else
+                        ("config3: sequence-parallel GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens per "
+                         "GPU (%d total), per-shard eviction U[0.6, 0.9], zeta_max=5" % (S_SHARD, S_SHARD * world)),
+            "layers": LAYERS, "seeds": "layer l of shard r: keys/values seed 1000 r + l, query seed l",
+            "l2": "inputs > L2: 4 layers of KV (1.07 GB per GPU) rotate per step",
+            "parallelism": "single GPU" if world == 1 else
+                           f"sequence-parallel x{world}, LSE merge of per-shard partials"}
+
+
+def make_host_layers(rank, evict, world):
+    """The layers of shard `rank` (same seeds as make_layers) on the host, with
+    τ calibrated on the scores of the CPU port."""
+    import random
+    import numpy as np
+    import torch
+    from orthocache_b200 import synthetic as syn
+    from oracle import port
+    nb = S_SHARD // 512
+    out = []
+    for l in range(LAYERS):
+        seed = 1000 * rank + l
+        L = Layer()
+        L.evict = evict if world == 1 else random.Random(seed).uniform(0.6, 0.9)
+        kinds = syn.block_kinds(nb, L.evict, seed=seed)
+        L.k = syn.make_keys(nb, HKV, D, kinds, seed=seed, device="cpu")
+        L.v = syn.make_values(S_SHARD, HKV, D, seed=seed, device="cpu")
+        L.q = syn.make_queries(1, HQ, D, seed=l, device="cpu")
+        bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
+        bmax, zeta = port.scores(bits(L.k), bits(L.q))
+        L.tau, L.kept = syn.calibrate_tau(torch.tensor(zeta), torch.tensor(bmax), ZETA_MAX, L.evict)
+        out.append(L)
+    return out
+
+
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU path (the C port, all host threads), rank 0 only."""
+    """--impl reference: the reference's CPU path for the same workload (the C
+    port of its algorithm, all host threads), rank 0 only: each step runs one
+    layer of every shard (all `world` shards of configuration 3 at N > 1), the
+    layers rotating like ours."""
     if rank != 0:
         return
     import torch
-    from orthocache_b200 import synthetic as syn
-    from oracle import oc_oracle as O, port
     import numpy as np
-    nb = S_SHARD // 512
+    from oracle import port
     torch.manual_seed(0)
-    kinds = syn.block_kinds(nb, args.evict, seed=0)
-    L = Layer()
-    L.k = syn.make_keys(nb, HKV, D, kinds, seed=0, device="cpu")
-    L.v = syn.make_values(S_SHARD, HKV, D, seed=0, device="cpu")
-    L.q = syn.make_queries(1, HQ, D, seed=0, device="cpu")
-    sc = O.score_blocks(L.q.float().numpy(), L.k.float().numpy(), -1e30, ZETA_MAX)
-    L.tau, _ = syn.calibrate_tau(torch.tensor(sc["zeta"]), torch.tensor(sc["bound_max"]), ZETA_MAX, args.evict)
+    shards = [make_host_layers(r, args.evict, world) for r in range(world)]
     bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)
-    kb, vb, qb = bits(L.k), bits(L.v), bits(L.q)
-    steps = max(1, min(args.steps, 200))
-    for _ in range(max(1, min(args.warmup, 5))):
-        port.decode(kb, vb, qb, L.tau, ZETA_MAX)
+    data = [[(bits(L.k), bits(L.v), bits(L.q), L.tau) for L in layers] for layers in shards]
+    steps = max(1, min(args.steps, max(4, 200 // world)))
+
+    def step(i):
+        for sh in data:
+            kb, vb, qb, tau = sh[i % LAYERS]
+            port.decode(kb, vb, qb, tau, ZETA_MAX)
+
+    for i in range(max(1, min(args.warmup, 5))):
+        step(i)
     t0 = time.perf_counter()
-    for _ in range(steps):
-        port.decode(kb, vb, qb, L.tau, ZETA_MAX)
+    for i in range(steps):
+        step(i)
     us = (time.perf_counter() - t0) / steps * 1e6
     cores = port.threads()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(us, 2), "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config1: GQA decode B=1, Hq=32/Hkv=8, D=128, S=65536, evict=%.2f" % args.evict,
-                   "layers": 1, "l2": "host run"},
-        "cpu_baseline": {"value": round(us, 2), "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": "full layer (65536 tokens) per step; reference JAX CPU path unavailable "
-                                   "(jax not installed), C/OpenMP port of its algorithm timed instead"},
+        "config": workload_config(world, args.evict),
+        "cpu_baseline": {"value": round(us, 2), "unit": UNIT, "cores": cores, "kind": "port", "cpu": cpu_model(),
+                         "sample": "each step one full layer (65536 tokens) of each of the %d shards, the %d layers "
+                                   "rotating; the reference's JAX CPU path is unavailable (jax not installed), "
+                                   "the C/OpenMP port of its algorithm (oracle/oc_port.c) is timed instead"
+                                   % (world, LAYERS)},
         "e2e": {"value": round(us, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -316,6 +368,37 @@ def warmup_steps(step, min_steps, min_seconds, world, sync, device):
                 return i
 
 
+def sharded_parity(eng, L, rank, world, device):
+    """N > 1: the merged output of one sharded layer against the oracle.
+    Every rank computes, on its host, the reference's two-gate mask of its
+    shard, the compaction and the shard's unnormalised attention state
+    (m, l, o); rank 0 merges the states of all shards (log-sum-exp) and
+    compares with the output the GPUs produced."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from oracle import oc_oracle as O
+    eng.step(L)
+    torch.cuda.synchronize()
+    from oracle import port
+    qf, kf, vf = (t.float().cpu().numpy() for t in (L.q, L.k, L.v))
+    bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+    bmax, zeta = port.scores(bits(L.k), bits(L.q))  # the two gates' scores (C port of the reference)
+    perm, n = O.stream_compact_mask((bmax >= np.float32(L.tau)) & (zeta <= np.float32(ZETA_MAX)))
+    mask_ok = int(eng.count[0]) == n and np.array_equal(eng.perm.cpu().numpy(), perm)
+    part = O.partial_attention(qf, kf, vf, perm, n)
+    parts = [None] * world
+    dist.all_gather_object(parts, (part, mask_ok))
+    if rank != 0:
+        return None
+    want = O.merge_partials([p for p, _ in parts])
+    got = eng.out.float().cpu().numpy()[0]
+    ok = bool(np.allclose(got, want, rtol=1e-2, atol=2e-2))
+    return {"checked": "layer 0 merged over %d shards vs oracle mask + partial states + LSE merge" % world,
+            "max_abs_err": float(np.abs(got - want).max()), "masks_bit_exact": all(m for _, m in parts),
+            "ok": ok and all(m for _, m in parts), "tolerance": "1e-2 rel / 2e-2 abs"}
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -342,7 +425,7 @@ def run_ours(args, rank, world, local_rank):
     # and each kernel may start while the one before it drains (programmatic
     # dependent launch).  Multi-GPU steps run eagerly (NCCL in the step).
     graphs = None
-    if world == 1:
+    if world == 1 or eng.dec.peer:
         cap = torch.cuda.Stream()
         cap.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(cap):
@@ -361,49 +444,72 @@ def run_ours(args, rank, world, local_rank):
                 eng.step(L)
             g_one.append(g)
         graphs = (g_all, g_one)
+        barrier()
         for s in range(2):
             g_all.replay()
         torch.cuda.synchronize()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The timed region: exactly K layers between one pair of CUDA events,
+    # repeated in R windows (each with its own events, a barrier and a
+    # synchronize on both sides); the value is the median window, the spread
+    # is reported beside it.
+    R = 7
+    win_ms = []
     with Clocks(local_rank) as clk:
-        barrier()
-        torch.cuda.synchronize()
-        start.record()
-        if graphs is not None:
-            for s in range(K // LAYERS):
-                graphs[0].replay()
-            for s in range(K % LAYERS):
-                graphs[1][s].replay()
-        else:
-            for s in range(K):
-                eng.step(layers[s % LAYERS])
-        stop.record()
-        torch.cuda.synchronize()
-        barrier()
-    ms = start.elapsed_time(stop) / K
-    # Launch durations: CUDA events bracketing each launch on the launching
-    # stream, eager, inputs rotating past L2.  The scorer alone (oc_score_blocks)
-    # and the whole layer (oc_decode_step: at N = 1 a single launch of the
-    # fused kernel, the roofline kernel).
-    # each launch on the launching stream, eager, inputs rotating past L2.
+        for _ in range(R):
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            torch.cuda.synchronize()
+            start.record()
+            if graphs is not None:
+                for s in range(K // LAYERS):
+                    graphs[0].replay()
+                for s in range(K % LAYERS):
+                    graphs[1][s].replay()
+            else:
+                for s in range(K):
+                    eng.step(layers[s % LAYERS])
+            stop.record()
+            torch.cuda.synchronize()
+            barrier()
+            win_ms.append(start.elapsed_time(stop) / K)
+    if world > 1:
+        t = torch.tensor(win_ms, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)  # per window, the slowest rank
+        win_ms = t.tolist()
+    ms = statistics.median(win_ms)
+    # The scorer alone (oc_score_blocks, the stand-alone form of the fused
+    # layer's scoring phase): average launch duration in a CUDA-graph replay
+    # of LAYERS launches on rotating inputs (the same measurement as the
+    # layer's); and one eager launch of the whole layer bracketed by events.
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        for L in layers:
+            eng.score(L)
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+    g_score = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_score):
+        for L in layers:
+            eng.score(L)
+    g_score.replay()
+    reps = max(8, min(K, 400) // LAYERS)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g_score.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    t_score = e0.elapsed_time(e1) / (reps * LAYERS)
     Kb = max(LAYERS, min(K, 400))
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(Kb)]
-    for s in range(Kb):
-        evs[s][0].record()
-        eng.score(layers[s % LAYERS])
-        evs[s][1].record()
-    torch.cuda.synchronize()
-    t_score = statistics.median(e[0].elapsed_time(e[1]) for e in evs)
     for s in range(Kb):
         evs[s][0].record()
         eng.step(layers[s % LAYERS])
         evs[s][1].record()
     torch.cuda.synchronize()
     t_step_eager = statistics.median(e[0].elapsed_time(e[1]) for e in evs)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
 
     # ---- end to end through the public API, host buffers ----
     from orthocache_b200 import _lib  # noqa: F401
@@ -436,53 +542,66 @@ def run_ours(args, rank, world, local_rank):
     # correctness guard on the last step: retained count matches the calibration
     assert int(cnt_host[0]) == layers[(Ke - 1) % LAYERS].kept, "retained block count changed"
 
-    if rank != 0:
-        return
-    hbm, peak_kind = peaks()
     k_bytes = S_SHARD * HKV * D * 2
     kept = statistics.mean(L.kept for L in layers)
     alg_bytes = k_bytes + kept / nb * 2 * k_bytes + HQ * D * 2 * 2
+    parity = None
+    if world > 1:
+        # whole-job algorithmic bytes (every shard's own eviction)
+        t = torch.tensor([alg_bytes], dtype=torch.float64, device=device)
+        dist.all_reduce(t)
+        job_bytes = float(t.item())
+        if not args.no_parity:
+            parity = sharded_parity(eng, layers[0], rank, world, device)
+    if rank != 0:
+        return
+    hbm, peak_kind = peaks()
     score_gbs = k_bytes / (t_score * 1e-3) / 1e9
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         us_cpu, cores, reps = cpu_port_time(layers[0])
-        cpu = {"value": round(us_cpu, 2), "unit": UNIT, "cores": cores, "kind": "port",
+        cpu = {"value": round(us_cpu, 2), "unit": UNIT, "cores": cores, "kind": "port", "cpu": cpu_model(),
                "sample": f"one full layer of this workload (layer 0), median of {reps} runs; C/OpenMP port of "
                          "the reference's compute_multiband_mask + compaction + online-softmax loop"}
     line = {
         "metric": METRIC, "value": round(ms * 1e3, 3), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": ("config1: GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens, evict=%.2f, "
-                                "zeta_max=5" % (S_SHARD, args.evict)) if world == 1 else
-                               ("config3: sequence-parallel GQA decode B=1, Hq=32/Hkv=8, D=128, bf16, %d tokens per "
-                                "GPU (%d total), per-shard eviction U[0.6, 0.9], zeta_max=5" % (S_SHARD, S_SHARD * world)),
-                   "l2": "inputs > L2: 4 layers of KV (1.07 GB) rotate per step",
-                   "parallelism": "single GPU" if world == 1 else f"sequence-parallel x{world}, LSE merge"},
+        "config": workload_config(world, args.evict),
         "roofline": ({"bound": "hbm", "kernel": "score_tma_kernel<128,true> (fused decode layer)",
                       "achieved": round(alg_bytes / (ms * 1e-3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                       "frac": round(alg_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
                       "traffic": FUSED_TRAFFIC if abs(args.evict - 0.75) < 1e-9 else None,
+                      "traffic_source": FUSED_TRAFFIC_SOURCE if abs(args.evict - 0.75) < 1e-9 else None,
                       "peak_kind": peak_kind, "bytes_per_launch": int(alg_bytes),
                       "eager_launch_us": round(t_step_eager * 1e3, 2),
                       "eager_frac": round(alg_bytes / (t_step_eager * 1e-3) / 1e9 / hbm, 4),
                       "how": "algorithmic bytes |K| + kept/nb (|K|+|V|) per launch over the average launch "
-                             "duration in the timed region (CUDA events around K graph-replayed launches, one "
-                             "kernel per layer); eager_*: one launch alone, bracketed by CUDA events; traffic = "
-                             "dram bytes read+written per launch from the ncu capture in profiles/"}
+                             "duration in the timed region (median of the windows of K graph-replayed launches, "
+                             "one kernel per layer); eager_*: one launch alone, bracketed by CUDA events; traffic "
+                             "= dram bytes read+written per launch from the ncu capture in profiles/"}
                      if world == 1 else
-                     {"bound": "hbm", "kernel": "score_tma_kernel<128,false> (scorer)",
-                      "achieved": round(score_gbs, 1), "peak": hbm, "unit": "GB/s",
-                      "frac": round(score_gbs / hbm, 4), "traffic": None, "peak_kind": peak_kind,
-                      "bytes_per_launch": k_bytes}),
+                     {"bound": "hbm", "kernel": "score_tma_kernel<128,true> (fused decode layer, %s)" % (
+                         "partials exchanged by NVLink peer stores inside the kernel" if eng.dec.peer else
+                         "partials all-gathered by NCCL, then merged"),
+                      "achieved": round(job_bytes / (ms * 1e-3) / 1e9, 1), "peak": hbm * world, "unit": "GB/s",
+                      "frac": round(job_bytes / (ms * 1e-3) / 1e9 / (hbm * world), 4), "traffic": None,
+                      "peak_kind": peak_kind + " x %d GPUs" % world, "bytes_per_launch": int(job_bytes),
+                      "how": "whole-job algorithmic bytes (each shard: |K| + kept/nb (|K|+|V|)) over the max-over-"
+                             "ranks average layer time, against the sum of the GPUs' measured copy peaks"}),
         "scorer_roofline": {"kernel": "score_tma_kernel<128,false> (oc_score_blocks alone)",
                             "achieved": round(score_gbs, 1), "frac": round(score_gbs / hbm, 4),
                             "bytes_per_launch": k_bytes},
         "step_roofline": {"alg_bytes": int(alg_bytes), "achieved_gbs": round(alg_bytes / (ms * 1e-3) / 1e9, 1),
                           "frac": round(alg_bytes / (ms * 1e-3) / 1e9 / hbm, 4)},
         "kernel_us": {"score": round(t_score * 1e3, 2), "step_eager": round(t_step_eager * 1e3, 2),
-                      "how": "median of eager launches bracketed by CUDA events"},
-        "timed_region": ("CUDA-graph replay of %d consecutive layers" % LAYERS) if world == 1 else "eager launches",
+                      "how": "score: average launch in a CUDA-graph replay of %d scorer launches on rotating "
+                             "inputs; step_eager: median of eager launches bracketed by CUDA events" % LAYERS},
+        "windows": {"count": R, "steps_each": K, "median_ms_per_step": round(ms, 5),
+                    "min_ms_per_step": round(min(win_ms), 5), "max_ms_per_step": round(max(win_ms), 5)},
+        "timed_region": ("CUDA-graph replay of %d consecutive layers" % LAYERS) if graphs is not None else
+                        "eager launches",
+        "parity": parity,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": UNIT, "h2d_bytes_per_step": HQ * D * 2,
                 "d2h_bytes_per_step": HQ * D * 2 + 4,
@@ -670,6 +789,143 @@ def run_prefill(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# configuration 4: the 60-layer decode stack
+# ---------------------------------------------------------------------------
+C4_LAYERS, C4_GLOBAL_EVERY = 60, 6      # layers 5, 11, ..., 59 are global (10 of 60)
+C4_B, C4_HQ, C4_HKV, C4_D = 8, 32, 16, 256
+C4_SHARD = 16384                        # tokens per GPU: 131072 over 8 GPUs
+C4_WINDOW = 1024
+
+
+def run_stack(args, rank, world, local_rank):
+    """Configuration 4: one decode step (one token for each of 8 sequences)
+    through 60 attention layers, 50 sliding-window (window 1024, no
+    eviction) interleaved with 10 global layers (OrthoCache eviction at 75 %),
+    32/16 heads, head_dim 256, bf16, random-init.  The KV cache is sharded
+    by sequence, 16384 tokens per GPU (131072 at 8 GPUs; weak scaling), 60
+    distinct layers resident in HBM (129 GB per GPU).  Global layers' keys
+    follow the configuration-2 band mixture with the proportions re-drawn
+    per layer from the seed; sliding layers' keys are N(0, 1)."""
+    import random
+    import torch
+    import torch.distributed as dist
+    from orthocache_b200 import synthetic as syn, score_blocks
+    from orthocache_b200.stack import DecodeStack
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    nb = C4_SHARD // 512
+    kinds = ["global" if (l % C4_GLOBAL_EVERY) == C4_GLOBAL_EVERY - 1 else "sliding" for l in range(C4_LAYERS)]
+    qs, ks, vs, taus = [], [], [], []
+    for l, kind in enumerate(kinds):
+        seed = 100000 * rank + l
+        rng = random.Random(1000 + l)
+        fs, fm = rng.uniform(0.2, 0.4), rng.uniform(0.3, 0.5)
+        if kind == "global":
+            k = torch.stack([syn.make_keys(nb, C4_HKV, C4_D, syn.block_kinds(nb, fs, fm, seed=seed * 10 + b),
+                                           seed=seed * 10 + b, device=device) for b in range(C4_B)])
+        else:
+            g = torch.Generator(device=device).manual_seed(seed)
+            k = torch.randn((C4_B, C4_SHARD, C4_HKV, C4_D), generator=g, device=device).bfloat16()
+        g = torch.Generator(device=device).manual_seed(seed + 7)
+        v = torch.randn((C4_B, C4_SHARD, C4_HKV, C4_D), generator=g, device=device).bfloat16()
+        q = torch.stack([syn.make_queries(1, C4_HQ, C4_D, seed=l * 10 + b, device=device) for b in range(C4_B)])
+        tau = 0.0
+        if kind == "global":
+            sc = score_blocks(k, q, want=("zeta", "bound_max"))
+            tau, _ = syn.calibrate_tau(sc["zeta"].reshape(-1, C4_HKV), sc["bound_max"].reshape(-1, C4_HKV),
+                                       ZETA_MAX, 0.75)
+        qs.append(q); ks.append(k); vs.append(v); taus.append(tau)
+    torch.cuda.synchronize()
+    st = DecodeStack(kinds, C4_B, C4_HQ, C4_HKV, C4_D, C4_SHARD, window=C4_WINDOW, zeta_max=ZETA_MAX,
+                     group=None if world == 1 else dist.group.WORLD, device=device)
+    for _ in range(max(args.warmup, 3)):
+        st.step(qs, ks, vs, taus)
+    torch.cuda.synchronize()
+    K = max(2, min(args.steps, 20))
+    graph = None
+    if world == 1:
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
+            st.step(qs, ks, vs, taus)
+        torch.cuda.current_stream().wait_stream(cap)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            st.step(qs, ks, vs, taus)
+        graph.replay()
+        torch.cuda.synchronize()
+    run = (lambda: graph.replay()) if graph is not None else (lambda: st.step(qs, ks, vs, taus))
+    with Clocks(local_rank) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = e0.elapsed_time(e1) / K
+    # per layer kind: eager launches of one layer of each kind
+    per = {}
+    for kind in ("sliding", "global"):
+        li = kinds.index(kind)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(10):
+            st.layer(li, qs[li], ks[li], vs[li], taus[li])
+        b.record()
+        torch.cuda.synchronize()
+        per[kind] = a.elapsed_time(b) / 10
+    if world > 1:
+        t = torch.tensor([ms, per["sliding"], per["global"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, per["sliding"], per["global"] = t.tolist()
+    if rank != 0:
+        return
+    kv_layer = C4_B * C4_SHARD * C4_HKV * C4_D * 2
+    hbm, peak_kind = peaks()
+    # algorithmic bytes per step and GPU: sliding layers read the window's K
+    # and V on the last shard only; global layers read all keys and the
+    # retained quarter of K and V
+    win = C4_B * C4_WINDOW * C4_HKV * C4_D * 2 * 2
+    glob = kv_layer + 0.25 * 2 * kv_layer
+    n_glob = kinds.count("global")
+    step_bytes_last = (len(kinds) - n_glob) * win + n_glob * glob
+    line = {
+        "metric": "60-layer decode step ms (B=8, 131072-token context over 8 GPUs, 50 sliding + 10 global layers)",
+        "value": round(ms, 4), "unit": "ms/step", "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random-init)",
+        "config": {"workload": "config4: 60 layers (10 global at evict 0.75, 50 sliding window 1024), B=8, "
+                               "Hq=32/Hkv=16, D=256, bf16, %d tokens per GPU (%d total)" % (C4_SHARD,
+                                                                                           C4_SHARD * world),
+                   "l2": "inputs > L2: 60 distinct layers of KV (%.0f GB per GPU)" % (
+                       2 * len(kinds) * kv_layer / 1e9),
+                   "parallelism": "single GPU" if world == 1 else f"sequence-parallel x{world}, LSE merge"},
+        "tokens_per_s": round(C4_B / (ms * 1e-3), 1),
+        "layer_ms": {"sliding": round(per["sliding"], 4), "global": round(per["global"], 4),
+                     "how": "10 eager launches of one layer of each kind, CUDA events"},
+        "roofline": {"bound": "hbm", "achieved": round(step_bytes_last / (ms * 1e-3) / 1e9, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(step_bytes_last / (ms * 1e-3) / 1e9 / hbm, 4),
+                     "traffic": None, "peak_kind": peak_kind,
+                     "bytes_per_launch": int(step_bytes_last),
+                     "how": "algorithmic bytes of one step on the GPU holding the window (the slowest): 50 x "
+                            "window K+V + 10 x (|K| + 0.25 (|K|+|V|)), over the step time"},
+        "timed_region": "CUDA-graph replay of whole steps" if graph is not None else "eager steps",
+        "cpu_baseline": None,
+        "e2e": None,
+        "gpu_launches": K * (len(kinds) - n_glob + 3 * n_glob) * (1 if world == 1 else 2),
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -686,6 +942,8 @@ def main():
     try:
         if args.config == 2:
             run_prefill(args, rank, world, local_rank)
+        elif args.config == 4:
+            run_stack(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

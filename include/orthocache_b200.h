@@ -391,6 +391,43 @@ int oc_partial_attention(const void* q, const void* k, const void* v, int dtype,
                          void* workspace, size_t workspace_bytes, oc_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Paged KV cache.  The reference's index table (indirect_attention.py:155-159:
+ * the kernel reads keys and values only through block indices) doubles as a
+ * page table: keys / values live in a pool of num_pages blocks of block_size
+ * tokens, k_pool / v_pool (num_pages * block_size, kv_heads, head_dim), shared
+ * by the batch; logical block j of batch row b is pool page
+ * block_table[b * table_stride + j].  idx / count are the compaction of the
+ * LOGICAL mask (oc_stream_compact), exactly as for the contiguous entry
+ * points; a page outside [0, num_pages) is skipped.
+ *
+ * Attention (split-KV, any q_len; dtype / head_dim as oc_indirect_attention);
+ * workspace = oc_indirect_attention_paged_workspace_bytes(). */
+size_t oc_indirect_attention_paged_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                                   int block_size, int max_blocks);
+int oc_indirect_attention_paged(const void* q, const void* k_pool, const void* v_pool, int dtype,
+                                const int32_t* block_table, int table_stride, const int32_t* idx, int idx_stride,
+                                const int32_t* count, int count_stride, int batch, int q_len, int q_heads,
+                                int kv_heads, int head_dim, int num_pages, int block_size, int max_blocks, void* out,
+                                int out_dtype, void* workspace, size_t workspace_bytes, oc_stream_t stream);
+/* Chunked prefill on the tensor cores over a paged pool (conditions of
+ * oc_prefill_attention); workspace = oc_prefill_attention_paged_workspace_bytes(). */
+size_t oc_prefill_attention_paged_workspace_bytes(int batch, int max_blocks);
+int oc_prefill_attention_paged(const void* q, const void* k_pool, const void* v_pool, int dtype,
+                               const int32_t* block_table, int table_stride, const int32_t* idx, int idx_stride,
+                               const int32_t* count, int count_stride, int batch, int q_len, int q_heads,
+                               int kv_heads, int head_dim, int num_pages, int block_size, int max_blocks, void* out,
+                               int out_dtype, void* workspace, size_t workspace_bytes, oc_stream_t stream);
+/* The two gates from the write-time metadata of a paged pool: dc_pool
+ * (num_pages, kv_heads, head_dim), e_ac_pool / zeta_pool (num_pages,
+ * kv_heads) as oc_block_metadata writes them for the pool (batch 1, seq_len
+ * num_pages * 512); outputs per LOGICAL (batch, block, head) as
+ * oc_score_from_metadata. */
+int oc_score_from_metadata_paged(const float* dc_pool, const float* e_ac_pool, const float* zeta_pool, int num_pages,
+                                 const int32_t* block_table, int table_stride, const void* q, int q_dtype, int batch,
+                                 int num_blocks, int kv_heads, int head_dim, int q_len, int q_heads, float tau,
+                                 float zeta_max, float* bound_max, float* bounds, uint8_t* keep, oc_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Sequence-parallel exchange over NCCL (one rank per GPU).  `comm` is an
  * ncclComm_t created by the caller (any NCCL 2.x: the library resolves NCCL
  * at run time, preferring the copy already loaded in the process, else
@@ -456,9 +493,26 @@ int oc_alltoallv_heads(void* comm, const void* k, const void* v, int dtype, cons
  * log-sum-exp merge writes out on every rank — attention over the union of
  * all shards' retained blocks (distributed_attention.py:95-128 across
  * devices).  No KV block crosses NVLink.  Workspace: the size below,
- * zero-filled once (its leading region is oc_decode_step's). */
+ * zero-filled once (its leading region is oc_decode_step's).  Without
+ * oc_sharded_connect the exchange is an NCCL all-gather of the packed
+ * partials and a merge kernel; every rank must make the same calls. */
 size_t oc_decode_step_sharded_workspace_bytes(int nranks, int batch, int q_len, int q_heads, int kv_heads,
                                               int head_dim, int seq_len);
+/* Collective, once per workspace (after zero-filling it): map every rank's
+ * exchange region (inside its workspace) into every other rank by CUDA IPC
+ * (plain peer memory over NVLink; no multicast).  Afterwards
+ * oc_decode_step_sharded on this workspace runs as ONE kernel per layer: the
+ * fused layer's group merges store this shard's partial into every rank's
+ * region, publish it with a release flag carrying the call number, wait
+ * (bounded) for every rank's flag and merge the P partials — no NCCL kernel
+ * and no host synchronisation in the step, so the step can be captured in
+ * a CUDA graph.  All ranks agree on the outcome (a rank that cannot map the
+ * regions makes every rank return an error and keep the NCCL path).  Needs
+ * bf16, head_dim 128 and <= 8 query rows per KV head; the caller keeps the
+ * workspace alive until oc_sharded_disconnect. */
+int oc_sharded_connect(void* comm, void* workspace, size_t workspace_bytes, int batch, int q_len, int q_heads,
+                       int kv_heads, int head_dim, int seq_len, oc_stream_t stream);
+int oc_sharded_disconnect(void* workspace);
 int oc_decode_step_sharded(void* comm, const void* q, const void* k, const void* v, int dtype, int batch,
                            int q_len, int q_heads, int kv_heads, int head_dim, int seq_len, float tau,
                            float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count, void* out, int out_dtype,

@@ -325,6 +325,46 @@ def indirect_attention(q, keys, values, perm, num_active, block_size=BLOCK):
     return out.reshape(sq, hq, d).astype(np.float32)
 
 
+def partial_attention(q, keys, values, perm, num_active, block_size=BLOCK):
+    """Unnormalised attention state of one shard over blocks perm[:num_active]:
+    (m, l, o) per query row in float64 with m the max logit (natural units),
+    l = sum exp(s - m), o = sum exp(s - m) v — the running state of the
+    online softmax of ``_multihead_loop`` (``adaptive_attention.py:90-120``)
+    and of ``distributed_attention.py:95-128`` after the shard's last block.
+    No retained block: m = -inf, l = 0, o = 0.  Shapes (Sq, Hq), (Sq, Hq),
+    (Sq, Hq, D)."""
+    q = np.asarray(q, np.float64)
+    sq, hq, d = q.shape
+    k = np.asarray(keys, np.float64)
+    v = np.asarray(values, np.float64)
+    s, hkv, _ = k.shape
+    g = _group(hq, hkv)
+    if num_active == 0:
+        return np.full((sq, hq), -np.inf), np.zeros((sq, hq)), np.zeros((sq, hq, d))
+    blocks = np.asarray(perm[:num_active], np.int64)
+    tok = (blocks[:, None] * block_size + np.arange(block_size)[None, :]).reshape(-1)
+    ks = k[tok].reshape(-1, hkv, 1, d)
+    vs = v[tok].reshape(-1, hkv, 1, d)
+    qg = q.reshape(sq, hkv, g, d)
+    logits = np.einsum("qhgd,khxd->qkhg", qg, ks) / math.sqrt(d)
+    m = logits.max(axis=1)
+    w = np.exp(logits - m[:, None])
+    l = w.sum(axis=1)
+    o = np.einsum("qkhg,khxd->qhgd", w, vs)
+    return m.reshape(sq, hq), l.reshape(sq, hq), o.reshape(sq, hq, d)
+
+
+def merge_partials(parts):
+    """Log-sum-exp merge of shard states [(m, l, o), ...] into o / l (zeros
+    where no shard retained anything); float32 (Sq, Hq, D)."""
+    m = np.max(np.stack([p[0] for p in parts]), axis=0)
+    safe = np.where(np.isfinite(m), m, 0.0)
+    l = sum(p[1] * np.where(np.isfinite(p[0]), np.exp(p[0] - safe), 0.0) for p in parts)
+    o = sum(p[2] * np.where(np.isfinite(p[0]), np.exp(p[0] - safe), 0.0)[..., None] for p in parts)
+    out = np.where(l[..., None] > 0, o / np.where(l > 0, l, 1.0)[..., None], 0.0)
+    return out.astype(np.float32)
+
+
 def block_sparse_attention(q, keys, values, block_mask, block_size=BLOCK):
     """Predicated attention with a per-(block, head) mask (``sparse_attention.py:5-64``).
 

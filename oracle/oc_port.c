@@ -66,31 +66,14 @@ static void load_tile(float* t, const uint16_t* k, int j, int h, int H, int D) {
   }
 }
 
-int oc_port_threads(void) {
-#ifdef _OPENMP
-  return omp_get_max_threads();
-#else
-  return 1;
-#endif
-}
-
-/*
- * One decode step.  k, v: (S, Hkv, D) bf16; q: (Sq, Hq, D) bf16.
- * Outputs: keep (nb, Hkv) uint8; perm (nb) int32; *count; out (Sq, Hq, D) f32.
- * blocks_limit > 0 restricts scoring to the first blocks_limit blocks (a
- * bounded sample for timing); attention still covers the retained ones.
- * Scratch: compact_k / compact_v, each nb*512*Hkv*D uint16 (caller-owned).
- */
-int oc_port_decode(const uint16_t* k, const uint16_t* v, const uint16_t* q, int S, int Hkv, int Hq, int D,
-                   int Sq, float tau, float zeta_max, int blocks_limit, uint8_t* keep, int32_t* perm,
-                   int32_t* count, float* out, uint16_t* compact_k, uint16_t* compact_v) {
-  const int nb_all = S / BLK;
-  const int nb = blocks_limit > 0 && blocks_limit < nb_all ? blocks_limit : nb_all;
+/* The two gates' scores of the first nb blocks: bmax (nb, Hkv) = max over the
+ * Sq*G query rows of the query-aware bound (FWHT pass 1), zeta (nb, Hkv) =
+ * E_high / (E_low + 1e-6) (FWHT pass 2), as compute_multiband_mask computes
+ * them (spectral_energy.py:141-234). */
+static void port_scores(const uint16_t* k, const uint16_t* q, int nb, int Hkv, int Hq, int D, int Sq, float* bmax,
+                        float* zeta) {
   const int G = Hq / Hkv;
   const float sqrt_d = sqrtf((float)D);
-  float* bmax = (float*)malloc(sizeof(float) * nb * Hkv);
-  float* zeta = (float*)malloc(sizeof(float) * nb * Hkv);
-
   /* Gate 1: query-aware bounds (FWHT pass 1). */
 #pragma omp parallel
   {
@@ -138,6 +121,40 @@ int oc_port_decode(const uint16_t* k, const uint16_t* v, const uint16_t* q, int 
     }
     free(t);
   }
+}
+
+int oc_port_scores(const uint16_t* k, const uint16_t* q, int S, int Hkv, int Hq, int D, int Sq, float* bmax,
+                   float* zeta) {
+  port_scores(k, q, S / BLK, Hkv, Hq, D, Sq, bmax, zeta);
+  return 0;
+}
+
+int oc_port_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/*
+ * One decode step.  k, v: (S, Hkv, D) bf16; q: (Sq, Hq, D) bf16.
+ * Outputs: keep (nb, Hkv) uint8; perm (nb) int32; *count; out (Sq, Hq, D) f32.
+ * blocks_limit > 0 restricts scoring to the first blocks_limit blocks (a
+ * bounded sample for timing); attention still covers the retained ones.
+ * Scratch: compact_k / compact_v, each nb*512*Hkv*D uint16 (caller-owned).
+ */
+int oc_port_decode(const uint16_t* k, const uint16_t* v, const uint16_t* q, int S, int Hkv, int Hq, int D,
+                   int Sq, float tau, float zeta_max, int blocks_limit, uint8_t* keep, int32_t* perm,
+                   int32_t* count, float* out, uint16_t* compact_k, uint16_t* compact_v) {
+  const int nb_all = S / BLK;
+  const int nb = blocks_limit > 0 && blocks_limit < nb_all ? blocks_limit : nb_all;
+  const int G = Hq / Hkv;
+  const float sqrt_d = sqrtf((float)D);
+  float* bmax = (float*)malloc(sizeof(float) * nb * Hkv);
+  float* zeta = (float*)malloc(sizeof(float) * nb * Hkv);
+
+  port_scores(k, q, nb, Hkv, Hq, D, Sq, bmax, zeta);
   /* Two gates, union over heads, stable compaction. */
   int n = 0;
   for (int j = 0; j < nb_all; ++j) {

@@ -25,6 +25,18 @@ def threads():
     return lib().oc_port_threads()
 
 
+def scores(k_bits, q_bits):
+    """(bound_max, zeta) float32 (nb, Hkv) of the two gates, from the port."""
+    S, H, D = k_bits.shape
+    Sq, Hq, _ = q_bits.shape
+    nb = S // 512
+    bmax = np.zeros((nb, H), np.float32)
+    zeta = np.zeros((nb, H), np.float32)
+    p = lambda a: a.ctypes.data_as(C.c_void_p)
+    lib().oc_port_scores(p(k_bits), p(q_bits), S, H, Hq, D, Sq, p(bmax), p(zeta))
+    return bmax, zeta
+
+
 def decode(k_bits, v_bits, q_bits, tau, zeta_max, blocks_limit=0):
     """k_bits/v_bits (S,Hkv,D), q_bits (Sq,Hq,D): uint16 bf16 bit patterns.
     Returns keep (nb,Hkv) bool, perm (nb,), count, out (Sq,Hq,D) f32."""

@@ -26,6 +26,7 @@ from .pipeline import orthocache_forward
 from .indirect_attention import indirect_attention, compile_indirect_attention
 from .adaptive_attention import orthocache_attention, orthocache_attention_batched
 from .metadata_cache import SpectralMetadataCache
+from .paged import PagedKVCache
 
 __all__ = [
     "fwht_512", "compute_block_energy_jax", "generate_threshold_mask", "compute_query_aware_bounds",
@@ -33,5 +34,5 @@ __all__ = [
     "compute_multiband_mask", "score_blocks", "jax_block_sparse_attention",
     "compile_pallas_sparse_attention", "stream_compact", "stream_decompact", "compact_and_attend",
     "orthocache_forward", "indirect_attention", "compile_indirect_attention", "orthocache_attention",
-    "orthocache_attention_batched", "SpectralMetadataCache",
+    "orthocache_attention_batched", "SpectralMetadataCache", "PagedKVCache",
 ]

@@ -55,12 +55,22 @@ SIGNATURES = {
                                     _p, _sz, _p]),
     "oc_alltoallv_heads": (_i, [_p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _p, _p, _p, C.POINTER(_i), _p, _sz, _p]),
     "oc_decode_step_sharded_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
+    "oc_sharded_connect": (_i, [_p, _p, _sz, _i, _i, _i, _i, _i, _i, _p]),
+    "oc_sharded_disconnect": (_i, [_p]),
     "oc_decode_step_sharded": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p, _p, _p, _i, _p, _sz,
                                     _p]),
     "oc_indirect_attention": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
                                    _i, _p, _i, _p, _sz, _p]),
     "oc_prefill_attention": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
                                   _i, _p, _i, _p]),
+    "oc_indirect_attention_paged_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i, _i]),
+    "oc_indirect_attention_paged": (_i, [_p, _p, _p, _i, _p, _i, _p, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+                                         _p, _i, _p, _sz, _p]),
+    "oc_prefill_attention_paged_workspace_bytes": (_sz, [_i, _i]),
+    "oc_prefill_attention_paged": (_i, [_p, _p, _p, _i, _p, _i, _p, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+                                        _p, _i, _p, _sz, _p]),
+    "oc_score_from_metadata_paged": (_i, [_p, _p, _p, _i, _p, _i, _p, _i, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p,
+                                          _p, _p]),
     "oc_indirect_attention_noalloc_max_scratch_bytes": (_sz, []),
     "oc_indirect_attention_noalloc": (_i, [_p, _p, _p, _i, _p, _i, _i, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i,
                                            _i, _p, _i, _p]),

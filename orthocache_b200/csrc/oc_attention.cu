@@ -43,6 +43,8 @@ struct AttnArgs {
   int idx_stride, idx_hstride;      // list of (b, h) starts at b*idx_stride + h*idx_hstride
   int cnt_stride, cnt_hstride;      // its length is count[b*cnt_stride + h*cnt_hstride]
   int B, Sq, Hq, Hkv, G, D, S, bs;
+  int kv_rows;      // token rows of K / V per batch row (S; 0 for a page pool shared by the batch)
+  int nblk;         // block indices below this are valid (S / bs; the pool's pages)
   int R;            // query rows per kv head = Sq * G
   int n_rt;         // row tiles
   int chunk;        // tokens per item
@@ -129,7 +131,7 @@ attn_partial_kernel(AttnArgs a) {
     const int tok0 = blk * a.bs + c * a.chunk;
     const int r0 = rt * RT;
     const int nr = min(RT, a.R - r0);
-    if (blk < 0 || blk >= a.S / a.bs) {
+    if (blk < 0 || blk >= a.nblk) {
       // Out-of-range index: this item contributes nothing (no memory access).
       const size_t part = (((size_t)b * a.max_items + item) * a.Hkv + h) * a.R + r0;
       for (int x = tid; x < nr * D; x += kThreads) a.ws_o[part * D + x] = 0.f;
@@ -157,9 +159,9 @@ attn_partial_kernel(AttnArgs a) {
 
     const size_t tok_stride = (size_t)a.Hkv * D;
     const T* kbase = reinterpret_cast<const T*>(a.k) +
-                     (((size_t)b * a.S + tok0) * a.Hkv + h) * D + d0;
+                     (((size_t)b * a.kv_rows + tok0) * a.Hkv + h) * D + d0;
     const T* vbase = reinterpret_cast<const T*>(a.v) +
-                     (((size_t)b * a.S + tok0) * a.Hkv + h) * D + d0;
+                     (((size_t)b * a.kv_rows + tok0) * a.Hkv + h) * D + d0;
     const int trow0 = warp * ROWS_PER_WARP + sub;
 
     // ---- logits: s[r][t] = q_r . k_t (scaled) ----
@@ -449,7 +451,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     const int blk = k < kBlkCache ? s_blk[k] : a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
     // An out-of-range index is never dereferenced: block 0 is loaded instead
     // and the item is skipped.
-    const int y = (blk < 0 || blk >= a.S / a.bs) ? pos.b * a.S : pos.b * a.S + blk * a.bs + c * CH;
+    const int y = (blk < 0 || blk >= a.nblk) ? pos.b * a.kv_rows : pos.b * a.kv_rows + blk * a.bs + c * CH;
     uint8_t* dst = smem + (size_t)(k % kVStages) * kVStageBytes;
     uint64_t* bar = &full[k % kVStages];
     mbar_expect_tx(bar, 2 * KB);
@@ -562,7 +564,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     }
     const int slot = item / a.chunks;
     const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
-    const bool valid = !s_abort && blk >= 0 && blk < a.S / a.bs;
+    const bool valid = !s_abort && blk >= 0 && blk < a.nblk;
     const uint8_t* ks = smem + (size_t)stage * kVStageBytes;
     const uint8_t* vs = ks + KB;
     // K and V rows of this warp's tokens into registers, then release the stage.
@@ -653,7 +655,7 @@ template <int D>
 int launch_attn_stream(const AttnArgs& a, int rt, cudaStream_t st) {
   constexpr int CH = 8192 / D;
   CUtensorMap km, vm;
-  const uint64_t cols = (uint64_t)a.Hkv * D, rows = (uint64_t)a.B * a.S;
+  const uint64_t cols = (uint64_t)a.Hkv * D, rows = a.kv_rows ? (uint64_t)a.B * a.kv_rows : (uint64_t)a.nblk * a.bs;
   int rc = encode_map_2d(&km, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, D, CH);
   if (!rc) rc = encode_map_2d(&vm, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, D, CH);
   if (rc) return set_error(OC_ERR_CUDA, "attention: tensor map encode failed (%d)", rc);
@@ -803,7 +805,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   auto issue = [&](int k, const ItemIter& pos) {
     const int slot = pos.item / a.chunks, cc = pos.item - slot * a.chunks;
     const int blk = k < kBlkCache ? s_blk[k] : a.idx[(size_t)pos.b * a.idx_stride + (size_t)pos.h * a.idx_hstride + slot];
-    const int y = (blk < 0 || blk >= a.S / a.bs) ? pos.b * a.S : pos.b * a.S + blk * a.bs + cc * CH;
+    const int y = (blk < 0 || blk >= a.nblk) ? pos.b * a.kv_rows : pos.b * a.kv_rows + blk * a.bs + cc * CH;
     uint8_t* dst = smem + (size_t)(k % kMStages) * kMStageBytes;
     uint64_t* bar = &full[k % kMStages];
     mbar_expect_tx(bar, 2 * KB);
@@ -924,7 +926,7 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     if (k == 0) OC_STAMP(2);
     const int slot = item / a.chunks;
     const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
-    const bool valid = !s_abort && blk >= 0 && blk < a.S / a.bs;
+    const bool valid = !s_abort && blk >= 0 && blk < a.nblk;
     const uint32_t ks_base = smem_u32(smem + (size_t)stage * kMStageBytes);
     const uint32_t vs_base = ks_base + KB;
     // All fragments of this warp's 16 tokens, then the stage is released.
@@ -1009,7 +1011,7 @@ int launch_attn_mma(const AttnArgs& a, int rt, cudaStream_t st) {
   constexpr int CH = 8192 / D;
   constexpr int NT = 32 * CH / 16;
   CUtensorMap km, vm;
-  const uint64_t cols = (uint64_t)a.Hkv * D, rows = (uint64_t)a.B * a.S;
+  const uint64_t cols = (uint64_t)a.Hkv * D, rows = a.kv_rows ? (uint64_t)a.B * a.kv_rows : (uint64_t)a.nblk * a.bs;
   int rc = encode_map_2d(&km, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, CH, true);
   if (!rc) rc = encode_map_2d(&vm, a.v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, CH, true);
   if (rc) return set_error(OC_ERR_CUDA, "attention: tensor map encode failed (%d)", rc);
@@ -1260,7 +1262,7 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
                   int B, int Sq, int Hq, int Hkv, int D,
                   int S, int bs, int max_blocks, void* out, int out_dtype, float* pm, float* pl,
                   float* po, void* ws, size_t ws_bytes, int mode, cudaStream_t st,
-                  const uint8_t* keep = nullptr, int32_t* perm_out = nullptr) {
+                  const uint8_t* keep = nullptr, int32_t* perm_out = nullptr, int pool_pages = 0) {
   int rc = validate_attn(q, k, v, dtype, idx, idx_stride, idx_hstride, count, B, Sq, Hq, Hkv, D, S, bs,
                          max_blocks);
   if (rc) return rc;
@@ -1274,6 +1276,10 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.idx_stride = idx_stride; a.idx_hstride = idx_hstride;
   a.cnt_stride = cnt_stride; a.cnt_hstride = cnt_hstride;
   a.B = B; a.Sq = Sq; a.Hq = Hq; a.Hkv = Hkv; a.G = Hq / Hkv; a.D = D; a.S = S; a.bs = bs;
+  // pool_pages > 0: k / v are a pool of pool_pages blocks shared by the
+  // batch, and the index lists hold pool pages
+  a.kv_rows = pool_pages > 0 ? 0 : S;
+  a.nblk = pool_pages > 0 ? pool_pages : S / bs;
   a.R = Sq * a.G;
   const bool tma = use_tma_path(dtype, bs, D);
   const bool mma = tma && (D == 64 || D == 128);  // tensor-core stream kernel
@@ -1368,6 +1374,42 @@ extern "C" int oc_indirect_attention(const void* q, const void* k, const void* v
                        count_head_stride, batch, q_len, q_heads, kv_heads, head_dim,
                        seq_len, block_size, max_blocks, out, out_dtype, nullptr, nullptr, nullptr, workspace,
                        workspace_bytes, 0, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t oc_indirect_attention_paged_workspace_bytes(int batch, int q_len, int q_heads, int kv_heads,
+                                                              int head_dim, int block_size, int max_blocks) {
+  const size_t attn = oc_indirect_attention_workspace_bytes(batch, q_len, q_heads, kv_heads, head_dim, block_size,
+                                                            max_blocks);
+  if (!attn && max_blocks > 0) return 0;
+  return align256((size_t)batch * max_blocks * sizeof(int32_t)) + attn;
+}
+
+extern "C" int oc_indirect_attention_paged(const void* q, const void* k_pool, const void* v_pool, int dtype,
+                                           const int32_t* block_table, int table_stride, const int32_t* idx,
+                                           int idx_stride, const int32_t* count, int count_stride, int batch,
+                                           int q_len, int q_heads, int kv_heads, int head_dim, int num_pages,
+                                           int block_size, int max_blocks, void* out, int out_dtype,
+                                           void* workspace, size_t workspace_bytes, oc_stream_t stream) {
+  OC_REQUIRE(out && block_table && idx && count, OC_ERR_NULL, "oc_indirect_attention_paged: NULL pointer");
+  OC_REQUIRE(num_pages >= 1 && table_stride >= 1 && max_blocks >= 0 && max_blocks <= table_stride, OC_ERR_SHAPE,
+             "oc_indirect_attention_paged: num_pages %d, table_stride %d, max_blocks %d", num_pages, table_stride,
+             max_blocks);
+  OC_REQUIRE(idx_stride >= 0 && count_stride >= 0 && batch >= 1, OC_ERR_SHAPE, "oc_indirect_attention_paged: bad strides");
+  const size_t need = oc_indirect_attention_paged_workspace_bytes(batch, q_len, q_heads, kv_heads, head_dim,
+                                                                  block_size, max_blocks);
+  OC_REQUIRE(need && workspace && workspace_bytes >= need, OC_ERR_CAPACITY,
+             "oc_indirect_attention_paged: workspace %zu < %zu bytes", workspace_bytes, need);
+  OC_REQUIRE((int64_t)num_pages * block_size < INT32_MAX, OC_ERR_SHAPE, "oc_indirect_attention_paged: pool too large");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int32_t* phys = static_cast<int32_t*>(workspace);
+  const size_t lists = align256((size_t)batch * max_blocks * sizeof(int32_t));
+  int rc = compose_page_lists(block_table, table_stride, table_stride, idx, idx_stride, count, count_stride, batch,
+                              max_blocks, num_pages, phys, st);
+  if (rc) return rc;
+  return run_attention(q, k_pool, v_pool, dtype, phys, max_blocks, 0, count, count_stride, 0, batch, q_len, q_heads,
+                       kv_heads, head_dim, table_stride * block_size, block_size, max_blocks, out, out_dtype, nullptr,
+                       nullptr, nullptr, static_cast<char*>(workspace) + lists, workspace_bytes - lists, 0, st,
+                       nullptr, nullptr, num_pages);
 }
 
 extern "C" int oc_partial_attention(const void* q, const void* k, const void* v, int dtype,

@@ -21,6 +21,7 @@
 // process (the one that created the caller's communicator, e.g. PyTorch's) if
 // there is one, else libnccl.so.2 (or the path in OC_NCCL_LIBRARY).  Only the
 // types come from nccl.h; the ABI of these calls is stable across NCCL 2.x.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -318,13 +319,170 @@ extern "C" int oc_alltoallv_heads(void* comm, const void* k, const void* v, int 
   return OC_OK;
 }
 
+namespace oc {
+namespace {
+
+// Layout of the sharded decode workspace: the decode step's workspace, the
+// packed send partial and P received partials of the NCCL path, the table of
+// the P ranks' exchange-region addresses, then this rank's exchange region.
+struct ShardedLayout {
+  size_t base, part, table, region, bytes;
+  int NG;
+};
+
+ShardedLayout sharded_layout(int P, int B, int Sq, int Hq, int Hkv, int D, int S) {
+  ShardedLayout L = {};
+  L.base = oc_decode_step_workspace_bytes(B, Sq, Hq, Hkv, D, S);
+  if (!L.base || P < 1) return L;
+  const size_t rows = (size_t)B * Sq * Hq;
+  L.part = (rows * (D + 2) * sizeof(float) + 255) / 256 * 256;
+  L.NG = B * Hkv;
+  L.table = L.base + L.part * (1 + P);
+  L.region = L.table + ((size_t)P * sizeof(void*) + 255) / 256 * 256;
+  L.bytes = L.region + xchg_region_bytes(P, L.NG);
+  return L;
+}
+
+// Workspaces whose exchange regions are mapped into every rank (host side).
+struct Connection {
+  int P, rank;
+  std::vector<void*> opened;  // peer allocations mapped by cudaIpcOpenMemHandle
+};
+std::mutex g_conn_mu;
+std::vector<std::pair<void*, Connection>> g_conns;
+
+Connection* find_conn(void* ws) {
+  for (auto& c : g_conns)
+    if (c.first == ws) return &c.second;
+  return nullptr;
+}
+
+using AddrRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddrRangeFn addr_range_fn() {
+  static AddrRangeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddrRangeFn>(p);
+  }
+  return fn;
+}
+
+struct IpcRecord {
+  cudaIpcMemHandle_t handle;
+  uint64_t offset;  // of the exchange region from the allocation's base
+  uint64_t pad;
+};
+
+}  // namespace
+}  // namespace oc
+
 extern "C" size_t oc_decode_step_sharded_workspace_bytes(int nranks, int batch, int q_len, int q_heads,
                                                          int kv_heads, int head_dim, int seq_len) {
-  const size_t base = oc_decode_step_workspace_bytes(batch, q_len, q_heads, kv_heads, head_dim, seq_len);
-  if (!base || nranks < 1) return 0;
-  const size_t rows = (size_t)batch * q_len * q_heads;
-  const size_t part = (rows * (head_dim + 2) * sizeof(float) + 255) / 256 * 256;
-  return base + part * (1 + nranks);
+  return oc::sharded_layout(nranks, batch, q_len, q_heads, kv_heads, head_dim, seq_len).bytes;
+}
+
+extern "C" int oc_sharded_connect(void* comm, void* workspace, size_t workspace_bytes, int batch, int q_len,
+                                  int q_heads, int kv_heads, int head_dim, int seq_len, oc_stream_t stream) {
+  const char* what = "oc_sharded_connect";
+  OC_REQUIRE(comm && workspace, OC_ERR_NULL, "%s: NULL argument", what);
+  const NcclApi* n = nccl();
+  if (!n) return set_error(OC_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
+  ncclComm_t c = reinterpret_cast<ncclComm_t>(comm);
+  int P = 0, me = 0, rc;
+  if ((rc = comm_shape(n, c, &P, &me, what))) return rc;
+  const ShardedLayout L = sharded_layout(P, batch, q_len, q_heads, kv_heads, head_dim, seq_len);
+  OC_REQUIRE(L.bytes && workspace_bytes >= L.bytes, OC_ERR_CAPACITY, "%s: workspace %zu < %zu bytes", what,
+             workspace_bytes, L.bytes);
+  OC_REQUIRE(head_dim == 128 && q_len * (q_heads / kv_heads) <= 8, OC_ERR_UNSUPPORTED,
+             "%s: the peer exchange serves the fused decode layer (head_dim 128, <= 8 query rows per KV head)",
+             what);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  char* region = ws + L.region;
+  AddrRangeFn range = addr_range_fn();
+  if (!range) return set_error(OC_ERR_CUDA, "%s: cuMemGetAddressRange is unavailable", what);
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(region)) != CUDA_SUCCESS)
+    return set_error(OC_ERR_CUDA, "%s: cuMemGetAddressRange failed", what);
+  IpcRecord mine = {};
+  cudaError_t e = cudaIpcGetMemHandle(&mine.handle, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "%s: cudaIpcGetMemHandle: %s", what, cudaGetErrorString(e));
+  mine.offset = reinterpret_cast<uint64_t>(region) - base;
+  // all-gather the records through NCCL, staged in the NCCL path's receive
+  // buffers (scratch at this point)
+  char* stage = ws + L.base;
+  const size_t rec = sizeof(IpcRecord);
+  OC_REQUIRE(rec * (1 + P) <= L.part * (1 + P), OC_ERR_CAPACITY, "%s: staging too small", what);
+  e = cudaMemcpyAsync(stage, &mine, rec, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  OC_NCCL(n->AllGather(stage, stage + rec, rec, ncclUint8, c, st), what);
+  std::vector<IpcRecord> all(P);
+  e = cudaMemcpyAsync(all.data(), stage + rec, rec * P, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  Connection conn;
+  conn.P = P;
+  conn.rank = me;
+  std::vector<char*> table(P);
+  cudaError_t open_err = cudaSuccess;
+  for (int p = 0; p < P && open_err == cudaSuccess; ++p) {
+    if (p == me) {
+      table[p] = region;
+      continue;
+    }
+    void* mapped = nullptr;
+    open_err = cudaIpcOpenMemHandle(&mapped, all[p].handle, cudaIpcMemLazyEnablePeerAccess);
+    if (open_err == cudaSuccess) {
+      conn.opened.push_back(mapped);
+      table[p] = static_cast<char*>(mapped) + all[p].offset;
+    }
+  }
+  // the table, and flags that start at zero (the call numbers start at 1)
+  const size_t flag_off = (size_t)2 * P * L.NG * kXchgBlock * sizeof(float);
+  e = open_err;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ws + L.table, table.data(), sizeof(char*) * P, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(region + flag_off, 0, (size_t)2 * P * L.NG * sizeof(int), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  // Agree on the outcome: every rank learns whether every other rank is
+  // connected (and has its flags at zero) before any exchange, so that no
+  // rank takes the peer path while another takes NCCL.
+  mine.pad = e == cudaSuccess ? 0 : 1;
+  cudaError_t e2 = cudaMemcpyAsync(stage, &mine, rec, cudaMemcpyHostToDevice, st);
+  if (e2 != cudaSuccess) return set_error(OC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e2));
+  OC_NCCL(n->AllGather(stage, stage + rec, rec, ncclUint8, c, st), what);
+  e2 = cudaMemcpyAsync(all.data(), stage + rec, rec * P, cudaMemcpyDeviceToHost, st);
+  if (e2 == cudaSuccess) e2 = cudaStreamSynchronize(st);
+  if (e2 != cudaSuccess) return set_error(OC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e2));
+  bool all_ok = true;
+  for (int p = 0; p < P; ++p) all_ok = all_ok && all[p].pad == 0;
+  if (!all_ok) {
+    for (void* m : conn.opened) cudaIpcCloseMemHandle(m);
+    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return set_error(OC_ERR_UNSUPPORTED, "%s: another rank could not map the exchange regions", what);
+  }
+  std::lock_guard<std::mutex> lock(g_conn_mu);
+  if (Connection* old = find_conn(workspace)) {
+    for (void* m : old->opened) cudaIpcCloseMemHandle(m);
+    *old = conn;
+  } else {
+    g_conns.emplace_back(workspace, conn);
+  }
+  return OC_OK;
+}
+
+extern "C" int oc_sharded_disconnect(void* workspace) {
+  std::lock_guard<std::mutex> lock(g_conn_mu);
+  for (size_t i = 0; i < g_conns.size(); ++i)
+    if (g_conns[i].first == workspace) {
+      for (void* m : g_conns[i].second.opened) cudaIpcCloseMemHandle(m);
+      g_conns.erase(g_conns.begin() + i);
+      return OC_OK;
+    }
+  return OC_OK;
 }
 
 extern "C" int oc_decode_step_sharded(void* comm, const void* q, const void* k, const void* v, int dtype, int batch,
@@ -338,20 +496,38 @@ extern "C" int oc_decode_step_sharded(void* comm, const void* q, const void* k, 
   ncclComm_t c = reinterpret_cast<ncclComm_t>(comm);
   int P = 0, me = 0, rc;
   if ((rc = comm_shape(n, c, &P, &me, what))) return rc;
-  const size_t need = oc_decode_step_sharded_workspace_bytes(P, batch, q_len, q_heads, kv_heads, head_dim, seq_len);
-  OC_REQUIRE(need && workspace_bytes >= need, OC_ERR_CAPACITY, "%s: workspace %zu < %zu bytes", what, workspace_bytes,
-             need);
-  const size_t base = oc_decode_step_workspace_bytes(batch, q_len, q_heads, kv_heads, head_dim, seq_len);
+  const ShardedLayout L = sharded_layout(P, batch, q_len, q_heads, kv_heads, head_dim, seq_len);
+  OC_REQUIRE(L.bytes && workspace_bytes >= L.bytes, OC_ERR_CAPACITY, "%s: workspace %zu < %zu bytes", what,
+             workspace_bytes, L.bytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  bool connected = false;
+  {
+    std::lock_guard<std::mutex> lock(g_conn_mu);
+    const Connection* cn = find_conn(workspace);
+    connected = cn && cn->P == P && cn->rank == me;
+  }
+  if (connected && dtype == OC_BF16) {
+    // one kernel: the fused layer merges its shard's partial with every
+    // rank's through the mapped exchange regions
+    PeerXchg px;
+    px.bases = reinterpret_cast<char* const*>(ws + L.table);
+    px.P = P;
+    px.rank = me;
+    px.flag_off = (size_t)2 * P * L.NG * kXchgBlock * sizeof(float);
+    rc = decode_fused(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max, keep, perm, count,
+                      out, out_dtype, nullptr, nullptr, nullptr, workspace, L.base, st, &px);
+    if (rc != OC_ERR_UNSUPPORTED) return rc;
+  }
   const int rows = batch * q_len * q_heads;
-  const size_t part = ((size_t)rows * (head_dim + 2) * sizeof(float) + 255) / 256 * 256;
-  float* send = reinterpret_cast<float*>(static_cast<char*>(workspace) + base);
-  float* recv = reinterpret_cast<float*>(static_cast<char*>(workspace) + base + part);
+  float* send = reinterpret_cast<float*>(ws + L.base);
+  float* recv = reinterpret_cast<float*>(ws + L.base + L.part);
   // this shard's partial, packed [m (rows) | l (rows) | o (rows, D)]
   rc = oc_decode_step_partial(q, k, v, dtype, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max, keep,
-                              perm, count, send, send + rows, send + 2 * (size_t)rows, workspace, base, stream);
+                              perm, count, send, send + rows, send + 2 * (size_t)rows, workspace, L.base, stream);
   if (rc) return rc;
   // the P partials land back to back in recv, the layout the merge reads
   const size_t floats = (size_t)rows * (head_dim + 2);
-  OC_NCCL(n->AllGather(send, recv, floats, ncclFloat32, c, reinterpret_cast<cudaStream_t>(stream)), what);
+  OC_NCCL(n->AllGather(send, recv, floats, ncclFloat32, c, st), what);
   return oc_merge_partials_packed(recv, P, rows, head_dim, out, out_dtype, stream);
 }

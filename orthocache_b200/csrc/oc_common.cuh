@@ -44,10 +44,29 @@ int wait_limit_prefill(unsigned long long ns);
 // po non-null it writes the layer's (m, l, o) partials (the format of
 // oc_partial_attention) instead of out.
 size_t decode_fused_bytes(int batch, int seq_len, int kv_heads);
+// Cross-GPU exchange of the fused layer's per-shard partials by peer stores:
+// every rank's exchange region (recv blocks, then flags) is mapped into
+// every other rank's address space; bases[p] is rank p's region (this
+// rank's own at [rank]), a device array of P pointers.  Region layout:
+// recv float[2][P][NG][kXchgBlock] (parity of the call, source rank, group
+// (b, h): m[8] | l[8] | o[8][128]), then flags int[2][P][NG].
+struct PeerXchg {
+  char* const* bases;
+  int P, rank;
+  size_t flag_off;  // byte offset of the flags inside a region
+};
+constexpr int kXchgBlock = 8 * (128 + 2);
+size_t xchg_region_bytes(int P, int NG);
 int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
                  int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
                  void* out, int out_dtype, float* pm, float* pl, float* po, void* ws, size_t ws_bytes,
-                 cudaStream_t st);
+                 cudaStream_t st, const PeerXchg* px = nullptr);
+
+// Paged KV: phys (batch, max_blocks) = block_table[b][idx[b][i]] for the
+// first min(count[b], max_blocks) entries, -1 elsewhere (oc_compact.cu).
+int compose_page_lists(const int32_t* table, int table_stride, int nlogical, const int32_t* idx, int idx_stride,
+                       const int32_t* count, int count_stride, int batch, int max_blocks, int num_pages,
+                       int32_t* phys, cudaStream_t st);
 
 #define OC_REQUIRE(cond, code, ...)                                   \
   do {                                                                \

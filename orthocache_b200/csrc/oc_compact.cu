@@ -332,3 +332,41 @@ extern "C" int oc_exchange_index(const int32_t* all_counts, int num_devices, int
   exchange_index_kernel<<<1, kScanThreads, 0, st>>>(all_counts, num_devices, slots, order, total, offsets);
   return check_launch("exchange_index_kernel");
 }
+
+// ---------------------------------------------------------------------------
+// Paged KV: index lists of logical blocks -> lists of pool pages.
+// phys[b][i] = table[b][idx[b][i]] for i < min(count[b], max_blocks), -1
+// elsewhere or for a logical index outside the table (the attention kernels
+// skip negative entries).
+// ---------------------------------------------------------------------------
+namespace oc {
+namespace {
+__global__ void page_lists_kernel(const int32_t* __restrict__ table, int table_stride, int nlogical,
+                                  const int32_t* __restrict__ idx, int idx_stride, const int32_t* __restrict__ count,
+                                  int count_stride, int max_blocks, int num_pages, int32_t* __restrict__ phys) {
+  const int b = blockIdx.y;
+  const int n = min(max(count[(size_t)b * count_stride], 0), max_blocks);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < max_blocks; i += gridDim.x * blockDim.x) {
+    int p = -1;
+    if (i < n) {
+      const int j = idx[(size_t)b * idx_stride + i];
+      if (j >= 0 && j < nlogical) {
+        p = table[(size_t)b * table_stride + j];
+        if (p < 0 || p >= num_pages) p = -1;
+      }
+    }
+    phys[(size_t)b * max_blocks + i] = p;
+  }
+}
+}  // namespace
+
+int compose_page_lists(const int32_t* table, int table_stride, int nlogical, const int32_t* idx, int idx_stride,
+                       const int32_t* count, int count_stride, int batch, int max_blocks, int num_pages,
+                       int32_t* phys, cudaStream_t st) {
+  if (max_blocks == 0) return OC_OK;
+  dim3 grid((max_blocks + 255) / 256, batch);
+  page_lists_kernel<<<grid, 256, 0, st>>>(table, table_stride, nlogical, idx, idx_stride, count, count_stride,
+                                          max_blocks, num_pages, phys);
+  return check_launch("page_lists_kernel");
+}
+}  // namespace oc

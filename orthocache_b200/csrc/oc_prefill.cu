@@ -83,6 +83,7 @@ struct PfArgs {
   void* out;
   int out_dtype;
   int B, Sq, Hq, Hkv, S, bs, max_blocks;
+  int kv_rows;  // token rows of K / V per batch row (S; 0 for a page pool shared by the batch)
   int idx_stride, idx_hstride, count_stride, count_hstride;
   int G, nqt, tiles_per_head, npairs, units;
   float scale_log2;  // log2(e) / sqrt(D)
@@ -246,7 +247,7 @@ __device__ __forceinline__ PfUnit pf_unit(const PfArgs& a, int u) {
 __device__ __forceinline__ int pf_token(const PfArgs& a, const PfUnit& w, int j) {
   const int tpb = a.bs / kPfTok;
   const int blk = w.idx[j / tpb];
-  return w.b * a.S + blk * a.bs + (j % tpb) * kPfTok;
+  return w.b * a.kv_rows + blk * a.bs + (j % tpb) * kPfTok;
 }
 
 __device__ __forceinline__ bool pf_wait(PfSmem& sm, uint64_t* bar, uint32_t parity) {
@@ -574,12 +575,13 @@ int prefill_status(int* status, int reset) {
 
 using namespace oc;
 
-extern "C" int oc_prefill_attention(const void* q, const void* k, const void* v, int dtype,
-                                    const int32_t* idx, int idx_stride, int idx_head_stride,
-                                    const int32_t* count, int count_stride, int count_head_stride,
-                                    int batch, int q_len, int q_heads, int kv_heads, int head_dim,
-                                    int seq_len, int block_size, int max_blocks,
-                                    void* out, int out_dtype, oc_stream_t stream) {
+namespace {
+// pool_pages > 0: k / v are a pool of pool_pages blocks shared by the batch
+// and idx holds pool pages; seq_len is then the logical capacity.
+int prefill_impl(const void* q, const void* k, const void* v, int dtype, const int32_t* idx, int idx_stride,
+                 int idx_head_stride, const int32_t* count, int count_stride, int count_head_stride, int batch,
+                 int q_len, int q_heads, int kv_heads, int head_dim, int seq_len, int block_size, int max_blocks,
+                 void* out, int out_dtype, oc_stream_t stream, int pool_pages) {
   OC_REQUIRE(q && k && v && idx && count && out, OC_ERR_NULL, "oc_prefill_attention: NULL pointer");
   OC_REQUIRE(dtype == OC_BF16, OC_ERR_DTYPE, "oc_prefill_attention: inputs must be bfloat16");
   OC_REQUIRE(out_dtype == OC_BF16 || out_dtype == OC_F32, OC_ERR_DTYPE, "oc_prefill_attention: bad out dtype");
@@ -609,6 +611,7 @@ extern "C" int oc_prefill_attention(const void* q, const void* k, const void* v,
   a.Hq = q_heads;
   a.Hkv = kv_heads;
   a.S = seq_len;
+  a.kv_rows = pool_pages > 0 ? 0 : seq_len;
   a.bs = block_size;
   a.max_blocks = max_blocks;
   a.idx_stride = idx_stride;
@@ -626,8 +629,9 @@ extern "C" int oc_prefill_attention(const void* q, const void* k, const void* v,
 
   CUtensorMap mq, mk, mv;
   int rc = pf_map(&mq, q, q_heads, (int64_t)batch * q_len, "q");
-  if (!rc) rc = pf_map(&mk, k, kv_heads, (int64_t)batch * seq_len, "k");
-  if (!rc) rc = pf_map(&mv, v, kv_heads, (int64_t)batch * seq_len, "v");
+  const int64_t kv_total = pool_pages > 0 ? (int64_t)pool_pages * block_size : (int64_t)batch * seq_len;
+  if (!rc) rc = pf_map(&mk, k, kv_heads, kv_total, "k");
+  if (!rc) rc = pf_map(&mv, v, kv_heads, kv_total, "v");
   if (rc) return rc;
 
   auto kern = out_dtype == OC_BF16 ? prefill_attn_kernel<__nv_bfloat16> : prefill_attn_kernel<float>;
@@ -641,3 +645,43 @@ extern "C" int oc_prefill_attention(const void* q, const void* k, const void* v,
   kern<<<grid, kPfThreads, kPfSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, a);
   return check_launch("prefill_attn_kernel");
 }
+}  // namespace
+
+extern "C" int oc_prefill_attention(const void* q, const void* k, const void* v, int dtype,
+                                    const int32_t* idx, int idx_stride, int idx_head_stride,
+                                    const int32_t* count, int count_stride, int count_head_stride,
+                                    int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                    int seq_len, int block_size, int max_blocks,
+                                    void* out, int out_dtype, oc_stream_t stream) {
+  return prefill_impl(q, k, v, dtype, idx, idx_stride, idx_head_stride, count, count_stride, count_head_stride, batch,
+                      q_len, q_heads, kv_heads, head_dim, seq_len, block_size, max_blocks, out, out_dtype, stream, 0);
+}
+
+extern "C" size_t oc_prefill_attention_paged_workspace_bytes(int batch, int max_blocks) {
+  if (batch < 1 || max_blocks < 0) return 0;
+  return ((size_t)batch * max_blocks * sizeof(int32_t) + 255) / 256 * 256;
+}
+
+extern "C" int oc_prefill_attention_paged(const void* q, const void* k_pool, const void* v_pool, int dtype,
+                                          const int32_t* block_table, int table_stride, const int32_t* idx,
+                                          int idx_stride, const int32_t* count, int count_stride, int batch,
+                                          int q_len, int q_heads, int kv_heads, int head_dim, int num_pages,
+                                          int block_size, int max_blocks, void* out, int out_dtype, void* workspace,
+                                          size_t workspace_bytes, oc_stream_t stream) {
+  OC_REQUIRE(block_table && idx && count && workspace, OC_ERR_NULL, "oc_prefill_attention_paged: NULL pointer");
+  OC_REQUIRE(num_pages >= 1 && table_stride >= 1 && max_blocks >= 0 && max_blocks <= table_stride && batch >= 1,
+             OC_ERR_SHAPE, "oc_prefill_attention_paged: num_pages %d, table_stride %d, max_blocks %d", num_pages,
+             table_stride, max_blocks);
+  OC_REQUIRE((int64_t)num_pages * block_size < INT32_MAX, OC_ERR_SHAPE, "oc_prefill_attention_paged: pool too large");
+  const size_t need = oc_prefill_attention_paged_workspace_bytes(batch, max_blocks);
+  OC_REQUIRE(workspace_bytes >= need, OC_ERR_CAPACITY, "oc_prefill_attention_paged: workspace %zu < %zu bytes",
+             workspace_bytes, need);
+  int32_t* phys = static_cast<int32_t*>(workspace);
+  int rc = compose_page_lists(block_table, table_stride, table_stride, idx, idx_stride, count, count_stride, batch,
+                              max_blocks, num_pages, phys, reinterpret_cast<cudaStream_t>(stream));
+  if (rc) return rc;
+  return prefill_impl(q, k_pool, v_pool, dtype, phys, max_blocks, 0, count, count_stride, 0, batch, q_len, q_heads,
+                      kv_heads, head_dim, table_stride * block_size, block_size, max_blocks, out, out_dtype, stream,
+                      num_pages);
+}
+

@@ -453,6 +453,7 @@ struct FusedArgs {
   int32_t* count;   // (B)
   int B, NG, cpg, R;
   float scale_log2;
+  PeerXchg px;      // px.P > 0: merge this shard's partial with every rank's by peer stores
 };
 
 // One call's counters.  A call uses set (epoch & 1); CTA 0 zeroes the other
@@ -545,6 +546,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   __shared__ __align__(8) uint64_t empty[kStages];  // fused: stage free for the producer
   __shared__ int s_desc[kStages];            // fused: unit in a stage (block * 4 + chunk), -1 = end
   __shared__ int s_set;                      // fused: counter set of this call
+  __shared__ int s_seq;                      // fused: calls before this one (the epoch)
   __shared__ __align__(8) uint64_t setbar;   // fused: s_set is known (after the previous kernel)
   __shared__ int s_merge;                    // fused: this CTA merges its group
   __shared__ int s_rel[kStages];             // warps done with a stage
@@ -650,7 +652,8 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     pdl_wait();
     if constexpr (FUSED) {
       if (e == 0 && lane == 0) {
-        s_set = __ldcg(f.epoch) & 1;
+        s_seq = __ldcg(f.epoch);
+        s_set = s_seq & 1;
         OC_SSTAMP(8, globaltimer_ns());
       }
       asm volatile("bar.sync 1, %0;" ::"r"(NE * 32) : "memory");
@@ -1184,11 +1187,73 @@ scored:
         }
         const int s = r / a.G, gq = r - s * a.G;
         const size_t orow = ((size_t)bq * a.Sq + s) * a.Hq + (size_t)hq * a.G + gq;
-        if (f.pm) {
+        if (f.px.P > 0) {
+          // This shard's partial of group grp into slot [parity][rank][grp]
+          // of every rank's exchange region (plain stores over NVLink).
+          const size_t slot = ((size_t)(s_seq & 1) * f.px.P + f.px.rank) * f.NG + grp;
+          for (int p = 0; p < f.px.P; ++p) {
+            float* blk = reinterpret_cast<float*>(f.px.bases[p]) + slot * kXchgBlock;
+            blk[16 + r * D + d] = O;
+            if (d == 0) { blk[r] = M; blk[8 + r] = L; }
+          }
+        } else if (f.pm) {
           // Unnormalised partial of this shard for a cross-shard merge.
           f.po[orow * D + d] = O;
           if (d == 0) { f.pm[orow] = M; f.pl[orow] = L; }
         } else {
+          const float y = L > 0.f ? O / L : 0.f;
+          if (f.out_bf16) reinterpret_cast<__nv_bfloat16*>(f.out)[orow * D + d] = __float2bfloat16_rn(y);
+          else reinterpret_cast<float*>(f.out)[orow * D + d] = y;
+        }
+      }
+    }
+    if (f.px.P > 0 && s_merge) {
+      // Publish: every thread's stores reach the peers before the flag
+      // (system-scope fence, then the barrier, then a release store), and
+      // the flag carries the call number, so slots are reused every other
+      // call without clearing.  Then wait (bounded) for every rank's flag of
+      // this call and merge the P partials of the group: out on every rank.
+      __threadfence_system();
+      asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+      const int par = s_seq & 1, flag = s_seq + 1;
+      if (tid < f.px.P) {
+        int* fl = reinterpret_cast<int*>(f.px.bases[tid] + f.px.flag_off) +
+                  ((size_t)par * f.px.P + f.px.rank) * f.NG + grp;
+        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl), "r"(flag) : "memory");
+      }
+      if (tid < 32) {
+        const int* mine = reinterpret_cast<const int*>(f.px.bases[f.px.rank] + f.px.flag_off) +
+                          (size_t)par * f.px.P * f.NG + grp;
+        const uint64_t t0 = globaltimer_ns();
+        for (int src = lane; src < f.px.P; src += 32) {
+          int v;
+          for (;;) {
+            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + (size_t)src * f.NG) : "memory");
+            if (v == flag) break;
+            if (globaltimer_ns() - t0 > g_wait_limit_ns) { s_abort = 1; atomicExch(&g_score_status, 1); break; }
+            __nanosleep(64);
+          }
+        }
+        __syncwarp();
+      }
+      asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+      if (!s_abort) {
+        const float* base = reinterpret_cast<const float*>(f.px.bases[f.px.rank]);
+        for (int x = tid; x < f.R * D; x += kScoreThreads) {
+          const int r = x / D, d = x - r * D;
+          float M = -INFINITY;
+          for (int src = 0; src < f.px.P; ++src)
+            M = fmaxf(M, __ldcv(base + ((size_t)(par * f.px.P + src) * f.NG + grp) * kXchgBlock + r));
+          float L = 0.f, O = 0.f;
+          if (M != -INFINITY)
+            for (int src = 0; src < f.px.P; ++src) {
+              const float* blk = base + ((size_t)(par * f.px.P + src) * f.NG + grp) * kXchgBlock;
+              const float w = exp2f(__ldcv(blk + r) - M);
+              L = fmaf(__ldcv(blk + 8 + r), w, L);
+              O = fmaf(__ldcv(blk + 16 + r * D + d), w, O);
+            }
+          const int s = r / a.G, gq = r - s * a.G;
+          const size_t orow = ((size_t)bq * a.Sq + s) * a.Hq + (size_t)hq * a.G + gq;
           const float y = L > 0.f ? O / L : 0.f;
           if (f.out_bf16) reinterpret_cast<__nv_bfloat16*>(f.out)[orow * D + d] = __float2bfloat16_rn(y);
           else reinterpret_cast<float*>(f.out)[orow * D + d] = y;
@@ -1491,20 +1556,41 @@ int score_blocks_impl(const void* keys, const void* q, int dtype, int batch, int
 // ---------------------------------------------------------------------------
 namespace oc {
 namespace {
+// Where the metadata of logical cell (b, j, h) lives: the cell itself, or,
+// for a paged cache, page table[b][j] of a pool of num_pages pages (-1: an
+// invalid page, whose block is never kept).
+struct MetaSrc {
+  const int32_t* table;
+  int table_stride, num_pages;
+};
+__device__ __forceinline__ int64_t meta_src(const MetaSrc& m, int b, int j, int h, int nb, int H) {
+  if (!m.table) return ((int64_t)b * nb + j) * H + h;
+  const int p = m.table[(size_t)b * m.table_stride + j];
+  return (p >= 0 && p < m.num_pages) ? (int64_t)p * H + h : -1;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 meta_gates_kernel(const float* __restrict__ dc, const float* __restrict__ e_ac, const float* __restrict__ zeta,
                   const T* __restrict__ q, int nb, int H, int D, int Sq, int Hq, int G, int64_t cells, float tau,
-                  float zeta_max, float* bound_max, float* bounds, uint8_t* keep) {
+                  float zeta_max, float* bound_max, float* bounds, uint8_t* keep, MetaSrc ms) {
   const int lane = threadIdx.x & 31;
   const int64_t cell = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (cell >= cells) return;
   const int h = (int)(cell % H);
   const int j = (int)((cell / H) % nb);
   const int b = (int)(cell / ((int64_t)H * nb));
+  const int64_t src = meta_src(ms, b, j, h, nb, H);
+  if (src < 0) {
+    if (lane == 0) {
+      if (bound_max) bound_max[cell] = -INFINITY;
+      if (keep) keep[cell] = 0;
+    }
+    return;
+  }
   const float sqrt_d = sqrtf((float)D);
-  const float resid_scale = sqrtf(e_ac[cell]);
-  const float* dcc = dc + cell * D;
+  const float resid_scale = sqrtf(e_ac[src]);
+  const float* dcc = dc + src * D;
   float bmax = -INFINITY;
   const int rows = Sq * G;
   for (int r = 0; r < rows; ++r) {
@@ -1525,7 +1611,7 @@ meta_gates_kernel(const float* __restrict__ dc, const float* __restrict__ e_ac, 
   }
   if (lane == 0) {
     if (bound_max) bound_max[cell] = bmax;
-    if (keep) keep[cell] = (bmax >= tau && zeta[cell] <= zeta_max) ? 1 : 0;
+    if (keep) keep[cell] = (bmax >= tau && zeta[src] <= zeta_max) ? 1 : 0;
   }
 }
 }  // namespace
@@ -1566,7 +1652,7 @@ constexpr int kMetaGemmMinRows = 32;  // query rows per KV head above which the 
 template <typename T>
 __global__ void __launch_bounds__(256)
 meta_bound_gemm_kernel(const float* __restrict__ dc, const float* __restrict__ e_ac, const T* __restrict__ q,
-                       int nb, int H, int D, int Sq, int Hq, int G, int* key, float* bounds) {
+                       int nb, int H, int D, int Sq, int Hq, int G, int* key, float* bounds, MetaSrc ms) {
   __shared__ float qs[kMbK][kMbRows + 4];
   __shared__ float ds[kMbK][kMbBlk + 4];
   __shared__ float s_nrm[kMbRows];
@@ -1584,7 +1670,8 @@ meta_bound_gemm_kernel(const float* __restrict__ dc, const float* __restrict__ e
     qrow = q + (((size_t)b * Sq + s) * Hq + (size_t)h * G + g) * D;
   }
   const int lb = tid >> 2, lq = tid & 3;  // dc: block lb, 8 dims at lq*8
-  const float* dcrow = (j0 + lb < nb) ? dc + (((size_t)b * nb + j0 + lb) * H + h) * D : nullptr;
+  const int64_t dsrc = (j0 + lb < nb) ? meta_src(ms, b, j0 + lb, h, nb, H) : -1;
+  const float* dcrow = dsrc >= 0 ? dc + dsrc * D : nullptr;
   float acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -1624,12 +1711,13 @@ meta_bound_gemm_kernel(const float* __restrict__ dc, const float* __restrict__ e
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const int j = j0 + tx * 4 + c;
-    const float rs = j < nb ? sqrtf(e_ac[((size_t)b * nb + j) * H + h]) : 0.f;
+    const int64_t esrc = j < nb ? meta_src(ms, b, j, h, nb, H) : -1;
+    const float rs = esrc >= 0 ? sqrtf(e_ac[esrc]) : 0.f;
     bm[c] = -INFINITY;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = r0 + ty * 8 + i;
-      if (r < rows && j < nb) {
+      if (r < rows && esrc >= 0) {
         const float bound = acc[i][c] / sqrt_d + (sqrtf(s_nrm[ty * 8 + i]) * rs) / sqrt_d;
         if (bounds) {
           const int s = r / G, g = r - s * G;
@@ -1650,18 +1738,20 @@ meta_bound_gemm_kernel(const float* __restrict__ dc, const float* __restrict__ e
 }
 
 __global__ void meta_bound_gates_kernel(float* bound_max, const float* __restrict__ zeta, int64_t cells, float tau,
-                                        float zeta_max, uint8_t* keep) {
+                                        float zeta_max, uint8_t* keep, int nb, int H, MetaSrc ms) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= cells) return;
   const float bm = key2f(reinterpret_cast<int*>(bound_max)[i]);
   bound_max[i] = bm;
-  if (keep) keep[i] = (bm >= tau && zeta[i] <= zeta_max) ? 1 : 0;
+  const int h = (int)(i % H), j = (int)((i / H) % nb), b = (int)(i / ((int64_t)H * nb));
+  const int64_t src = meta_src(ms, b, j, h, nb, H);
+  if (keep) keep[i] = (src >= 0 && bm >= tau && zeta[src] <= zeta_max) ? 1 : 0;
 }
 
 template <typename T>
 int launch_meta_bound_gemm(const float* dc, const float* e_ac, const float* zeta, const T* q, int B, int nb, int H,
                            int D, int Sq, int Hq, float tau, float zeta_max, float* bound_max, float* bounds,
-                           uint8_t* keep, cudaStream_t st) {
+                           uint8_t* keep, cudaStream_t st, MetaSrc ms) {
   const int64_t cells = (int64_t)B * nb * H;
   const int G = Hq / H;
   const int64_t rows = (int64_t)Sq * G;
@@ -1672,18 +1762,20 @@ int launch_meta_bound_gemm(const float* dc, const float* e_ac, const float* zeta
   int* key = reinterpret_cast<int*>(bound_max);
   meta_bound_init_kernel<<<g1, 256, 0, st>>>(key, cells);
   dim3 grid((unsigned)gx, (unsigned)(B * H), (unsigned)((nb + kMbBlk - 1) / kMbBlk));
-  meta_bound_gemm_kernel<T><<<grid, 256, 0, st>>>(dc, e_ac, q, nb, H, D, Sq, Hq, G, key, bounds);
-  meta_bound_gates_kernel<<<g1, 256, 0, st>>>(bound_max, zeta, cells, tau, zeta_max, keep);
+  meta_bound_gemm_kernel<T><<<grid, 256, 0, st>>>(dc, e_ac, q, nb, H, D, Sq, Hq, G, key, bounds, ms);
+  meta_bound_gates_kernel<<<g1, 256, 0, st>>>(bound_max, zeta, cells, tau, zeta_max, keep, nb, H, ms);
   return check_launch("meta_bound_gemm_kernel");
 }
 
 }  // namespace
 }  // namespace oc
 
-extern "C" int oc_score_from_metadata(const float* dc, const float* e_ac, const float* zeta, const void* q,
-                                      int q_dtype, int batch, int num_blocks, int kv_heads, int head_dim,
-                                      int q_len, int q_heads, float tau, float zeta_max, float* bound_max,
-                                      float* bounds, uint8_t* keep, oc_stream_t stream) {
+namespace oc {
+namespace {
+int score_from_metadata_impl(const float* dc, const float* e_ac, const float* zeta, const void* q, int q_dtype,
+                             int batch, int num_blocks, int kv_heads, int head_dim, int q_len, int q_heads, float tau,
+                             float zeta_max, float* bound_max, float* bounds, uint8_t* keep, MetaSrc ms,
+                             oc_stream_t stream) {
   OC_REQUIRE(dc && e_ac && zeta && q, OC_ERR_NULL, "oc_score_from_metadata: null input");
   OC_REQUIRE(bound_max || bounds || keep, OC_ERR_NULL, "oc_score_from_metadata: no output");
   OC_REQUIRE(batch >= 1 && num_blocks >= 0 && kv_heads >= 1 && head_dim >= 1 && q_len >= 1 &&
@@ -1700,23 +1792,48 @@ extern "C" int oc_score_from_metadata(const float* dc, const float* e_ac, const 
   if ((int64_t)q_len * G > kMetaGemmMinRows && bound_max && head_dim % kMbK == 0) {
     if (q_dtype == OC_F32)
       return launch_meta_bound_gemm<float>(dc, e_ac, zeta, (const float*)q, batch, num_blocks, kv_heads, head_dim,
-                                           q_len, q_heads, tau, zeta_max, bound_max, bounds, keep, st);
+                                           q_len, q_heads, tau, zeta_max, bound_max, bounds, keep, st, ms);
     if (q_dtype == OC_BF16)
       return launch_meta_bound_gemm<__nv_bfloat16>(dc, e_ac, zeta, (const __nv_bfloat16*)q, batch, num_blocks,
                                                    kv_heads, head_dim, q_len, q_heads, tau, zeta_max, bound_max,
-                                                   bounds, keep, st);
+                                                   bounds, keep, st, ms);
   }
   if (q_dtype == OC_F32)
     meta_gates_kernel<float><<<(unsigned)grid, 256, 0, st>>>(dc, e_ac, zeta, (const float*)q, num_blocks, kv_heads,
                                                              head_dim, q_len, q_heads, G, cells, tau, zeta_max,
-                                                             bound_max, bounds, keep);
+                                                             bound_max, bounds, keep, ms);
   else if (q_dtype == OC_BF16)
     meta_gates_kernel<__nv_bfloat16><<<(unsigned)grid, 256, 0, st>>>(
         dc, e_ac, zeta, (const __nv_bfloat16*)q, num_blocks, kv_heads, head_dim, q_len, q_heads, G, cells, tau,
-        zeta_max, bound_max, bounds, keep);
+        zeta_max, bound_max, bounds, keep, ms);
   else
     return set_error(OC_ERR_DTYPE, "oc_score_from_metadata: q dtype %d", q_dtype);
   return check_launch("meta_gates_kernel");
+}
+}  // namespace
+}  // namespace oc
+
+extern "C" int oc_score_from_metadata(const float* dc, const float* e_ac, const float* zeta, const void* q,
+                                      int q_dtype, int batch, int num_blocks, int kv_heads, int head_dim,
+                                      int q_len, int q_heads, float tau, float zeta_max, float* bound_max,
+                                      float* bounds, uint8_t* keep, oc_stream_t stream) {
+  return oc::score_from_metadata_impl(dc, e_ac, zeta, q, q_dtype, batch, num_blocks, kv_heads, head_dim, q_len,
+                                      q_heads, tau, zeta_max, bound_max, bounds, keep, oc::MetaSrc{nullptr, 0, 0},
+                                      stream);
+}
+
+extern "C" int oc_score_from_metadata_paged(const float* dc_pool, const float* e_ac_pool, const float* zeta_pool,
+                                            int num_pages, const int32_t* block_table, int table_stride,
+                                            const void* q, int q_dtype, int batch, int num_blocks, int kv_heads,
+                                            int head_dim, int q_len, int q_heads, float tau, float zeta_max,
+                                            float* bound_max, float* bounds, uint8_t* keep, oc_stream_t stream) {
+  OC_REQUIRE(block_table, OC_ERR_NULL, "oc_score_from_metadata_paged: block_table is NULL");
+  OC_REQUIRE(num_pages >= 1 && table_stride >= num_blocks, OC_ERR_SHAPE,
+             "oc_score_from_metadata_paged: num_pages %d, table_stride %d < num_blocks %d", num_pages, table_stride,
+             num_blocks);
+  return oc::score_from_metadata_impl(dc_pool, e_ac_pool, zeta_pool, q, q_dtype, batch, num_blocks, kv_heads,
+                                      head_dim, q_len, q_heads, tau, zeta_max, bound_max, bounds, keep,
+                                      oc::MetaSrc{block_table, table_stride, num_pages}, stream);
 }
 
 namespace oc {
@@ -1744,6 +1861,11 @@ extern "C" int oc_probe_read_score_stamps(unsigned long long* host, int n) {
 // ---------------------------------------------------------------------------
 namespace oc {
 
+size_t xchg_region_bytes(int P, int NG) {
+  const size_t recv = (size_t)2 * P * NG * kXchgBlock * sizeof(float);
+  return recv + ((size_t)2 * P * NG * sizeof(int) + 255) / 256 * 256;
+}
+
 size_t decode_fused_bytes(int batch, int seq_len, int kv_heads) {
   return fused_layout(batch, seq_len / kBlock, kv_heads).bytes;
 }
@@ -1751,7 +1873,7 @@ size_t decode_fused_bytes(int batch, int seq_len, int kv_heads) {
 int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
                  int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
                  void* out, int out_dtype, float* pm, float* pl, float* po, void* ws, size_t ws_bytes,
-                 cudaStream_t st) {
+                 cudaStream_t st, const PeerXchg* px) {
   if (head_dim != 128 || !q || q_len < 1 || kv_heads < 1 || q_heads % kv_heads) return OC_ERR_UNSUPPORTED;
   const int G = q_heads / kv_heads, R = q_len * G, nb = seq_len / kBlock;
   // Counts share an int32 with 16 bits each (blk_state, the row word): at
@@ -1785,6 +1907,7 @@ int decode_fused(const void* q, const void* k, const void* v, int batch, int q_l
   f.perm = perm; f.count = count;
   f.B = batch; f.NG = L.NG; f.cpg = L.cpg; f.R = R;
   f.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  if (px) f.px = *px;
 
   CUtensorMap km, ak, av;
   const uint64_t cols = (uint64_t)kv_heads * 128, rows = (uint64_t)batch * seq_len;

@@ -349,17 +349,29 @@ def head_partitioned_attention(q, k_shard, v_shard, block_mask, comm, block_size
 
 
 class ShardedDecoder:
-    """Sequence-parallel decode through ``oc_decode_step_sharded``: per layer
-    one fused kernel on this rank's shard, one all-gather of the (m, l, o)
-    partials, one merge.  Holds the zero-filled workspace between calls."""
+    """Sequence-parallel decode through ``oc_decode_step_sharded``.
 
-    def __init__(self, comm, q_heads, kv_heads, head_dim, seq_len, batch=1, q_len=1):
+    ``peer=True`` (default) maps every rank's exchange region into every
+    other rank (``oc_sharded_connect``, collective): each layer is then one
+    fused kernel that merges the shards' (m, l, o) partials over NVLink peer
+    stores.  Otherwise (or if mapping fails on any rank) each layer is the
+    fused kernel, an NCCL all-gather of the partials and a merge kernel.
+    Holds the zero-filled workspace between calls."""
+
+    def __init__(self, comm, q_heads, kv_heads, head_dim, seq_len, batch=1, q_len=1, peer=True):
         self.comm = comm
         self.shape = (batch, q_len, q_heads, kv_heads, head_dim, seq_len)
         dev = comm.device
         self.ws_bytes = _lib.query("oc_decode_step_sharded_workspace_bytes", comm.size, batch, q_len, q_heads,
                                    kv_heads, head_dim, seq_len)
         self.ws = torch.zeros((self.ws_bytes,), dtype=torch.uint8, device=dev)
+        self.peer = False
+        if peer:
+            lib = _lib.load()
+            rc = lib.oc_sharded_connect(comm.ptr, _lib.ptr(self.ws), self.ws_bytes, batch, q_len, q_heads, kv_heads,
+                                        head_dim, seq_len, _lib.stream_ptr(dev))
+            self.peer = rc == 0
+            self.connect_error = None if rc == 0 else lib.oc_last_error().decode(errors="replace")
         nb = seq_len // BLOCK_SIZE
         self.keep = torch.empty((batch, nb, kv_heads), dtype=torch.uint8, device=dev)
         self.perm = torch.empty((batch, nb), dtype=torch.int32, device=dev)
@@ -373,6 +385,11 @@ class ShardedDecoder:
                   _lib.ptr(self.perm), _lib.ptr(self.count), _lib.ptr(self.out), 1, _lib.ptr(self.ws),
                   self.ws_bytes, _lib.stream_ptr(k.device))
         return self.out
+
+    def close(self):
+        if self.peer:
+            _lib.load().oc_sharded_disconnect(_lib.ptr(self.ws))
+            self.peer = False
 
 
 def ici_data_volume(num_blocks_per_device: int, num_devices: int, active_counts, num_heads: int,

@@ -6,19 +6,12 @@ scorer over the keys (the reference transforms the keys up to four times).
 """
 from __future__ import annotations
 
-import math
-import time
-
 import torch
 
 from . import _core, _lib
 from .spectral_energy import score_blocks
 
 _MODES = ("dense", "sparse", "compact")
-
-
-def _sync():
-    torch.cuda.synchronize()
 
 
 def _dense_attention(q, keys, values, head_dim=None):
@@ -43,11 +36,23 @@ def _compute_auto_tau(q, keys, block_size=512):
     return bm.mean() - bm.std(unbiased=False)
 
 
+def _elapsed(e0, e1):
+    """Milliseconds between two recorded CUDA events, read when asked for."""
+    def read():
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+    return read
+
+
 def orthocache_forward(q, keys, values, block_size: int = 512, zeta_max: float = 5.0,
                        tau: float | None = None, mode: str = "compact"):
     """Full pipeline: spectral analysis -> two-gate eviction -> attention (``pipeline.py:33-157``).
 
     Returns (output (Sq, H, D) in q's dtype, metadata dict with the reference's keys).
+    Nothing here waits for the GPU: τ (auto: mean - std of the bounds, on the
+    device), the ζ statistics, the retained counts and the timings (CUDA
+    events) are device values that the metadata dict (``_core.Meta``) reads
+    only when a key is accessed.
     """
     if mode not in _MODES:
         raise ValueError(f"Unknown mode: {mode!r}. Use 'dense', 'sparse', or 'compact'.")
@@ -55,46 +60,47 @@ def orthocache_forward(q, keys, values, block_size: int = 512, zeta_max: float =
     B, S, H, D = k.shape
     Sq = qq.shape[1]
     num_blocks = S // block_size
-    metadata = {
+    metadata = _core.Meta({
         "mode": mode, "seq_len_q": Sq, "seq_len_k": S, "num_blocks": num_blocks,
         "num_heads": H, "head_dim": D, "block_size": block_size, "zeta_max": zeta_max,
-    }
+    })
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
     if mode == "dense":
-        t0 = time.perf_counter()
         out = _dense_attention(qq, k, v, D)
-        _sync()
-        metadata["latency_ms"] = (time.perf_counter() - t0) * 1000
+        ev[1].record()
+        metadata["latency_ms"] = _elapsed(ev[0], ev[1])
         metadata["eviction_rate"] = 0.0
         return (out if batched else out[0]), metadata
 
-    t_spec = time.perf_counter()
     sc = score_blocks(k, qq, block_size=block_size, want=("zeta", "bound_max"))
     zeta, bmax = sc["zeta"], sc["bound_max"]
     if tau is None:
         tau_dev = (bmax.mean() - bmax.std(unbiased=False)).reshape(1).float()
-        tau = float(tau_dev.item())
+        metadata["tau"] = tau_dev.reshape(())
         metadata["tau_auto"] = True
+        tau_host = 0.0  # unused: the gates read tau_dev
     else:
         tau_dev = None
+        tau_host = float(tau)
+        metadata["tau"] = tau_host
         metadata["tau_auto"] = False
-    metadata["tau"] = tau
     keep = torch.empty(bmax.shape, dtype=torch.uint8, device=k.device)
     _lib.call("oc_apply_gates", _lib.ptr(bmax), _lib.ptr(zeta), bmax.numel(), _lib.ptr(tau_dev),
-              float(tau), float(zeta_max), _lib.ptr(keep), _lib.stream_ptr(k.device))
-    _sync()
-    metadata["spectral_ms"] = (time.perf_counter() - t_spec) * 1000
+              tau_host, float(zeta_max), _lib.ptr(keep), _lib.stream_ptr(k.device))
+    ev[1].record()
+    metadata["spectral_ms"] = _elapsed(ev[0], ev[1])
 
     z = zeta.mean(dim=-1)  # mean over heads, per block (pipeline.py:123)
-    metadata["zeta_mean"] = float(z.mean())
-    metadata["zeta_std"] = float(z.std(unbiased=False))
-    metadata["zeta_min"] = float(z.min())
-    metadata["zeta_max_observed"] = float(z.max())
+    metadata["zeta_mean"] = z.mean()
+    metadata["zeta_std"] = z.std(unbiased=False)
+    metadata["zeta_min"] = z.min()
+    metadata["zeta_max_observed"] = z.max()
 
-    t_attn = time.perf_counter()
     if mode == "compact":
         perm, count = _core.compact(keep, batched=True)
         out = _core.attend(qq, k, v, perm, count, block_size)
-        retained = int(count.sum().item()) if batched else int(count[0].item())
+        retained = count.sum()
         metadata["compact_num_active"] = retained
     else:  # sparse: per-head masks
         perm, count = _core.compact_per_head(keep)
@@ -102,12 +108,12 @@ def orthocache_forward(q, keys, values, block_size: int = 512, zeta_max: float =
                            idx_head_stride=num_blocks, count_stride=H, count_head_stride=1)
         _core.fill_empty_heads(out, v, count, H, 1)
         un, uc = _core.compact(keep, batched=True)
-        retained = int(uc.sum().item()) if batched else int(uc[0].item())
-    _sync()
+        retained = uc.sum()
+    ev[2].record()
+    total = num_blocks * B
     metadata["blocks_retained"] = retained
-    metadata["blocks_evicted"] = num_blocks * B - retained
-    metadata["eviction_rate"] = 1.0 - retained / (num_blocks * B) if num_blocks else 0.0
-    t_end = time.perf_counter()
-    metadata["attention_ms"] = (t_end - t_attn) * 1000
-    metadata["total_ms"] = (t_end - t_spec) * 1000
+    metadata["blocks_evicted"] = lambda: total - int(retained.item())
+    metadata["eviction_rate"] = lambda: (1.0 - int(retained.item()) / total) if total else 0.0
+    metadata["attention_ms"] = _elapsed(ev[1], ev[2])
+    metadata["total_ms"] = _elapsed(ev[0], ev[2])
     return (out if batched else out[0]), metadata

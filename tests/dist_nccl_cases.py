@@ -8,11 +8,12 @@ check what it received against the oracle without further communication:
     oracle's, the valid-slot order is the oracle's;
   * oc_alltoallv_heads: this rank's KV heads of every rank's retained blocks,
     bit-exact, in rank order;
-  * attention over the union of all shards' retained blocks, three ways —
+  * attention over the union of all shards' retained blocks, four ways —
     the stratified exchange + indirect attention, the head-partitioned
     AllToAllv + attention + output all-gather, and the fused sharded decode
-    layer (oc_decode_step_sharded: per-shard partials + NCCL all-gather + log-
-    sum-exp merge) — each against the oracle's attention over the
+    layer (oc_decode_step_sharded) with its partials exchanged by an NCCL
+    all-gather and by NVLink peer stores inside the one kernel (also as a
+    replayed CUDA graph) — each against the oracle's attention over the
     concatenated shards (1e-2 relative / 2e-2 absolute, bf16).
 Writes ok<rank> into the result directory when every check passed.
 """
@@ -131,16 +132,37 @@ def main():
             out_h = ocd.head_partitioned_attention(q, k_me, v_me, keep_me, comm)
             np.testing.assert_allclose(out_h.float().cpu().numpy(), want_out, rtol=RTOL, atol=ATOL)
 
-        # -- fused sharded decode layer (partials + NCCL all-gather + merge) --------
-        dec = ocd.ShardedDecoder(comm, HQ, HKV, D, NB * BS)
-        for _ in range(3):  # repeated calls reuse the workspace's counter sets
-            out_d = dec(q, k_me, v_me, -float("inf"), ZETA_MAX)
-        torch.cuda.synchronize()
-        np.testing.assert_allclose(out_d[0].float().cpu().numpy(), want_out, rtol=RTOL, atol=ATOL)
-        assert int(dec.count[0]) == counts[rank]
-        assert np.array_equal(dec.perm[0].cpu().numpy(), perms[rank])
+        # -- fused sharded decode layer: NCCL all-gather of the partials, then
+        #    the one-kernel form that merges them over NVLink peer stores -------
         from orthocache_b200 import _lib
-        assert _lib.load().oc_device_status(1) == 0
+        for peer in (False, True):
+            dec = ocd.ShardedDecoder(comm, HQ, HKV, D, NB * BS, peer=peer)
+            if peer:
+                assert dec.peer, dec.connect_error
+            dist.barrier()
+            for _ in range(3):  # repeated calls reuse the workspace's counter sets and exchange slots
+                out_d = dec(q, k_me, v_me, -float("inf"), ZETA_MAX)
+            torch.cuda.synchronize()
+            np.testing.assert_allclose(out_d[0].float().cpu().numpy(), want_out, rtol=RTOL, atol=ATOL)
+            assert int(dec.count[0]) == counts[rank]
+            assert np.array_equal(dec.perm[0].cpu().numpy(), perms[rank])
+            assert _lib.load().oc_device_status(1) == 0, f"bounded wait gave up (peer={peer})"
+            if peer:
+                # the one-kernel step captured in a CUDA graph and replayed
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=side):
+                    dec(q, k_me, v_me, -float("inf"), ZETA_MAX)
+                    dec(q, k_me, v_me, -float("inf"), ZETA_MAX)
+                dist.barrier()
+                for _ in range(3):
+                    dec.out.zero_()
+                    g.replay()
+                torch.cuda.synchronize()
+                np.testing.assert_allclose(dec.out[0].float().cpu().numpy(), want_out, rtol=RTOL, atol=ATOL)
+                assert _lib.load().oc_device_status(1) == 0, "bounded wait gave up in the graph replay"
+            dec.close()
 
         comm.check()
         dist.barrier()

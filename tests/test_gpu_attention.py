@@ -150,7 +150,13 @@ def test_orthocache_forward_modes():   # test_pipeline.py / test_compaction.py:2
                                rtol=2e-4, atol=2e-4)
     assert meta["mode"] == "dense" and meta["eviction_rate"] == 0.0
     for mode in ("sparse", "compact"):
-        out, meta = oc.orthocache_forward(dev(q), dev(k), dev(v), zeta_max=100.0, mode=mode)
+        qd, kd, vd = dev(q), dev(k), dev(v)
+        torch.cuda.synchronize()
+        torch.cuda.set_sync_debug_mode("error")  # the call itself never waits for the GPU
+        try:
+            out, meta = oc.orthocache_forward(qd, kd, vd, zeta_max=100.0, mode=mode)
+        finally:
+            torch.cuda.set_sync_debug_mode(0)
         tau = O.auto_tau(q, k)
         assert abs(meta["tau"] - tau) < 1e-4 * max(1, abs(tau))
         keep = O.multiband_mask(q, k, meta["tau"], 100.0)

@@ -175,3 +175,23 @@ def test_bounds_from_write_time_metadata_match_reference():  # test_energy.py:33
     dc, e_ac, _ = O.block_metadata(X["bounds_keys"])
     np.testing.assert_allclose(O.bounds_from_metadata(X["bounds_q"], dc, e_ac), GOLD["bounds"],
                                rtol=1e-5, atol=1e-5)
+
+
+def test_partial_states_merge_to_the_union_attention():
+    """Splitting the retained blocks over shards and merging the shards'
+    (m, l, o) in log-sum-exp form gives the attention over the union
+    (distributed_attention.py:95-128 applied across shards)."""
+    rs = np.random.RandomState(7)
+    q = rs.randn(2, 8, 16) * 0.5
+    shards = [(rs.randn(4 * 8, 2, 16), rs.randn(4 * 8, 2, 16)) for _ in range(3)]
+    perms = [np.array([2, 0, 1, 3]), np.array([1, 3, 0, 2]), np.array([0, 1, 2, 3])]
+    counts = [2, 0, 3]
+    parts = [O.partial_attention(q, k, v, p, n, block_size=8) for (k, v), p, n in zip(shards, perms, counts)]
+    got = O.merge_partials(parts)
+    k_all = np.concatenate([k for k, _ in shards])
+    v_all = np.concatenate([v for _, v in shards])
+    gperm = np.concatenate([p[:n] + 4 * i for i, (p, n) in enumerate(zip(perms, counts))])
+    want = O.indirect_attention(q, k_all, v_all, gperm, len(gperm), block_size=8)
+    np.testing.assert_allclose(got, want, rtol=1e-6, atol=1e-6)
+    empty = O.merge_partials([O.partial_attention(q, *shards[1], perms[1], 0, block_size=8)])
+    assert np.all(empty == 0)
