@@ -531,6 +531,72 @@ __device__ __forceinline__ void fused_write_perm(const int* st, int nb, int32_t*
   }
 }
 
+// The cross-GPU half of the fused layer's group merge (FusedArgs::px): kept
+// out of line so that the single-GPU kernel's register allocation does not
+// pay for it.  Publish: every thread's stores of this shard's partial reached
+// the peers before the flag (system-scope fence, then the barrier, then a
+// release store), and the flag carries the call number, so slots are reused
+// every other call without clearing.  Then wait (bounded) for every rank's
+// flag of this call and merge the P partials of the group: out on every rank.
+struct PeerMergeArgs {
+  PeerXchg px;
+  int NG, R, G, Sq, Hq, out_bf16;
+  void* out;
+};
+
+__device__ __noinline__ void fused_peer_merge(const PeerMergeArgs pa, int grp, int bq, int hq, int seq, int tid,
+                                              volatile int* abort_flag) {
+  constexpr int D = 128;
+  const PeerXchg& px = pa.px;
+  const int lane = tid & 31;
+  __threadfence_system();
+  asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+  const int par = seq & 1, flag = seq + 1;
+  if (tid < px.P) {
+    int* fl = reinterpret_cast<int*>(px.bases[tid] + px.flag_off) +
+              ((size_t)par * px.P + px.rank) * pa.NG + grp;
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl), "r"(flag) : "memory");
+  }
+  if (tid < 32) {
+    const int* mine = reinterpret_cast<const int*>(px.bases[px.rank] + px.flag_off) +
+                      (size_t)par * px.P * pa.NG + grp;
+    const uint64_t t0 = globaltimer_ns();
+    for (int src = lane; src < px.P; src += 32) {
+      int v;
+      for (;;) {
+        asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + (size_t)src * pa.NG) : "memory");
+        if (v == flag) break;
+        if (globaltimer_ns() - t0 > g_wait_limit_ns) { *abort_flag = 1; atomicExch(&g_score_status, 1); break; }
+        __nanosleep(64);
+      }
+    }
+    __syncwarp();
+  }
+  asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+  if (!*abort_flag) {
+    const float* base = reinterpret_cast<const float*>(px.bases[px.rank]);
+    for (int x = tid; x < pa.R * D; x += kScoreThreads) {
+      const int r = x / D, d = x - r * D;
+      float M = -INFINITY;
+      for (int src = 0; src < px.P; ++src)
+        M = fmaxf(M, __ldcv(base + ((size_t)(par * px.P + src) * pa.NG + grp) * kXchgBlock + r));
+      float L = 0.f, O = 0.f;
+      if (M != -INFINITY)
+        for (int src = 0; src < px.P; ++src) {
+          const float* blk = base + ((size_t)(par * px.P + src) * pa.NG + grp) * kXchgBlock;
+          const float w = exp2f(__ldcv(blk + r) - M);
+          L = fmaf(__ldcv(blk + 8 + r), w, L);
+          O = fmaf(__ldcv(blk + 16 + r * D + d), w, O);
+        }
+      const int s = r / pa.G, gq = r - s * pa.G;
+      const size_t orow = ((size_t)bq * pa.Sq + s) * pa.Hq + (size_t)hq * pa.G + gq;
+      const float y = L > 0.f ? O / L : 0.f;
+      if (pa.out_bf16) reinterpret_cast<__nv_bfloat16*>(pa.out)[orow * D + d] = __float2bfloat16_rn(y);
+      else reinterpret_cast<float*>(pa.out)[orow * D + d] = y;
+    }
+  }
+}
+
 template <int D, bool FUSED>
 __global__ void __launch_bounds__(kFusedThreads, 1)
 score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap amap_k,
@@ -830,7 +896,12 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
           // queue entry is all that is needed from its publisher (keys and
           // values are inputs), so relaxed loads poll it; the end-of-queue
           // test acquires the row word.
-          int w = atomicAdd(fs.grp_ctr + grp, 1);
+          // Units are claimed in pairs (one atomic and one queue look per two
+          // 128-token chunks of the same block: kUnitClaim divides CPB).
+          constexpr int kUnitClaim = 2;
+          static_assert(CPB % kUnitClaim == 0, "a claim stays within one block");
+          int w = atomicAdd(fs.grp_ctr + grp, kUnitClaim);
+          int w_end = w + kUnitClaim;
           int vq = w / CPB < a.nb ? ld_relaxed(qb + w / CPB) : 0;
           OC_SSTAMP(9, 0);
           for (int k = n_units;; ++k) {
@@ -874,8 +945,13 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
               tma_load_2d(dst + jb * (kFusedChunk * 128), &amap_k, &full[s], h * D + jb * 64, y);
               tma_load_2d(dst + kSlabB / 2 + jb * (kFusedChunk * 128), &amap_v, &full[s], h * D + jb * 64, y);
             }
-            w = atomicAdd(fs.grp_ctr + grp, 1);
-            vq = w / CPB < a.nb ? ld_relaxed(qb + w / CPB) : 0;
+            if (++w == w_end) {
+              w = atomicAdd(fs.grp_ctr + grp, kUnitClaim);
+              w_end = w + kUnitClaim;
+              vq = w / CPB < a.nb ? ld_relaxed(qb + w / CPB) : 0;
+            } else {
+              vq = desc / CPB + 1;  // the same block: its queue entry is known
+            }
           }
         }
       }
@@ -1208,57 +1284,11 @@ scored:
       }
     }
     if (f.px.P > 0 && s_merge) {
-      // Publish: every thread's stores reach the peers before the flag
-      // (system-scope fence, then the barrier, then a release store), and
-      // the flag carries the call number, so slots are reused every other
-      // call without clearing.  Then wait (bounded) for every rank's flag of
-      // this call and merge the P partials of the group: out on every rank.
-      __threadfence_system();
-      asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
-      const int par = s_seq & 1, flag = s_seq + 1;
-      if (tid < f.px.P) {
-        int* fl = reinterpret_cast<int*>(f.px.bases[tid] + f.px.flag_off) +
-                  ((size_t)par * f.px.P + f.px.rank) * f.NG + grp;
-        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl), "r"(flag) : "memory");
-      }
-      if (tid < 32) {
-        const int* mine = reinterpret_cast<const int*>(f.px.bases[f.px.rank] + f.px.flag_off) +
-                          (size_t)par * f.px.P * f.NG + grp;
-        const uint64_t t0 = globaltimer_ns();
-        for (int src = lane; src < f.px.P; src += 32) {
-          int v;
-          for (;;) {
-            asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + (size_t)src * f.NG) : "memory");
-            if (v == flag) break;
-            if (globaltimer_ns() - t0 > g_wait_limit_ns) { s_abort = 1; atomicExch(&g_score_status, 1); break; }
-            __nanosleep(64);
-          }
-        }
-        __syncwarp();
-      }
-      asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
-      if (!s_abort) {
-        const float* base = reinterpret_cast<const float*>(f.px.bases[f.px.rank]);
-        for (int x = tid; x < f.R * D; x += kScoreThreads) {
-          const int r = x / D, d = x - r * D;
-          float M = -INFINITY;
-          for (int src = 0; src < f.px.P; ++src)
-            M = fmaxf(M, __ldcv(base + ((size_t)(par * f.px.P + src) * f.NG + grp) * kXchgBlock + r));
-          float L = 0.f, O = 0.f;
-          if (M != -INFINITY)
-            for (int src = 0; src < f.px.P; ++src) {
-              const float* blk = base + ((size_t)(par * f.px.P + src) * f.NG + grp) * kXchgBlock;
-              const float w = exp2f(__ldcv(blk + r) - M);
-              L = fmaf(__ldcv(blk + 8 + r), w, L);
-              O = fmaf(__ldcv(blk + 16 + r * D + d), w, O);
-            }
-          const int s = r / a.G, gq = r - s * a.G;
-          const size_t orow = ((size_t)bq * a.Sq + s) * a.Hq + (size_t)hq * a.G + gq;
-          const float y = L > 0.f ? O / L : 0.f;
-          if (f.out_bf16) reinterpret_cast<__nv_bfloat16*>(f.out)[orow * D + d] = __float2bfloat16_rn(y);
-          else reinterpret_cast<float*>(f.out)[orow * D + d] = y;
-        }
-      }
+      PeerMergeArgs pa;
+      pa.px = f.px;
+      pa.NG = f.NG; pa.R = f.R; pa.G = a.G; pa.Sq = a.Sq; pa.Hq = a.Hq;
+      pa.out = f.out; pa.out_bf16 = f.out_bf16;
+      fused_peer_merge(pa, grp, bq, hq, s_seq, tid, &s_abort);
     }
     if (tid == 0) OC_SSTAMP(14, globaltimer_ns());
   }
