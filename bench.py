@@ -61,6 +61,10 @@ def parse():
     p.add_argument("--evict", type=float, default=0.75)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="N > 1: skip the oracle check of the merged output")
+    p.add_argument("--no-peer", action="store_true",
+                   help="N > 1: exchange the partials through NCCL instead of peer stores in the kernel")
+    p.add_argument("--uniform-evict", action="store_true",
+                   help="N > 1: every shard at --evict instead of configuration 3's U[0.6, 0.9] (diagnostic)")
     p.add_argument("--config", type=int, choices=[1, 2, 4], default=1,
                    help="1: decode layer (the headline metric); 2: chunked prefill on the tensor cores; "
                         "4: the 60-layer decode stack (sliding-window + global layers, D 256)")
@@ -139,7 +143,7 @@ class Layer:
     pass
 
 
-def make_layers(rank, evict, device, world=1):
+def make_layers(rank, evict, device, world=1, uniform=False):
     import torch
     from orthocache_b200 import synthetic as syn, score_blocks
     nb = S_SHARD // 512
@@ -149,7 +153,7 @@ def make_layers(rank, evict, device, world=1):
         seed = 1000 * rank + l
         L = Layer()
         # configuration 3: uneven per-shard eviction, uniform in 60-90 %
-        L.evict = evict if world == 1 else random.Random(seed).uniform(0.6, 0.9)
+        L.evict = evict if (world == 1 or uniform) else random.Random(seed).uniform(0.6, 0.9)
         L.kinds = syn.block_kinds(nb, L.evict, seed=seed)
         L.k = syn.make_keys(nb, HKV, D, L.kinds, seed=seed, device=device)
         L.v = syn.make_values(S_SHARD, HKV, D, seed=seed, device=device)
@@ -165,7 +169,7 @@ def make_layers(rank, evict, device, world=1):
 class Engine:
     """Device buffers and the C-ABI calls of one decode layer."""
 
-    def __init__(self, layers, device, world):
+    def __init__(self, layers, device, world, peer=True):
         import torch
         from orthocache_b200 import _lib
         self.torch, self.lib, self.layers, self.world = torch, _lib, layers, world
@@ -193,7 +197,7 @@ class Engine:
             from orthocache_b200.comm import NcclComm
             from orthocache_b200.distributed import ShardedDecoder
             self.comm = NcclComm(device=device)
-            self.dec = ShardedDecoder(self.comm, HQ, HKV, D, S_SHARD, peer=True)
+            self.dec = ShardedDecoder(self.comm, HQ, HKV, D, S_SHARD, peer=peer)
             self.keep, self.perm, self.count, self.out = self.dec.keep[0], self.dec.perm[0], self.dec.count, \
                 self.dec.out
             self.launches_per_step = 1 if self.dec.peer else 2
@@ -210,12 +214,24 @@ class Engine:
                 None, None, None, None, None, None, None, _l.ptr(self.keep), 0, self.stream)
 
     def decode(self, L, q=None):
-        """One layer through the one-call C ABI (score -> compact -> attend)."""
-        _l = self.lib
+        """One layer through the one-call C ABI (score -> compact -> attend).
+        The call's arguments (device pointers, sizes) are built once per
+        (layer, query buffer) and reused, as a serving loop would."""
         q = L.q if q is None else q
-        _l.call("oc_decode_step", _l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, 1, 1, HQ, HKV, D, S_SHARD, L.tau, ZETA_MAX,
-                _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(self.out), 1,
-                _l.ptr(self.ws), self.ws_bytes, self.stream)
+        key = (id(L), q.data_ptr(), self.stream)
+        args = self._args.get(key) if hasattr(self, "_args") else None
+        if args is None:
+            _l = self.lib
+            args = (_l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, 1, 1, HQ, HKV, D, S_SHARD, L.tau, ZETA_MAX,
+                    _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(self.out), 1,
+                    _l.ptr(self.ws), self.ws_bytes, self.stream)
+            if not hasattr(self, "_args"):
+                self._args = {}
+                self._fn = self.lib.load().oc_decode_step
+            self._args[key] = args
+        rc = self._fn(*args)
+        if rc != 0:
+            raise RuntimeError(self.lib.load().oc_last_error().decode())
 
     def decode_sharded(self, L, q=None):
         """One layer of sequence-parallel decode through oc_decode_step_sharded."""
@@ -407,8 +423,8 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    layers = make_layers(rank, args.evict, device, world)
-    eng = Engine(layers, device, world)
+    layers = make_layers(rank, args.evict, device, world, args.uniform_evict)
+    eng = Engine(layers, device, world, peer=not args.no_peer)
     nb = S_SHARD // 512
 
     def barrier():
@@ -515,7 +531,7 @@ def run_ours(args, rank, world, local_rank):
     from orthocache_b200 import _lib  # noqa: F401
     q_host = [L.q.cpu().pin_memory() for L in layers]
     q_dev = torch.empty_like(layers[0].q)
-    out_host = torch.empty((1, HQ, D), dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty(tuple(eng.out.shape), dtype=torch.bfloat16).pin_memory()
     cnt_host = torch.empty((1,), dtype=torch.int32).pin_memory()
     Ke = max(8, min(K, 2000))
     for s in range(4):
@@ -531,7 +547,6 @@ def run_ours(args, rank, world, local_rank):
         q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
         eng.step(L, q_dev)
         out_host.copy_(eng.out, non_blocking=True)
-        cnt_host.copy_(eng.count, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / Ke
@@ -540,6 +555,7 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     # correctness guard on the last step: retained count matches the calibration
+    cnt_host.copy_(eng.count)
     assert int(cnt_host[0]) == layers[(Ke - 1) % LAYERS].kept, "retained block count changed"
 
     k_bytes = S_SHARD * HKV * D * 2
@@ -604,9 +620,9 @@ def run_ours(args, rank, world, local_rank):
         "parity": parity,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": UNIT, "h2d_bytes_per_step": HQ * D * 2,
-                "d2h_bytes_per_step": HQ * D * 2 + 4,
-                "note": "public C-ABI calls per step; q copied from pinned host, output + count read back; "
-                        "KV cache resident in HBM as in decode"},
+                "d2h_bytes_per_step": HQ * D * 2,
+                "note": "public C-ABI call per step, eager; the query copied from pinned host memory, the "
+                        "attention output read back; KV cache resident in HBM as in decode"},
         "gpu_launches": K * eng.launches_per_step,
         "clocks": clk.summary(),
         "retained_blocks": kept,

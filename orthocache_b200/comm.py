@@ -83,7 +83,7 @@ class NcclComm:
 
     def close(self):
         if self._stop is not None:
-            self._stop()
+            self._stop.set()
         if self.ptr:
             _lib.load().oc_comm_destroy(self.ptr)
             self.ptr = None

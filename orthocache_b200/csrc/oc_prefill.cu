@@ -316,12 +316,17 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
       // in registers for its exponentials, the second is read again.
       float s[64];
       tmem_ld64_wait(t_s + 64, s);
-      float mx = s[0];
+      // Eight independent running maxima (a single chain of 128 dependent
+      // max operations would sit on the critical path of every K/V tile).
+      float m8[8];
 #pragma unroll
-      for (int i = 1; i < 64; ++i) mx = fmaxf(mx, s[i]);
+      for (int i = 0; i < 8; ++i) m8[i] = s[i];
+#pragma unroll
+      for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
       tmem_ld64_wait(t_s, s);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mx = fmaxf(mx, s[i]);
+      for (int i = 0; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= a.scale_log2;
       const bool need = mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, need)) {
@@ -346,7 +351,7 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
       // registers; tokens 64-127 to columns 32-63, after their logits (columns
       // 64-127, untouched so far) have been read.  One chunk of 8 in 4 takes
       // its exponentials on the FMA pipe.
-      float rs = 0.f;
+      float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums, as for the max
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         if (half == 1) tmem_ld64_wait(t_s + 64, s);
@@ -358,7 +363,7 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
           for (int i = 0; i < 8; ++i) {
             const float x = fmaf(s[8 * c + i], a.scale_log2, -m_used);
             p[i] = (c & 3) == 3 ? poly_ex2(x) : fast_ex2(x);
-            rs += p[i];
+            r8[i] += p[i];
           }
 #pragma unroll
           for (int i = 0; i < 4; ++i) pk[4 * c + i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
@@ -366,7 +371,7 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
         tmem_st32u(t_s + 32 * half, pk);
       }
       tc_wait_st();  // P and any rescaled O are in tensor memory
-      l += rs;
+      l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       tc_fence_before();
       mbar_arrive(&sm.p_full[t]);
     }

@@ -533,11 +533,11 @@ __device__ __forceinline__ void fused_write_perm(const int* st, int nb, int32_t*
 
 // The cross-GPU half of the fused layer's group merge (FusedArgs::px): kept
 // out of line so that the single-GPU kernel's register allocation does not
-// pay for it.  Publish: every thread's stores of this shard's partial reached
-// the peers before the flag (system-scope fence, then the barrier, then a
-// release store), and the flag carries the call number, so slots are reused
-// every other call without clearing.  Then wait (bounded) for every rank's
-// flag of this call and merge the P partials of the group: out on every rank.
+// pay for it.  The calling CTA has stored this shard's partial of the group
+// into every rank's slot; here it publishes a flag carrying the call number
+// (slots are reused every other call without clearing), waits (bounded) for
+// every rank's flag of this call and merges the P partials of the group:
+// out on every rank.
 struct PeerMergeArgs {
   PeerXchg px;
   int NG, R, G, Sq, Hq, out_bf16;
@@ -549,13 +549,19 @@ __device__ __noinline__ void fused_peer_merge(const PeerMergeArgs pa, int grp, i
   constexpr int D = 128;
   const PeerXchg& px = pa.px;
   const int lane = tid & 31;
-  __threadfence_system();
+  // Publish (the pattern of a grid barrier, at system scope): the CTA
+  // barrier orders every thread's peer stores before thread 0, whose one
+  // system-scope fence and release stores of the flags make them visible to
+  // the peers before the flags.  (A fence in every thread would serialise
+  // 512 system-scope fences.)
   asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
   const int par = seq & 1, flag = seq + 1;
-  if (tid < px.P) {
-    int* fl = reinterpret_cast<int*>(px.bases[tid] + px.flag_off) +
-              ((size_t)par * px.P + px.rank) * pa.NG + grp;
-    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl), "r"(flag) : "memory");
+  if (tid == 0) {
+    __threadfence_system();
+    for (int p = 0; p < px.P; ++p) {
+      int* fl = reinterpret_cast<int*>(px.bases[p] + px.flag_off) + ((size_t)par * px.P + px.rank) * pa.NG + grp;
+      asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl), "r"(flag) : "memory");
+    }
   }
   if (tid < 32) {
     const int* mine = reinterpret_cast<const int*>(px.bases[px.rank] + px.flag_off) +
