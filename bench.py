@@ -61,6 +61,8 @@ def parse():
     p.add_argument("--evict", type=float, default=0.75)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true", help="N > 1: skip the oracle check of the merged output")
+    p.add_argument("--no-variants", action="store_true",
+                   help="N > 1: skip timing the block-exchange variants (stratified all-gather, AllToAllv)")
     p.add_argument("--no-peer", action="store_true",
                    help="N > 1: exchange the partials through NCCL instead of peer stores in the kernel")
     p.add_argument("--uniform-evict", action="store_true",
@@ -213,17 +215,19 @@ class Engine:
                 1, 64, 64, 256, 256, 512, L.tau, ZETA_MAX,
                 None, None, None, None, None, None, None, _l.ptr(self.keep), 0, self.stream)
 
-    def decode(self, L, q=None):
+    def decode(self, L, q=None, out=None):
         """One layer through the one-call C ABI (score -> compact -> attend).
         The call's arguments (device pointers, sizes) are built once per
-        (layer, query buffer) and reused, as a serving loop would."""
+        (layer, query buffer, output buffer) and reused, as a serving loop
+        would."""
         q = L.q if q is None else q
-        key = (id(L), q.data_ptr(), self.stream)
+        out = self.out if out is None else out
+        key = (id(L), q.data_ptr(), out.data_ptr(), self.stream)
         args = self._args.get(key) if hasattr(self, "_args") else None
         if args is None:
             _l = self.lib
             args = (_l.ptr(q), _l.ptr(L.k), _l.ptr(L.v), 1, 1, 1, HQ, HKV, D, S_SHARD, L.tau, ZETA_MAX,
-                    _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(self.out), 1,
+                    _l.ptr(self.keep), _l.ptr(self.perm), _l.ptr(self.count), _l.ptr(out), 1,
                     _l.ptr(self.ws), self.ws_bytes, self.stream)
             if not hasattr(self, "_args"):
                 self._args = {}
@@ -384,6 +388,166 @@ def warmup_steps(step, min_steps, min_seconds, world, sync, device):
                 return i
 
 
+def e2e_pipelined(eng, layers, q_host, Ke):
+    """End to end through the public C ABI with host buffers, N = 1: every
+    step copies its query from pinned host memory and reads its output back,
+    on a copy stream, double-buffered so that the copies of steps i+1 and i
+    overlap step i+1's kernel (what a serving loop does).  Returns ms per
+    step (CUDA events on the compute stream, after every copy)."""
+    import torch
+    cs = torch.cuda.current_stream()
+    xs = torch.cuda.Stream()
+    q_dev = [torch.empty_like(layers[0].q) for _ in range(2)]
+    outs = [torch.empty_like(eng.out) for _ in range(2)]
+    out_host = [torch.empty(tuple(eng.out.shape), dtype=eng.out.dtype).pin_memory() for _ in range(2)]
+    ev = lambda: torch.cuda.Event()
+    ev_q, ev_k, ev_o = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+
+    def run(n):
+        with torch.cuda.stream(xs):
+            q_dev[0].copy_(q_host[0], non_blocking=True)
+            ev_q[0].record(xs)
+        for s in range(n):
+            b = s & 1
+            cs.wait_event(ev_q[b])
+            if s >= 2:
+                cs.wait_event(ev_o[b])  # step s-2's output has left outs[b]
+            eng.decode(layers[s % LAYERS], q_dev[b], outs[b])
+            ev_k[b].record(cs)
+            with torch.cuda.stream(xs):
+                if s + 1 < n:
+                    if s >= 1:
+                        xs.wait_event(ev_k[b ^ 1])  # step s-1's kernel has read q_dev[b ^ 1]
+                    q_dev[b ^ 1].copy_(q_host[(s + 1) % LAYERS], non_blocking=True)
+                    ev_q[b ^ 1].record(xs)
+                xs.wait_event(ev_k[b])
+                out_host[b].copy_(outs[b], non_blocking=True)
+                ev_o[b].record(xs)
+        cs.wait_stream(xs)
+
+    run(8)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cs)
+    run(Ke)
+    e1.record(cs)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / Ke
+
+
+def metadata_decode_time(eng, layers, K):
+    """Decode layers over write-time metadata: the average layer time in a
+    CUDA-graph replay of LAYERS layers and its roofline."""
+    import torch
+    from orthocache_b200 import _lib
+    nb = S_SHARD // 512
+    dev = layers[0].k.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    st = lambda: torch.cuda.current_stream().cuda_stream
+    for L in layers:
+        L.m_dc = torch.empty((nb, HKV, D), **f32)
+        L.m_eac = torch.empty((nb, HKV), **f32)
+        L.m_zeta = torch.empty((nb, HKV), **f32)
+        _lib.call("oc_block_metadata", _lib.ptr(L.k), 1, 1, S_SHARD, HKV, D, _lib.ptr(L.m_dc), _lib.ptr(L.m_eac),
+                  _lib.ptr(L.m_zeta), st())
+    bmax = torch.empty((nb, HKV), **f32)
+    keep = torch.empty((nb, HKV), dtype=torch.uint8, device=dev)
+    perm = torch.empty((nb,), dtype=torch.int32, device=dev)
+    count = torch.empty((1,), dtype=torch.int32, device=dev)
+    out = torch.empty((1, HQ, D), dtype=torch.bfloat16, device=dev)
+    ws_bytes = _lib.query("oc_indirect_attention_workspace_bytes", 1, 1, HQ, HKV, D, 512, nb)
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+
+    def layer(L):
+        _lib.call("oc_score_from_metadata", _lib.ptr(L.m_dc), _lib.ptr(L.m_eac), _lib.ptr(L.m_zeta), _lib.ptr(L.q),
+                  1, 1, nb, HKV, D, 1, HQ, L.tau, ZETA_MAX, _lib.ptr(bmax), None, _lib.ptr(keep), st())
+        _lib.call("oc_stream_compact", _lib.ptr(keep), 1, nb, HKV, _lib.ptr(perm), _lib.ptr(count), st())
+        _lib.call("oc_indirect_attention", _lib.ptr(L.q), _lib.ptr(L.k), _lib.ptr(L.v), 1, _lib.ptr(perm), nb, 0,
+                  _lib.ptr(count), 1, 0, 1, 1, HQ, HKV, D, S_SHARD, 512, nb, _lib.ptr(out), 1, _lib.ptr(ws),
+                  ws_bytes, st())
+
+    for L in layers:
+        layer(L)
+    torch.cuda.synchronize()
+    assert int(count[0]) == layers[-1].kept, "metadata path: retained count differs from the calibration"
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        for L in layers:
+            layer(L)
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for L in layers:
+            layer(L)
+    g.replay()
+    reps = max(8, min(K, 2000) // LAYERS)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / (reps * LAYERS) * 1e3
+    k_bytes = S_SHARD * HKV * D * 2
+    kept = statistics.mean(L.kept for L in layers)
+    alg = kept / nb * 2 * k_bytes + nb * HKV * (D + 2) * 4 + HQ * D * 2 * 2
+    hbm, kind = peaks()
+    return {"us_per_layer": round(us, 3), "alg_bytes": int(alg),
+            "achieved_gbs": round(alg / (us * 1e-6) / 1e9, 1), "frac": round(alg / (us * 1e-6) / 1e9 / hbm, 4),
+            "kernels": "oc_score_from_metadata + oc_stream_compact + oc_indirect_attention (3 per layer)",
+            "how": "average layer in a CUDA-graph replay of %d layers; metadata written once per block "
+                   "(write time, not timed); bytes = metadata + retained K and V + q / out" % LAYERS}
+
+
+def exchange_variants(eng, L, world, device, reps=20):
+    """N > 1: the reference-semantics ways of combining the shards, timed on
+    layer 0 beside the in-kernel LSE merge (eager, CUDA events, the slowest
+    rank): the stratified all-gather of the retained K/V blocks + indirect
+    attention over the gathered blocks, and the AllToAllv by KV head +
+    attention for this rank's heads + all-gather of the outputs.  Each
+    includes this shard's scoring and compaction."""
+    import torch
+    import torch.distributed as dist
+    from orthocache_b200 import distributed as ocd, score_blocks, _core
+    q = L.q
+
+    def scored():
+        keep = score_blocks(L.k, q, tau=L.tau, zeta_max=ZETA_MAX, want=("keep",))["keep"]
+        return keep, ocd.stream_compact(keep)
+
+    def stratified():
+        _, (idx, n) = scored()
+        kr, vr, counts, order, total, b = ocd.stratified_exchange(eng.comm, L.k, L.v, idx, n)
+        return _core.attend(q.unsqueeze(0), kr.unsqueeze(0), vr.unsqueeze(0), order.reshape(1, -1), total, 512,
+                            out_dtype=torch.bfloat16)
+
+    def alltoallv():
+        keep, _ = scored()
+        return ocd.head_partitioned_attention(q, L.k, L.v, keep, eng.comm)
+
+    out = {}
+    for name, fn in (("stratified_allgather", stratified), ("alltoallv_heads", alltoallv)):
+        for _ in range(3):
+            fn()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps * 1e3], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name + "_us"] = round(float(t.item()), 2)
+    out["how"] = ("eager, layer 0, %d calls between CUDA events, slowest rank; each includes the shard's scoring "
+                  "and compaction; the stratified exchange reads the counts on the host once per call" % reps)
+    return out
+
+
 def sharded_parity(eng, L, rank, world, device):
     """N > 1: the merged output of one sharded layer against the oracle.
     Every rank computes, on its host, the reference's two-gate mask of its
@@ -493,6 +657,11 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)  # per window, the slowest rank
         win_ms = t.tolist()
     ms = statistics.median(win_ms)
+    # Write-time metadata path (N = 1): the blocks' DC / E_AC / zeta computed
+    # once when written (oc_block_metadata), so a decode layer reads the
+    # metadata and only the retained blocks' K and V: the gates, the
+    # compaction and the split-KV attention, timed like the fused layer.
+    meta = metadata_decode_time(eng, layers, K) if world == 1 else None
     # The scorer alone (oc_score_blocks, the stand-alone form of the fused
     # layer's scoring phase): average launch duration in a CUDA-graph replay
     # of LAYERS launches on rotating inputs (the same measurement as the
@@ -530,27 +699,31 @@ def run_ours(args, rank, world, local_rank):
     # ---- end to end through the public API, host buffers ----
     from orthocache_b200 import _lib  # noqa: F401
     q_host = [L.q.cpu().pin_memory() for L in layers]
-    q_dev = torch.empty_like(layers[0].q)
-    out_host = torch.empty(tuple(eng.out.shape), dtype=torch.bfloat16).pin_memory()
     cnt_host = torch.empty((1,), dtype=torch.int32).pin_memory()
     Ke = max(8, min(K, 2000))
-    for s in range(4):
-        q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
-        eng.step(layers[s % LAYERS], q_dev)
-        out_host.copy_(eng.out, non_blocking=True)
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for s in range(Ke):
-        L = layers[s % LAYERS]
-        q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
-        eng.step(L, q_dev)
-        out_host.copy_(eng.out, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / Ke
-    if world > 1:
+    e2e_how = "serial"
+    if world == 1:
+        e2e_ms = e2e_pipelined(eng, layers, q_host, Ke)
+        e2e_how = "pipelined"
+    else:
+        q_dev = torch.empty_like(layers[0].q)
+        out_host = torch.empty(tuple(eng.out.shape), dtype=torch.bfloat16).pin_memory()
+        for s in range(4):
+            q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
+            eng.step(layers[s % LAYERS], q_dev)
+            out_host.copy_(eng.out, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s in range(Ke):
+            L = layers[s % LAYERS]
+            q_dev.copy_(q_host[s % LAYERS], non_blocking=True)
+            eng.step(L, q_dev)
+            out_host.copy_(eng.out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / Ke
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
@@ -562,6 +735,9 @@ def run_ours(args, rank, world, local_rank):
     kept = statistics.mean(L.kept for L in layers)
     alg_bytes = k_bytes + kept / nb * 2 * k_bytes + HQ * D * 2 * 2
     parity = None
+    variants = None
+    if world > 1 and not args.no_variants:
+        variants = exchange_variants(eng, layers[0], world, device)
     if world > 1:
         # whole-job algorithmic bytes (every shard's own eviction)
         t = torch.tensor([alg_bytes], dtype=torch.float64, device=device)
@@ -605,6 +781,7 @@ def run_ours(args, rank, world, local_rank):
                       "peak_kind": peak_kind + " x %d GPUs" % world, "bytes_per_launch": int(job_bytes),
                       "how": "whole-job algorithmic bytes (each shard: |K| + kept/nb (|K|+|V|)) over the max-over-"
                              "ranks average layer time, against the sum of the GPUs' measured copy peaks"}),
+        "metadata_decode": meta,
         "scorer_roofline": {"kernel": "score_tma_kernel<128,false> (oc_score_blocks alone)",
                             "achieved": round(score_gbs, 1), "frac": round(score_gbs / hbm, 4),
                             "bytes_per_launch": k_bytes},
@@ -618,11 +795,15 @@ def run_ours(args, rank, world, local_rank):
         "timed_region": ("CUDA-graph replay of %d consecutive layers" % LAYERS) if graphs is not None else
                         "eager launches",
         "parity": parity,
+        "exchange_variants": variants,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": UNIT, "h2d_bytes_per_step": HQ * D * 2,
                 "d2h_bytes_per_step": HQ * D * 2,
-                "note": "public C-ABI call per step, eager; the query copied from pinned host memory, the "
-                        "attention output read back; KV cache resident in HBM as in decode"},
+                "note": ("public C-ABI call per step, eager; the query copied from pinned host memory, the "
+                         "attention output read back; KV cache resident in HBM as in decode; " +
+                         ("copies on a second stream, double-buffered: step i+1's query goes up and step i's "
+                          "output comes back while step i+1 runs" if e2e_how == "pipelined" else
+                          "copies and call in one stream"))},
         "gpu_launches": K * eng.launches_per_step,
         "clocks": clk.summary(),
         "retained_blocks": kept,
