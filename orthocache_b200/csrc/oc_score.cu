@@ -394,7 +394,7 @@ __device__ int g_score_status = 0;
 
 #ifdef OC_TIMING
 // Diagnostic build only: per-CTA time stamps of the pipelined scorer.
-__device__ unsigned long long g_sstamp[1024][20];
+__device__ unsigned long long g_sstamp[1024][24];
 #define OC_SSTAMP(i, v) do { if (blockIdx.x < 1024) g_sstamp[blockIdx.x][i] = (v); } while (0)
 #else
 #define OC_SSTAMP(i, v) do {} while (0)
@@ -558,6 +558,7 @@ __device__ __noinline__ void fused_peer_merge(const PeerMergeArgs pa, int grp, i
   const int par = seq & 1, flag = seq + 1;
   if (tid == 0) {
     __threadfence_system();
+    OC_SSTAMP(23, globaltimer_ns());
     for (int p = 0; p < px.P; ++p) {
       int* fl = reinterpret_cast<int*>(px.bases[p] + px.flag_off) + ((size_t)par * px.P + px.rank) * pa.NG + grp;
       asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl), "r"(flag) : "memory");
@@ -579,6 +580,7 @@ __device__ __noinline__ void fused_peer_merge(const PeerMergeArgs pa, int grp, i
     __syncwarp();
   }
   asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+  if (tid == 0) OC_SSTAMP(22, globaltimer_ns());
   if (!*abort_flag) {
     const float* base = reinterpret_cast<const float*>(px.bases[px.rank]);
     for (int x = tid; x < pa.R * D; x += kScoreThreads) {
@@ -1294,7 +1296,9 @@ scored:
       pa.px = f.px;
       pa.NG = f.NG; pa.R = f.R; pa.G = a.G; pa.Sq = a.Sq; pa.Hq = a.Hq;
       pa.out = f.out; pa.out_bf16 = f.out_bf16;
+      if (tid == 0) OC_SSTAMP(20, globaltimer_ns());
       fused_peer_merge(pa, grp, bq, hq, s_seq, tid, &s_abort);
+      if (tid == 0) OC_SSTAMP(21, globaltimer_ns());
     }
     if (tid == 0) OC_SSTAMP(14, globaltimer_ns());
   }
@@ -1888,7 +1892,7 @@ int score_status(int* status, int reset) {
 
 #ifdef OC_TIMING
 extern "C" int oc_probe_read_score_stamps(unsigned long long* host, int n) {
-  return (int)cudaMemcpyFromSymbol(host, oc::g_sstamp, sizeof(unsigned long long) * 20 * n);
+  return (int)cudaMemcpyFromSymbol(host, oc::g_sstamp, sizeof(unsigned long long) * 24 * n);
 }
 #endif
 
