@@ -441,11 +441,10 @@ extern "C" int oc_sharded_connect(void* comm, void* workspace, size_t workspace_
       table[p] = static_cast<char*>(mapped) + all[p].offset;
     }
   }
-  // the table, and flags that start at zero (the call numbers start at 1)
-  const size_t flag_off = (size_t)2 * P * L.NG * kXchgBlock * sizeof(float);
+  // the table, and exchange words that start at zero (call numbers start at 1)
   e = open_err;
   if (e == cudaSuccess) e = cudaMemcpyAsync(ws + L.table, table.data(), sizeof(char*) * P, cudaMemcpyHostToDevice, st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(region + flag_off, 0, (size_t)2 * P * L.NG * sizeof(int), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(region, 0, xchg_region_bytes(P, L.NG), st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   // Agree on the outcome: every rank learns whether every other rank is
   // connected (and has its flags at zero) before any exchange, so that no
@@ -514,7 +513,6 @@ extern "C" int oc_decode_step_sharded(void* comm, const void* q, const void* k, 
     px.bases = reinterpret_cast<char* const*>(ws + L.table);
     px.P = P;
     px.rank = me;
-    px.flag_off = (size_t)2 * P * L.NG * kXchgBlock * sizeof(float);
     rc = decode_fused(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max, keep, perm, count,
                       out, out_dtype, nullptr, nullptr, nullptr, workspace, L.base, st, &px);
     if (rc != OC_ERR_UNSUPPORTED) return rc;

@@ -45,15 +45,15 @@ int wait_limit_prefill(unsigned long long ns);
 // oc_partial_attention) instead of out.
 size_t decode_fused_bytes(int batch, int seq_len, int kv_heads);
 // Cross-GPU exchange of the fused layer's per-shard partials by peer stores:
-// every rank's exchange region (recv blocks, then flags) is mapped into
-// every other rank's address space; bases[p] is rank p's region (this
-// rank's own at [rank]), a device array of P pointers.  Region layout:
-// recv float[2][P][NG][kXchgBlock] (parity of the call, source rank, group
-// (b, h): m[8] | l[8] | o[8][128]), then flags int[2][P][NG].
+// every rank's exchange region is mapped into every other rank's address
+// space; bases[p] is rank p's region (this rank's own at [rank]), a device
+// array of P pointers.  Region layout: uint64 words [2][P][NG][kXchgBlock]
+// (parity of the call, source rank, group (b, h): m[8] | l[8] | o[8][128]),
+// each word = the float's bits (low half) | the call number + 1 (high half),
+// so a reader knows a word is this call's by looking at it: no separate flag.
 struct PeerXchg {
   char* const* bases;
   int P, rank;
-  size_t flag_off;  // byte offset of the flags inside a region
 };
 constexpr int kXchgBlock = 8 * (128 + 2);
 size_t xchg_region_bytes(int P, int NG);

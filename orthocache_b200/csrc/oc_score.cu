@@ -531,13 +531,25 @@ __device__ __forceinline__ void fused_write_perm(const int* st, int nb, int32_t*
   }
 }
 
+// Words of the cross-GPU exchange: one 8-byte store / load each (single-copy
+// atomic), relaxed at system scope; a word is this call's when its high half
+// is the call number + 1 (slots alternate by parity, so a stale word holds
+// an older number).
+__device__ __forceinline__ void xchg_put(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t xchg_get(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // The cross-GPU half of the fused layer's group merge (FusedArgs::px): kept
 // out of line so that the single-GPU kernel's register allocation does not
 // pay for it.  The calling CTA has stored this shard's partial of the group
-// into every rank's slot; here it publishes a flag carrying the call number
-// (slots are reused every other call without clearing), waits (bounded) for
-// every rank's flag of this call and merges the P partials of the group:
-// out on every rank.
+// into every rank's slot; each thread here waits (bounded) for the words of
+// its output element from every rank and merges the P partials: out on
+// every rank.
 struct PeerMergeArgs {
   PeerXchg px;
   int NG, R, G, Sq, Hq, out_bf16;
@@ -548,61 +560,48 @@ __device__ __noinline__ void fused_peer_merge(const PeerMergeArgs pa, int grp, i
                                               volatile int* abort_flag) {
   constexpr int D = 128;
   const PeerXchg& px = pa.px;
-  const int lane = tid & 31;
-  // Publish (the pattern of a grid barrier, at system scope): the CTA
-  // barrier orders every thread's peer stores before thread 0, whose one
-  // system-scope fence and release stores of the flags make them visible to
-  // the peers before the flags.  (A fence in every thread would serialise
-  // 512 system-scope fences.)
-  asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
-  const int par = seq & 1, flag = seq + 1;
-  if (tid == 0) {
-    __threadfence_system();
-    OC_SSTAMP(23, globaltimer_ns());
-    for (int p = 0; p < px.P; ++p) {
-      int* fl = reinterpret_cast<int*>(px.bases[p] + px.flag_off) + ((size_t)par * px.P + px.rank) * pa.NG + grp;
-      asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(fl), "r"(flag) : "memory");
+  const int par = seq & 1;
+  const uint32_t want = (uint32_t)(seq + 1);
+  const uint64_t* base = reinterpret_cast<const uint64_t*>(px.bases[px.rank]);
+  const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
+  // a word of this call (bounded wait); false if the limit passed
+  auto get = [&](const uint64_t* p, float& v) {
+    uint64_t w = xchg_get(p);
+    while ((uint32_t)(w >> 32) != want) {
+      if (globaltimer_ns() - t0 > g_wait_limit_ns) return false;
+      __nanosleep(32);
+      w = xchg_get(p);
     }
-  }
-  if (tid < 32) {
-    const int* mine = reinterpret_cast<const int*>(px.bases[px.rank] + px.flag_off) +
-                      (size_t)par * px.P * pa.NG + grp;
-    const uint64_t t0 = globaltimer_ns();
-    for (int src = lane; src < px.P; src += 32) {
-      int v;
-      for (;;) {
-        asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine + (size_t)src * pa.NG) : "memory");
-        if (v == flag) break;
-        if (globaltimer_ns() - t0 > g_wait_limit_ns) { *abort_flag = 1; atomicExch(&g_score_status, 1); break; }
-        __nanosleep(64);
-      }
+    v = __uint_as_float((uint32_t)w);
+    return true;
+  };
+  for (int x = tid; x < pa.R * D && ok; x += kScoreThreads) {
+    const int r = x / D, d = x - r * D;
+    float M = -INFINITY, L = 0.f, O = 0.f;
+    for (int src = 0; src < px.P && ok; ++src) {
+      const uint64_t* blk = base + ((size_t)(par * px.P + src) * pa.NG + grp) * kXchgBlock;
+      float m, l, o;
+      ok = get(blk + r, m) && get(blk + 8 + r, l) && get(blk + 16 + r * D + d, o);
+      if (!ok || m == -INFINITY) continue;
+      const float mc = fmaxf(M, m);
+      const float sa = exp2f(M - mc), sb = exp2f(m - mc);
+      L = L * sa + l * sb;
+      O = O * sa + o * sb;
+      M = mc;
     }
-    __syncwarp();
+    if (!ok) break;
+    const int s = r / pa.G, gq = r - s * pa.G;
+    const size_t orow = ((size_t)bq * pa.Sq + s) * pa.Hq + (size_t)hq * pa.G + gq;
+    const float y = L > 0.f ? O / L : 0.f;
+    if (pa.out_bf16) reinterpret_cast<__nv_bfloat16*>(pa.out)[orow * D + d] = __float2bfloat16_rn(y);
+    else reinterpret_cast<float*>(pa.out)[orow * D + d] = y;
   }
-  asm volatile("bar.sync 2, %0;" ::"r"(kScoreThreads) : "memory");
+  if (!ok) {
+    *abort_flag = 1;
+    atomicExch(&g_score_status, 1);
+  }
   if (tid == 0) OC_SSTAMP(22, globaltimer_ns());
-  if (!*abort_flag) {
-    const float* base = reinterpret_cast<const float*>(px.bases[px.rank]);
-    for (int x = tid; x < pa.R * D; x += kScoreThreads) {
-      const int r = x / D, d = x - r * D;
-      float M = -INFINITY;
-      for (int src = 0; src < px.P; ++src)
-        M = fmaxf(M, __ldcv(base + ((size_t)(par * px.P + src) * pa.NG + grp) * kXchgBlock + r));
-      float L = 0.f, O = 0.f;
-      if (M != -INFINITY)
-        for (int src = 0; src < px.P; ++src) {
-          const float* blk = base + ((size_t)(par * px.P + src) * pa.NG + grp) * kXchgBlock;
-          const float w = exp2f(__ldcv(blk + r) - M);
-          L = fmaf(__ldcv(blk + 8 + r), w, L);
-          O = fmaf(__ldcv(blk + 16 + r * D + d), w, O);
-        }
-      const int s = r / pa.G, gq = r - s * pa.G;
-      const size_t orow = ((size_t)bq * pa.Sq + s) * pa.Hq + (size_t)hq * pa.G + gq;
-      const float y = L > 0.f ? O / L : 0.f;
-      if (pa.out_bf16) reinterpret_cast<__nv_bfloat16*>(pa.out)[orow * D + d] = __float2bfloat16_rn(y);
-      else reinterpret_cast<float*>(pa.out)[orow * D + d] = y;
-    }
-  }
 }
 
 template <int D, bool FUSED>
@@ -1274,11 +1273,17 @@ scored:
         if (f.px.P > 0) {
           // This shard's partial of group grp into slot [parity][rank][grp]
           // of every rank's exchange region (plain stores over NVLink).
+          // Each word carries its float and the call number + 1, so no
+          // fence or flag is needed: the reader waits for each word.
           const size_t slot = ((size_t)(s_seq & 1) * f.px.P + f.px.rank) * f.NG + grp;
+          const uint64_t tag = (uint64_t)(uint32_t)(s_seq + 1) << 32;
           for (int p = 0; p < f.px.P; ++p) {
-            float* blk = reinterpret_cast<float*>(f.px.bases[p]) + slot * kXchgBlock;
-            blk[16 + r * D + d] = O;
-            if (d == 0) { blk[r] = M; blk[8 + r] = L; }
+            uint64_t* blk = reinterpret_cast<uint64_t*>(f.px.bases[p]) + slot * kXchgBlock;
+            xchg_put(blk + 16 + r * D + d, tag | __float_as_uint(O));
+            if (d == 0) {
+              xchg_put(blk + r, tag | __float_as_uint(M));
+              xchg_put(blk + 8 + r, tag | __float_as_uint(L));
+            }
           }
         } else if (f.pm) {
           // Unnormalised partial of this shard for a cross-shard merge.
@@ -1902,8 +1907,7 @@ extern "C" int oc_probe_read_score_stamps(unsigned long long* host, int n) {
 namespace oc {
 
 size_t xchg_region_bytes(int P, int NG) {
-  const size_t recv = (size_t)2 * P * NG * kXchgBlock * sizeof(float);
-  return recv + ((size_t)2 * P * NG * sizeof(int) + 255) / 256 * 256;
+  return ((size_t)2 * P * NG * kXchgBlock * sizeof(uint64_t) + 255) / 256 * 256;
 }
 
 size_t decode_fused_bytes(int batch, int seq_len, int kv_heads) {
