@@ -308,37 +308,72 @@ constexpr int kVStageBytes = 32768;  // K + V of one item: 2 * CH * D * 2 with C
 
 __device__ int g_attn_status = 0;
 
-// Item w of the (batch, head, row tile, slot, chunk) order; false past the end.
-__device__ __forceinline__ bool run_item(const AttnArgs& a, int w, int& b, int& h, int& rt, int& item) {
-  for (b = 0; b < a.B; ++b)
-    for (h = 0; h < a.Hkv; ++h) {
-      const int n = list_len(a, b, h) * a.chunks;
-      const int tot = n * a.n_rt;
-      if (w < tot) {
-        rt = w / n;
-        item = w - rt * n;
-        return true;
-      }
-      w -= tot;
-    }
-  return false;
+// Work items of the (batch, kv head) lists: list i = (b = i / Hkv, h = i %
+// Hkv) holds list_len x chunks x row tiles items.  The stream kernels keep an
+// exclusive prefix of these counts in shared memory, pre[0 .. B*Hkv] (the
+// last entry is the total), built by the whole CTA in one round of
+// independent loads; locating an item is then a binary search instead of a
+// walk over every list before it.
+constexpr int kMaxLists = 1024;  // B * Hkv of the stream kernels (the host checks)
+
+template <int NT>
+__device__ __forceinline__ void build_list_prefix(const AttnArgs& a, int* pre, int* s_warp) {
+  constexpr int NW = NT / 32;
+  constexpr int kPer = (kMaxLists + NT - 1) / NT;
+  const int NL = a.B * a.Hkv;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int i0 = tid * kPer;
+  int len[kPer];
+  int v = 0;
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int i = i0 + u;
+    len[u] = i < NL ? list_len(a, i / a.Hkv, i % a.Hkv) * a.chunks * a.n_rt : 0;
+    v += len[u];
+  }
+  int x = v;  // inclusive scan over the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  int run = x - v;
+#pragma unroll
+  for (int w = 0; w < NW; ++w)
+    if (w < warp) run += s_warp[w];
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int i = i0 + u;
+    if (i < NL) pre[i] = run;
+    run += len[u];
+  }
+  if (tid == NT - 1) pre[NL] = run;
+  __syncthreads();
 }
 
-__device__ __forceinline__ int total_items(const AttnArgs& a) {
-  int n = 0;
-  for (int b = 0; b < a.B; ++b)
-    for (int h = 0; h < a.Hkv; ++h) n += list_len(a, b, h) * a.chunks * a.n_rt;
-  return n;
-}
-
-// Incremental walk over the (batch, head, row tile, item) order, skipping
-// empty lists; b == B marks the end.
+// Item w (< pre[NL]) of the (batch, head, row tile, slot, chunk) order.
 struct ItemIter {
-  int b, h, rt, item, n;
-  __device__ void start(const AttnArgs& a, int w, int N) {
-    if (w >= N) { b = a.B; h = rt = item = 0; n = 1; return; }
-    run_item(a, w, b, h, rt, item);
-    n = list_len(a, b, h) * a.chunks;
+  const int* pre;
+  int NL, li, b, h, rt, item, n;  // n: items of one row tile of list li; b == B marks the end
+  __device__ void start(const AttnArgs& a, const int* p, int w) {
+    pre = p;
+    NL = a.B * a.Hkv;
+    if (w >= pre[NL]) { li = NL; b = a.B; h = rt = item = 0; n = 1; return; }
+    int lo = 0, hi = NL;  // pre[lo] <= w < pre[hi]; ends on the non-empty list holding w
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (pre[mid] <= w) lo = mid;
+      else hi = mid;
+    }
+    li = lo;
+    b = li / a.Hkv;
+    h = li - b * a.Hkv;
+    n = (pre[li + 1] - pre[li]) / a.n_rt;
+    const int local = w - pre[li];
+    rt = local / n;
+    item = local - rt * n;
   }
   __device__ void next(const AttnArgs& a) {
     if (b >= a.B) return;
@@ -347,9 +382,11 @@ struct ItemIter {
     if (++rt < a.n_rt) return;
     rt = 0;
     do {
-      if (++h >= a.Hkv) { h = 0; ++b; }
-      n = b < a.B ? list_len(a, b, h) * a.chunks : 1;
+      if (++li >= NL) { b = a.B; n = 1; return; }
+      n = (pre[li + 1] - pre[li]) / a.n_rt;
     } while (n == 0);
+    b = li / a.Hkv;
+    h = li - b * a.Hkv;
   }
 };
 
@@ -379,29 +416,17 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[NV], int lane) {
 }
 
 // Block indices of a CTA's first kBlkCache items, loaded by one warp in a
-// single round of independent loads (lane i walks from the CTA's first item
-// to item i list by list), so that no stage refill waits on a global load.
+// single round of independent loads, so that no stage refill waits on a
+// global load.
 constexpr int kBlkCache = 64;
 
-__device__ __forceinline__ void fill_blk_cache(const AttnArgs& a, int beg, int N, int n_mine, int* s_blk,
+__device__ __forceinline__ void fill_blk_cache(const AttnArgs& a, const int* pre, int beg, int n_mine, int* s_blk,
                                                int lane) {
   const int n = min(n_mine, kBlkCache);
   for (int i = lane; i < n; i += 32) {
     ItemIter p;
-    p.start(a, beg, N);
-    int off = i;
-    while (off > 0 && p.b < a.B) {
-      const int rem = p.n - 1 - p.item;  // items after this one in its (batch, head, row tile) list
-      if (off <= rem) {
-        p.item += off;
-        off = 0;
-      } else {
-        off -= rem + 1;
-        p.item = p.n - 1;
-        p.next(a);
-      }
-    }
-    s_blk[i] = p.b < a.B ? a.idx[(size_t)p.b * a.idx_stride + (size_t)p.h * a.idx_hstride + p.item / a.chunks] : 0;
+    p.start(a, pre, beg + i);
+    s_blk[i] = a.idx[(size_t)p.b * a.idx_stride + (size_t)p.h * a.idx_hstride + p.item / a.chunks];
   }
 }
 
@@ -428,6 +453,8 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __shared__ int s_blk[kBlkCache];
   __shared__ float s_wm[kVWarps][RT], s_wl[kVWarps][RT];
   __shared__ float s_wo[kVWarps][RT][D];
+  __shared__ int s_pre[kMaxLists + 1];
+  __shared__ int s_scan[kVWarps];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) {
@@ -440,7 +467,8 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   // Launched as a programmatic dependent of the compaction: the lists and
   // counts (and everything else) are read only after it has finished.
   pdl_wait();
-  const int N = total_items(a);
+  build_list_prefix<kVThreads>(a, s_pre, s_scan);
+  const int N = s_pre[a.B * a.Hkv];
   const int per = (N + gridDim.x - 1) / gridDim.x;
   const int beg = min(N, (int)blockIdx.x * per), end = min(N, beg + per);
   const int n_mine = end - beg;
@@ -460,12 +488,12 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   };
 
   if (warp == 0) {
-    fill_blk_cache(a, beg, N, n_mine, s_blk, lane);
+    fill_blk_cache(a, s_pre, beg, n_mine, s_blk, lane);
     __syncwarp();
   }
   if (tid == 0) {
     ItemIter pre;
-    pre.start(a, beg, N);
+    pre.start(a, s_pre, beg);
     for (int k = 0; k < kVStages && k < n_mine; ++k) {
       issue(k, pre);
       pre.next(a);
@@ -484,8 +512,8 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   // Position of the item being consumed, and of the item kVStages ahead
   // (the one a stage released now is refilled with).
   ItemIter cur, ahead;
-  cur.start(a, beg, N);
-  ahead.start(a, beg, N);
+  cur.start(a, s_pre, beg);
+  ahead.start(a, s_pre, beg);
   for (int i = 0; i < kVStages; ++i) ahead.next(a);
   const int my_v = lane >> SH;            // value index this lane ends up holding
   const int my_t = my_v / RT, my_r = my_v % RT;
@@ -774,7 +802,8 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   __shared__ int s_blk[kBlkCache];
   __shared__ float s_wm[NW][RT], s_wl[NW][RT];
   __shared__ float s_wo[NW][RT][D];
-
+  __shared__ int s_pre[kMaxLists + 1];
+  __shared__ int s_wsum[NW];
 
   OC_STAMP(0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -796,7 +825,8 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     int* s_list = reinterpret_cast<int*>(smem + (size_t)kMStages * kMStageBytes);
     lists_from_keep<NT>(a, s_list, s_list + a.B * (a.S / a.bs), s_scan);
   }
-  const int N = total_items(a);
+  build_list_prefix<NT>(a, s_pre, s_wsum);
+  const int N = s_pre[a.B * a.Hkv];
   const int per = (N + gridDim.x - 1) / gridDim.x;
   const int beg = min(N, (int)blockIdx.x * per), end = min(N, beg + per);
   const int n_mine = end - beg;
@@ -817,13 +847,13 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   };
 
   if (warp == 0) {
-    fill_blk_cache(a, beg, N, n_mine, s_blk, lane);
+    fill_blk_cache(a, s_pre, beg, n_mine, s_blk, lane);
     OC_STAMP(7);
     __syncwarp();
   }
   if (tid == 0) {
     ItemIter pre;
-    pre.start(a, beg, N);
+    pre.start(a, s_pre, beg);
     for (int k = 0; k < kMStages && k < n_mine; ++k) {
       issue(k, pre);
       pre.next(a);
@@ -839,8 +869,8 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   uint32_t qa[KS][4];
   int cur_b = -1, cur_h = -1, cur_rt = -1, run_first = 0;
   ItemIter cur, ahead;
-  cur.start(a, beg, N);
-  ahead.start(a, beg, N);
+  cur.start(a, s_pre, beg);
+  ahead.start(a, s_pre, beg);
   for (int i = 0; i < kMStages; ++i) ahead.next(a);
   OC_STAMP(1);
 
@@ -1066,13 +1096,25 @@ attn_merge_kernel(AttnArgs a, TO* out, float* pm, float* pl, float* po, int mode
   // tile) list and every CTA boundary c * per that falls inside it.
   int np = n, s0 = 0, per = 1, c1 = 0;
   if (a.run_grid > 0 && n > 0) {
+    // Items of all lists and of the lists before (b, h): one load per
+    // thread, summed over the CTA.
+    __shared__ int s_tb[2][kMergeThreads / 32];
+    const int me = b * a.Hkv + h;
     int total = 0, before = 0;
-    for (int bb = 0; bb < a.B; ++bb)
-      for (int hh = 0; hh < a.Hkv; ++hh) {
-        const int len = list_len(a, bb, hh) * a.chunks * a.n_rt;
-        if (bb < b || (bb == b && hh < h)) before += len;
-        total += len;
-      }
+    for (int i = tid; i < a.B * a.Hkv; i += kMergeThreads) {
+      const int len = list_len(a, i / a.Hkv, i % a.Hkv) * a.chunks * a.n_rt;
+      total += len;
+      if (i < me) before += len;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      total += __shfl_xor_sync(0xffffffffu, total, o);
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+    }
+    if (lane == 0) { s_tb[0][warp] = total; s_tb[1][warp] = before; }
+    __syncthreads();
+    total = before = 0;
+    for (int w = 0; w < kMergeThreads / 32; ++w) { total += s_tb[0][w]; before += s_tb[1][w]; }
     per = (total + a.run_grid - 1) / a.run_grid;
     s0 = before + (r / a.rt_tile) * n;
     c1 = s0 / per + 1;                                   // first CTA boundary after s0
@@ -1202,7 +1244,11 @@ int pick_rt(int R, int D) {
 int chunk_for(int bs, int D) { return bs % (8192 / D) == 0 ? 8192 / D : 64; }
 
 // bfloat16 inputs stream through the bulk-tensor path when the chunk fits.
-bool use_tma_path(int dtype, int bs, int D) { return dtype == OC_BF16 && bs % (8192 / D) == 0; }
+// Stream kernels: bfloat16, whole items per block, and at most kMaxLists
+// (batch, kv head) lists (their prefix lives in shared memory).
+bool use_tma_path(int dtype, int bs, int D, int64_t lists) {
+  return dtype == OC_BF16 && bs % (8192 / D) == 0 && lists <= kMaxLists;
+}
 
 size_t attn_ws_bytes(int B, int Sq, int Hq, int Hkv, int D, int bs, int max_blocks) {
   const int G = Hq / Hkv;
@@ -1281,7 +1327,7 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.kv_rows = pool_pages > 0 ? 0 : S;
   a.nblk = pool_pages > 0 ? pool_pages : S / bs;
   a.R = Sq * a.G;
-  const bool tma = use_tma_path(dtype, bs, D);
+  const bool tma = use_tma_path(dtype, bs, D, (int64_t)B * Hkv);
   const bool mma = tma && (D == 64 || D == 128);  // tensor-core stream kernel
   int rt = pick_rt(a.R, D);
   if (tma && rt * D > 512) rt = 512 / D;

@@ -531,13 +531,13 @@ __device__ __forceinline__ void fused_write_perm(const int* st, int nb, int32_t*
   }
 }
 
-// Words of the cross-GPU exchange: one 8-byte store / load each (single-copy
-// atomic), relaxed at system scope; a word is this call's when its high half
-// is the call number + 1 (slots alternate by parity, so a stale word holds
-// an older number).
-__device__ __forceinline__ void xchg_put(uint64_t* p, uint64_t v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
+// Words of the cross-GPU exchange: one aligned 8-byte store / load each
+// (single-copy atomic), relaxed at system scope (a volatile store is one);
+// a word is this call's when its high half is the call number + 1 (slots
+// alternate by parity, so a stale word holds an older number).  The store
+// is a volatile access rather than inline assembly with a memory clobber:
+// the clobber would also pin the single-GPU merge loop's loads in place.
+__device__ __forceinline__ void xchg_put(uint64_t* p, uint64_t v) { *reinterpret_cast<volatile uint64_t*>(p) = v; }
 __device__ __forceinline__ uint64_t xchg_get(const uint64_t* p) {
   uint64_t v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
