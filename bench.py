@@ -450,20 +450,17 @@ def metadata_decode_time(eng, layers, K):
         L.m_zeta = torch.empty((nb, HKV), **f32)
         _lib.call("oc_block_metadata", _lib.ptr(L.k), 1, 1, S_SHARD, HKV, D, _lib.ptr(L.m_dc), _lib.ptr(L.m_eac),
                   _lib.ptr(L.m_zeta), st())
-    bmax = torch.empty((nb, HKV), **f32)
     keep = torch.empty((nb, HKV), dtype=torch.uint8, device=dev)
     perm = torch.empty((nb,), dtype=torch.int32, device=dev)
     count = torch.empty((1,), dtype=torch.int32, device=dev)
     out = torch.empty((1, HQ, D), dtype=torch.bfloat16, device=dev)
-    ws_bytes = _lib.query("oc_indirect_attention_workspace_bytes", 1, 1, HQ, HKV, D, 512, nb)
-    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    ws_bytes = _lib.query("oc_decode_step_workspace_bytes", 1, 1, HQ, HKV, D, S_SHARD)
+    ws = torch.zeros((ws_bytes,), dtype=torch.uint8, device=dev)
 
     def layer(L):
-        _lib.call("oc_score_from_metadata", _lib.ptr(L.m_dc), _lib.ptr(L.m_eac), _lib.ptr(L.m_zeta), _lib.ptr(L.q),
-                  1, 1, nb, HKV, D, 1, HQ, L.tau, ZETA_MAX, _lib.ptr(bmax), None, _lib.ptr(keep), st())
-        _lib.call("oc_stream_compact", _lib.ptr(keep), 1, nb, HKV, _lib.ptr(perm), _lib.ptr(count), st())
-        _lib.call("oc_indirect_attention", _lib.ptr(L.q), _lib.ptr(L.k), _lib.ptr(L.v), 1, _lib.ptr(perm), nb, 0,
-                  _lib.ptr(count), 1, 0, 1, 1, HQ, HKV, D, S_SHARD, 512, nb, _lib.ptr(out), 1, _lib.ptr(ws),
+        _lib.call("oc_decode_step_from_metadata", _lib.ptr(L.q), _lib.ptr(L.k), _lib.ptr(L.v), 1,
+                  _lib.ptr(L.m_dc), _lib.ptr(L.m_eac), _lib.ptr(L.m_zeta), 1, 1, HQ, HKV, D, S_SHARD, L.tau,
+                  ZETA_MAX, _lib.ptr(keep), _lib.ptr(perm), _lib.ptr(count), _lib.ptr(out), 1, _lib.ptr(ws),
                   ws_bytes, st())
 
     for L in layers:
@@ -497,7 +494,8 @@ def metadata_decode_time(eng, layers, K):
     hbm, kind = peaks()
     return {"us_per_layer": round(us, 3), "alg_bytes": int(alg),
             "achieved_gbs": round(alg / (us * 1e-6) / 1e9, 1), "frac": round(alg / (us * 1e-6) / 1e9 / hbm, 4),
-            "kernels": "oc_score_from_metadata + oc_stream_compact + oc_indirect_attention (3 per layer)",
+            "kernels": "oc_decode_step_from_metadata: one fused kernel per layer (gates from the metadata, "
+                       "in-kernel block decisions, attention over the retained blocks)",
             "how": "average layer in a CUDA-graph replay of %d layers; metadata written once per block "
                    "(write time, not timed); bytes = metadata + retained K and V + q / out" % LAYERS}
 

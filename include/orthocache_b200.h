@@ -331,6 +331,24 @@ int oc_decode_step(const void* q, const void* k, const void* v, int dtype,
                    void* out, int out_dtype,
                    void* workspace, size_t workspace_bytes, oc_stream_t stream);
 
+/* The same decode step with the blocks' gates taken from write-time
+ * spectral metadata (oc_block_metadata output: dc (B, nb, Hkv, D), e_ac and
+ * zeta (B, nb, Hkv) float32) instead of a pass over the keys: the bound of
+ * compute_query_aware_bounds (spectral_energy.py:141-177) from the DC
+ * coefficients and E_AC, the zeta gate of compute_multiband_mask
+ * (spectral_energy.py:199-234) from the stored zeta; the keys are read only
+ * for the retained blocks.  Same shapes, outputs and workspace contract as
+ * oc_decode_step (the one-kernel path under the same conditions; the
+ * separate kernels oc_score_from_metadata, oc_stream_compact and
+ * oc_indirect_attention otherwise). */
+int oc_decode_step_from_metadata(const void* q, const void* k, const void* v, int dtype,
+                                 const float* dc, const float* e_ac, const float* zeta,
+                                 int batch, int q_len, int q_heads, int kv_heads, int head_dim, int seq_len,
+                                 float tau, float zeta_max,
+                                 uint8_t* keep, int32_t* perm, int32_t* count,
+                                 void* out, int out_dtype,
+                                 void* workspace, size_t workspace_bytes, oc_stream_t stream);
+
 /* The decode step of one sequence shard, for the log-sum-exp merge across
  * shards (distributed_attention.py:95-128 applied across devices): as
  * oc_decode_step, but instead of out it writes the shard's unnormalised

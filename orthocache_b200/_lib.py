@@ -81,6 +81,8 @@ SIGNATURES = {
     "oc_decode_step_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "oc_decode_step": (_i, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p, _p, _p, _i, _p, _sz,
                             _p]),
+    "oc_decode_step_from_metadata": (_i, [_p, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p, _p,
+                                          _p, _i, _p, _sz, _p]),
     "oc_decode_step_partial": (_i, [_p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _f, _p, _p, _p, _p, _p, _p, _p,
                                     _sz, _p]),
     "oc_merge_partials_packed": (_i, [_p, _i, _i, _i, _p, _i, _p]),

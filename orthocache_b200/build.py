@@ -30,6 +30,10 @@ def _compile(src):
     obj = os.path.join(OBJ, os.path.basename(src).replace(".cu", ".o"))
     hdrs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     hdrs.append(os.path.join(ROOT, "include", "orthocache_b200.h"))
+    # sources that include another .cu (oc_score_meta.cu) depend on it
+    with open(src) as f:
+        text = f.read()
+    hdrs += [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu") and f'#include "{f}"' in text]
     if os.path.exists(obj):
         t = os.path.getmtime(obj)
         if t >= os.path.getmtime(src) and all(t >= os.path.getmtime(h) for h in hdrs):

@@ -1557,6 +1557,41 @@ extern "C" int oc_decode_step(const void* q, const void* k, const void* v, int d
                                seq_len, 512, nb, out, out_dtype, workspace, workspace_bytes, stream);
 }
 
+extern "C" int oc_decode_step_from_metadata(const void* q, const void* k, const void* v, int dtype,
+                                            const float* dc, const float* e_ac, const float* zeta,
+                                            int batch, int q_len, int q_heads, int kv_heads, int head_dim,
+                                            int seq_len, float tau, float zeta_max,
+                                            uint8_t* keep, int32_t* perm, int32_t* count,
+                                            void* out, int out_dtype,
+                                            void* workspace, size_t workspace_bytes, oc_stream_t stream) {
+  OC_REQUIRE(keep && perm && count && out, OC_ERR_NULL, "oc_decode_step_from_metadata: null output pointer");
+  OC_REQUIRE(dc && e_ac && zeta, OC_ERR_NULL, "oc_decode_step_from_metadata: null metadata pointer");
+  OC_REQUIRE(seq_len % 512 == 0, OC_ERR_SHAPE, "oc_decode_step_from_metadata: seq_len %d not a multiple of 512",
+             seq_len);
+  OC_REQUIRE(batch >= 1 && kv_heads >= 1, OC_ERR_SHAPE, "oc_decode_step_from_metadata: batch/kv_heads < 1");
+  const int nb = seq_len / 512;
+  const size_t fused_bytes = oc::decode_fused_bytes(batch, seq_len, kv_heads);
+  OC_REQUIRE(workspace && workspace_bytes >= fused_bytes, OC_ERR_CAPACITY,
+             "oc_decode_step_from_metadata: workspace of %zu bytes, need at least %zu", workspace_bytes,
+             fused_bytes);
+  if (dtype == OC_BF16 && seq_len > 0) {
+    // One persistent kernel: decisions from the metadata, then attention.
+    const int frc = oc::decode_fused(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max,
+                                     keep, perm, count, out, out_dtype, nullptr, nullptr, nullptr, workspace,
+                                     fused_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr, dc, e_ac, zeta);
+    if (frc != OC_ERR_UNSUPPORTED) return frc;
+  }
+  workspace = static_cast<uint8_t*>(workspace) + fused_bytes;
+  workspace_bytes -= fused_bytes;
+  int rc = oc_score_from_metadata(dc, e_ac, zeta, q, dtype, batch, nb, kv_heads, head_dim, q_len, q_heads, tau,
+                                  zeta_max, nullptr, nullptr, keep, stream);
+  if (rc) return rc;
+  rc = oc_stream_compact(keep, batch, nb, kv_heads, perm, count, stream);
+  if (rc) return rc;
+  return oc_indirect_attention(q, k, v, dtype, perm, nb, 0, count, 1, 0, batch, q_len, q_heads, kv_heads, head_dim,
+                               seq_len, 512, nb, out, out_dtype, workspace, workspace_bytes, stream);
+}
+
 extern "C" int oc_decode_step_partial(const void* q, const void* k, const void* v, int dtype,
                                       int batch, int q_len, int q_heads, int kv_heads, int head_dim, int seq_len,
                                       float tau, float zeta_max,

@@ -28,10 +28,12 @@ bool first_on_device(std::atomic<uint64_t>& done);
 // Device-side error status of the pipelined kernels (a bounded wait gave up):
 // copies it to *status (0 = none) and clears it if reset.  Synchronous.
 int score_status(int* status, int reset);
+int score_status_meta(int* status, int reset);  // the metadata form of the fused layer (oc_score_meta.cu)
 int attn_status(int* status, int reset);
 int prefill_status(int* status, int reset);
 // Set the bounded-wait limit of the kernels of each translation unit.
 int wait_limit_score(unsigned long long ns);
+int wait_limit_score_meta(unsigned long long ns);
 int wait_limit_attn(unsigned long long ns);
 int wait_limit_prefill(unsigned long long ns);
 
@@ -60,7 +62,16 @@ size_t xchg_region_bytes(int P, int NG);
 int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
                  int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
                  void* out, int out_dtype, float* pm, float* pl, float* po, void* ws, size_t ws_bytes,
-                 cudaStream_t st, const PeerXchg* px = nullptr);
+                 cudaStream_t st, const PeerXchg* px = nullptr, const float* meta_dc = nullptr,
+                 const float* meta_eac = nullptr, const float* meta_zeta = nullptr);
+// The same layer with the block decisions from write-time metadata (dc,
+// e_ac, zeta of oc_block_metadata); decode_fused forwards to it when the
+// metadata pointers are given.
+int decode_fused_meta(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
+                      int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm,
+                      int32_t* count, void* out, int out_dtype, float* pm, float* pl, float* po, void* ws,
+                      size_t ws_bytes, cudaStream_t st, const PeerXchg* px, const float* meta_dc,
+                      const float* meta_eac, const float* meta_zeta);
 
 // Paged KV: phys (batch, max_blocks) = block_table[b][idx[b][i]] for the
 // first min(count[b], max_blocks) entries, -1 elsewhere (oc_compact.cu).

@@ -604,7 +604,64 @@ __device__ __noinline__ void fused_peer_merge(const PeerMergeArgs pa, int grp, i
   if (tid == 0) OC_SSTAMP(22, globaltimer_ns());
 }
 
-template <int D, bool FUSED>
+// Keep decision of tile `tile` of this CTA from write-time metadata
+// (warp-collective, the result on every lane): the bound of the key path's
+// epilogue (block mean = DC / sqrt(512), residual sqrt(|q|^2) sqrt(E_AC))
+// and the two gates, with a.dc / a.e_ac / a.zeta the stored metadata.
+template <int D>
+__device__ __forceinline__ int meta_keep(const ScoreArgs& a, int tile, bool q_cached, const __nv_bfloat16* s_q,
+                                         const float* s_qn, int lane) {
+  const int rows = a.Sq * a.G;
+  const __nv_bfloat16* qb = q_cached ? s_q : reinterpret_cast<const __nv_bfloat16*>(a.q);
+  const int t = blockIdx.x + tile * gridDim.x;
+  const int h = t % a.H;
+  const int j = (t / a.H) % a.nb;
+  const int b = t / (a.H * a.nb);
+  const size_t cell = ((size_t)b * a.nb + j) * a.H + h;
+  const float resid_scale = sqrtf(__ldg(a.e_ac + cell));
+  const float z = __ldg(a.zeta + cell);
+  const float* dcp = a.dc + cell * D;
+  float dv[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) dv[r] = 0.f;
+#pragma unroll
+  for (int c = lane; c < D; c += 32) {
+    const float mean = __ldg(dcp + c) / kNorm;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < rows) {
+        const int s = r / a.G, gq = r - s * a.G;
+        const size_t qrow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + gq;
+        dv[r] = fmaf(__bfloat162float(qb[qrow * D + c]), mean, dv[r]);
+      }
+  }
+  const float dot = transpose_sum8(dv, lane);
+  const int r = lane >> 2;
+  float bound = -INFINITY;
+  if (r < rows) {
+    const int s = r / a.G, gq = r - s * a.G;
+    const size_t qrow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + gq;
+    float nrm = 0.f;
+    if (q_cached) {
+      nrm = s_qn[qrow];
+    } else {
+      for (int c = 0; c < D; ++c) {
+        const float qv = __bfloat162float(qb[qrow * D + c]);
+        nrm = fmaf(qv, qv, nrm);
+      }
+    }
+    const float sqrt_d = sqrtf((float)D);
+    bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
+  }
+  const float bmax = warp_max(bound);
+  return (bmax >= a.tau && z <= a.zeta_max) ? 1 : 0;
+}
+
+// META (with FUSED): the block decisions come from write-time metadata
+// instead of a pass over the keys, and ScoreArgs::dc / e_ac / zeta are those
+// INPUTS (per cell (b, j, h): D DC coefficients, E_AC, zeta); the compute
+// warps go straight to the attention phase.
+template <int D, bool FUSED, bool META = false>
 __global__ void __launch_bounds__(kFusedThreads, 1)
 score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap amap_k,
                  const __grid_constant__ CUtensorMap amap_v, ScoreArgs a, int n_tiles, FusedArgs f) {
@@ -646,7 +703,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   const uint32_t hA = ((__popc(g & (2 * c4)) & 1) ? 0xBF80u : 0x3F80u) |
                       (((__popc(g & (2 * c4 + 1)) & 1) ? 0xBF80u : 0x3F80u) << 16);
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int n_units = my_tiles * PARTS;
+  const int n_units = META ? 0 : my_tiles * PARTS;  // key slabs this CTA streams for scoring
   // Queries staged in shared memory when they fit (decode), so the tile
   // epilogue never waits on global memory.
   const size_t q_elems = a.q ? (size_t)(n_tiles / (a.H * a.nb)) * a.Sq * a.Hq * D : 0;
@@ -721,6 +778,17 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
       }
       asm volatile("bar.sync 1, %0;" ::"r"(NE * 32) : "memory");
     }
+    // This warp's tiles are e, e + NE, ...; with META the decisions of the
+    // first 32 are made before the wait for the previous kernel (the
+    // metadata and the queries are inputs), lane i holding tile i's.
+    int meta_kp = 0;
+    if constexpr (META) {
+      const int n_mine_tiles = e < my_tiles ? (my_tiles - 1 - e) / NE + 1 : 0;
+      for (int i = 0; i < min(n_mine_tiles, 32); ++i) {
+        const int kp = meta_keep<D>(a, e + i * NE, q_cached, s_q, s_qn, lane);
+        if (lane == i) meta_kp = kp;
+      }
+    }
     // Outputs and the workspace are written from here on.
     pdl_wait();
     if constexpr (FUSED) {
@@ -739,6 +807,46 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
       }
       if (e == 0 && lane == 0) mbar_arrive(&setbar);  // the compute warps may read s_set
     }
+    if constexpr (META) {
+      // Decisions from write-time metadata, 32 tiles at a time: lane i
+      // counts tile i's head in (the atomics of the 32 tiles in flight
+      // together); the last head of a block publishes it as in the key path.
+      const int n_mine_tiles = e < my_tiles ? (my_tiles - 1 - e) / NE + 1 : 0;
+      for (int c0 = 0; c0 < n_mine_tiles; c0 += 32) {
+        if (c0 > 0)
+          for (int i = 0; i < min(n_mine_tiles - c0, 32); ++i) {
+            const int kp = meta_keep<D>(a, e + (c0 + i) * NE, q_cached, s_q, s_qn, lane);
+            if (lane == i) meta_kp = kp;
+          }
+        int row_done = 0, b = 0;
+        if (c0 + lane < n_mine_tiles) {
+          const int t = blockIdx.x + (e + (c0 + lane) * NE) * gridDim.x;
+          const int h = t % a.H;
+          const int j = (t / a.H) % a.nb;
+          b = t / (a.H * a.nb);
+          const int kp = meta_kp;
+          if (a.keep) a.keep[((size_t)b * a.nb + j) * a.H + h] = (uint8_t)kp;
+          const int bj = b * a.nb + j;
+          const int old = atomicAdd(fs.blk_state + bj, 1 + (kp << 16));
+          if ((old & 0xffff) == a.H - 1) {
+            const bool kept = (old >> 16) + kp > 0;
+            const int rw = atom_add_acq_rel(fs.row + b, kept ? 0x10001 : 1);
+            if (kept) st_release(fs.queue + (size_t)b * a.nb + (rw >> 16), j + 1);
+            row_done = (rw & 0xffff) == a.nb - 1;
+          }
+        }
+        for (unsigned m = __ballot_sync(0xffffffffu, row_done); m; m &= m - 1) {
+          const int bb = __shfl_sync(0xffffffffu, b, __ffs(m) - 1);
+          fused_write_perm(fs.blk_state + (size_t)bb * a.nb, a.nb, f.perm + (size_t)bb * a.nb, f.count + bb, lane);
+          __syncwarp();
+          if (lane == 0) {
+            __threadfence();
+            if (atom_add_acq_rel(fs.decided_all, 1) == f.B - 1) atomicAdd(f.epoch, 1);
+          }
+        }
+        __syncwarp();
+      }
+    } else
     for (int tile = e; tile < my_tiles; tile += NE) {
       const int tb = e;
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[tb], (tile / NE) & 1))) {
@@ -973,7 +1081,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   // bank groups.  Lane (matrix lane / 8, row lane % 8) addresses:
   const uint32_t lane_off = (uint32_t)hb * (kSlabB / 2) + (uint32_t)((lane >> 3) * 8 + (lane & 7)) * 128 +
                             (uint32_t)((ch ^ (lane & 7)) << 4);
-  for (int tile = 0; tile < my_tiles; ++tile) {
+  for (int tile = 0; tile < (META ? 0 : my_tiles); ++tile) {
     const int tb = tile % NBUF;
     if (tile >= NBUF && !__all_sync(0xffffffffu, mbar_wait(&tempty[tb], (tile / NBUF - 1) & 1))) {
       s_abort = 1;
@@ -1498,9 +1606,101 @@ int launch_score(const ScoreArgs& a, int mode, int ncta, cudaStream_t st) {
   return check_launch("score_full_kernel");
 }
 
+// Host side of the fused decode layer, one instantiation per kernel form
+// (the key-scoring one here, the metadata one in oc_score_meta.cu, so that
+// neither form's code generation depends on the other's).
+template <bool META>
+int decode_fused_impl(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
+                 int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
+                 void* out, int out_dtype, float* pm, float* pl, float* po, void* ws, size_t ws_bytes,
+                 cudaStream_t st, const PeerXchg* px, const float* meta_dc, const float* meta_eac,
+                 const float* meta_zeta) {
+  if (head_dim != 128 || !q || q_len < 1 || kv_heads < 1 || q_heads % kv_heads) return OC_ERR_UNSUPPORTED;
+  const int G = q_heads / kv_heads, R = q_len * G, nb = seq_len / kBlock;
+  // Counts share an int32 with 16 bits each (blk_state, the row word): at
+  // most 32767 blocks per row and 32767 KV heads keep them non-negative.
+  if (R > kFusedMaxRows || nb < 1 || nb > 0x7fff || kv_heads > 0x7fff) return OC_ERR_UNSUPPORTED;
+  if (out_dtype != OC_BF16 && out_dtype != OC_F32) return OC_ERR_UNSUPPORTED;
+  const FusedLayout L = fused_layout(batch, nb, kv_heads);
+  const int64_t ntiles = (int64_t)batch * nb * kv_heads;
+  if (ntiles >= (1ll << 31)) return OC_ERR_UNSUPPORTED;
+  int grid = device_sm_count();
+  if (grid > kFusedMaxGrid) grid = kFusedMaxGrid;
+  if (ntiles < grid) grid = (int)ntiles;
+  if (L.NG > grid || !ws || ws_bytes < L.bytes) return OC_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (reinterpret_cast<uintptr_t>(ws) & 255))
+    return OC_ERR_UNSUPPORTED;
+
+  ScoreArgs a = {};
+  a.keys = k; a.q = q; a.S = seq_len; a.H = kv_heads; a.D = head_dim; a.nb = nb;
+  a.Sq = q_len; a.Hq = q_heads; a.G = G;
+  a.bands = Bands{{1, 64, 256}, {64, 256, kBlock}};
+  a.tau = tau; a.zeta_max = zeta_max; a.keep = keep;
+  FusedArgs f = {};
+  f.epoch = reinterpret_cast<int*>(ws);
+  f.sets = f.epoch + 1;
+  f.set_ints = L.set_ints;
+  float* pf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + L.counters);
+  const size_t parts = (size_t)L.NG * L.cpg * kFusedMaxRows;
+  f.part_m = pf; f.part_l = pf + parts; f.part_o = pf + 2 * parts;
+  f.out = out; f.out_bf16 = out_dtype == OC_BF16;
+  f.pm = pm; f.pl = pl; f.po = po;
+  f.perm = perm; f.count = count;
+  f.B = batch; f.NG = L.NG; f.cpg = L.cpg; f.R = R;
+  f.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  if (px) f.px = *px;
+  // Decisions from write-time metadata: all three arrays.
+  if (META && (!meta_dc || !meta_eac || !meta_zeta)) return OC_ERR_NULL;
+  if (META) {
+    a.dc = const_cast<float*>(meta_dc);
+    a.e_ac = const_cast<float*>(meta_eac);
+    a.zeta = const_cast<float*>(meta_zeta);
+  }
+
+  CUtensorMap km, ak, av;
+  const uint64_t cols = (uint64_t)kv_heads * 128, rows = (uint64_t)batch * seq_len;
+  int rc = 0;
+  const uint64_t kk[4] = {1, (uint64_t)k, (uint64_t)kv_heads | (128ull << 32), rows};
+  const uint64_t ka[4] = {2, (uint64_t)k, cols, rows};
+  const uint64_t kv[4] = {2, (uint64_t)v, cols, rows};
+  if (!map_cache_get(kk, &km) && !(rc = encode_score_map(&km, k, kv_heads, 128, (int64_t)batch * nb)))
+    map_cache_put(kk, km);
+  if (!rc && !map_cache_get(ka, &ak) &&
+      !(rc = encode_map_2d(&ak, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true)))
+    map_cache_put(ka, ak);
+  if (!rc && !map_cache_get(kv, &av) &&
+      !(rc = encode_map_2d(&av, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true)))
+    map_cache_put(kv, av);
+  if (rc) return set_error(OC_ERR_CUDA, "oc_decode_step: tensor map encode failed (%d)", rc);
+  const int smem = kStages * kSlabB + kQCacheBytes + 1024;
+  // Once per device: the shared-memory opt-in, and the check that a CTA of
+  // this size fits on every SM (the persistent grid relies on all its CTAs
+  // being resident at once; with less room the separate kernels run instead).
+  auto kern = score_tma_kernel<128, true, META>;
+  static std::atomic<uint64_t> s_setup{0}, s_fits{0};
+  if (first_on_device(s_setup)) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int per_sm = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFusedThreads, smem) == cudaSuccess &&
+        per_sm >= 1 && dev < kMaxCachedDevices)
+      s_fits.fetch_or(1ull << dev);
+  }
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= kMaxCachedDevices || !(s_fits.load() & (1ull << dev))) return OC_ERR_UNSUPPORTED;
+  }
+  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kFusedThreads), smem, st, km, ak, av, a, (int)ntiles, f);
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "score_tma_kernel (fused): %s", cudaGetErrorString(e));
+  return check_launch("score_tma_kernel (fused)");
+}
+
 }  // namespace
 }  // namespace oc
 
+#ifndef OC_SCORE_META_TU
 using namespace oc;
 
 extern "C" int oc_fwht512(const void* x, int x_dtype, int64_t ncols, float* y, oc_stream_t stream) {
@@ -1882,8 +2082,12 @@ extern "C" int oc_score_from_metadata_paged(const float* dc_pool, const float* e
 }
 
 namespace oc {
-int wait_limit_score(unsigned long long ns) { return set_wait_limit_here(ns); }
+int wait_limit_score(unsigned long long ns) {
+  const int rc = set_wait_limit_here(ns);
+  return rc ? rc : wait_limit_score_meta(ns);
+}
 int score_status(int* status, int reset) {
+  // this unit's flag, or'ed with the metadata form's (oc_score_meta.cu)
   cudaError_t e = cudaMemcpyFromSymbol(status, g_score_status, sizeof(int));
   if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
   if (reset) {
@@ -1891,6 +2095,10 @@ int score_status(int* status, int reset) {
     e = cudaMemcpyToSymbol(g_score_status, &zero, sizeof(int));
     if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
   }
+  int meta = 0;
+  const int rc = score_status_meta(&meta, reset);
+  if (rc) return rc;
+  *status |= meta;
   return OC_OK;
 }
 }  // namespace oc
@@ -1917,81 +2125,45 @@ size_t decode_fused_bytes(int batch, int seq_len, int kv_heads) {
 int decode_fused(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
                  int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm, int32_t* count,
                  void* out, int out_dtype, float* pm, float* pl, float* po, void* ws, size_t ws_bytes,
-                 cudaStream_t st, const PeerXchg* px) {
-  if (head_dim != 128 || !q || q_len < 1 || kv_heads < 1 || q_heads % kv_heads) return OC_ERR_UNSUPPORTED;
-  const int G = q_heads / kv_heads, R = q_len * G, nb = seq_len / kBlock;
-  // Counts share an int32 with 16 bits each (blk_state, the row word): at
-  // most 32767 blocks per row and 32767 KV heads keep them non-negative.
-  if (R > kFusedMaxRows || nb < 1 || nb > 0x7fff || kv_heads > 0x7fff) return OC_ERR_UNSUPPORTED;
-  if (out_dtype != OC_BF16 && out_dtype != OC_F32) return OC_ERR_UNSUPPORTED;
-  const FusedLayout L = fused_layout(batch, nb, kv_heads);
-  const int64_t ntiles = (int64_t)batch * nb * kv_heads;
-  if (ntiles >= (1ll << 31)) return OC_ERR_UNSUPPORTED;
-  int grid = device_sm_count();
-  if (grid > kFusedMaxGrid) grid = kFusedMaxGrid;
-  if (ntiles < grid) grid = (int)ntiles;
-  if (L.NG > grid || !ws || ws_bytes < L.bytes) return OC_ERR_UNSUPPORTED;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (reinterpret_cast<uintptr_t>(ws) & 255))
-    return OC_ERR_UNSUPPORTED;
-
-  ScoreArgs a = {};
-  a.keys = k; a.q = q; a.S = seq_len; a.H = kv_heads; a.D = head_dim; a.nb = nb;
-  a.Sq = q_len; a.Hq = q_heads; a.G = G;
-  a.bands = Bands{{1, 64, 256}, {64, 256, kBlock}};
-  a.tau = tau; a.zeta_max = zeta_max; a.keep = keep;
-  FusedArgs f = {};
-  f.epoch = reinterpret_cast<int*>(ws);
-  f.sets = f.epoch + 1;
-  f.set_ints = L.set_ints;
-  float* pf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + L.counters);
-  const size_t parts = (size_t)L.NG * L.cpg * kFusedMaxRows;
-  f.part_m = pf; f.part_l = pf + parts; f.part_o = pf + 2 * parts;
-  f.out = out; f.out_bf16 = out_dtype == OC_BF16;
-  f.pm = pm; f.pl = pl; f.po = po;
-  f.perm = perm; f.count = count;
-  f.B = batch; f.NG = L.NG; f.cpg = L.cpg; f.R = R;
-  f.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
-  if (px) f.px = *px;
-
-  CUtensorMap km, ak, av;
-  const uint64_t cols = (uint64_t)kv_heads * 128, rows = (uint64_t)batch * seq_len;
-  int rc = 0;
-  const uint64_t kk[4] = {1, (uint64_t)k, (uint64_t)kv_heads | (128ull << 32), rows};
-  const uint64_t ka[4] = {2, (uint64_t)k, cols, rows};
-  const uint64_t kv[4] = {2, (uint64_t)v, cols, rows};
-  if (!map_cache_get(kk, &km) && !(rc = encode_score_map(&km, k, kv_heads, 128, (int64_t)batch * nb)))
-    map_cache_put(kk, km);
-  if (!rc && !map_cache_get(ka, &ak) &&
-      !(rc = encode_map_2d(&ak, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true)))
-    map_cache_put(ka, ak);
-  if (!rc && !map_cache_get(kv, &av) &&
-      !(rc = encode_map_2d(&av, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, kFusedChunk, true)))
-    map_cache_put(kv, av);
-  if (rc) return set_error(OC_ERR_CUDA, "oc_decode_step: tensor map encode failed (%d)", rc);
-  const int smem = kStages * kSlabB + kQCacheBytes + 1024;
-  // Once per device: the shared-memory opt-in, and the check that a CTA of
-  // this size fits on every SM (the persistent grid relies on all its CTAs
-  // being resident at once; with less room the separate kernels run instead).
-  static std::atomic<uint64_t> s_setup{0}, s_fits{0};
-  if (first_on_device(s_setup)) {
-    cudaFuncSetAttribute(score_tma_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    int per_sm = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, score_tma_kernel<128, true>, kFusedThreads, smem) ==
-            cudaSuccess &&
-        per_sm >= 1 && dev < kMaxCachedDevices)
-      s_fits.fetch_or(1ull << dev);
-  }
-  {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= kMaxCachedDevices || !(s_fits.load() & (1ull << dev))) return OC_ERR_UNSUPPORTED;
-  }
-  const cudaError_t e = launch_pdl(score_tma_kernel<128, true>, dim3(grid), dim3(kFusedThreads), smem, st, km, ak,
-                                   av, a, (int)ntiles, f);
-  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "score_tma_kernel (fused): %s", cudaGetErrorString(e));
-  return check_launch("score_tma_kernel (fused)");
+                 cudaStream_t st, const PeerXchg* px, const float* meta_dc, const float* meta_eac,
+                 const float* meta_zeta) {
+  if (meta_dc || meta_eac || meta_zeta)
+    return decode_fused_meta(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max, keep, perm,
+                             count, out, out_dtype, pm, pl, po, ws, ws_bytes, st, px, meta_dc, meta_eac, meta_zeta);
+  return decode_fused_impl<false>(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max, keep,
+                                  perm, count, out, out_dtype, pm, pl, po, ws, ws_bytes, st, px, nullptr, nullptr,
+                                  nullptr);
 }
 
 }  // namespace oc
+#else  // OC_SCORE_META_TU: the metadata form of the fused layer only
+
+namespace oc {
+int decode_fused_meta(const void* q, const void* k, const void* v, int batch, int q_len, int q_heads, int kv_heads,
+                      int head_dim, int seq_len, float tau, float zeta_max, uint8_t* keep, int32_t* perm,
+                      int32_t* count, void* out, int out_dtype, float* pm, float* pl, float* po, void* ws,
+                      size_t ws_bytes, cudaStream_t st, const PeerXchg* px, const float* meta_dc,
+                      const float* meta_eac, const float* meta_zeta) {
+  return decode_fused_impl<true>(q, k, v, batch, q_len, q_heads, kv_heads, head_dim, seq_len, tau, zeta_max, keep,
+                                 perm, count, out, out_dtype, pm, pl, po, ws, ws_bytes, st, px, meta_dc, meta_eac,
+                                 meta_zeta);
+}
+int wait_limit_score_meta(unsigned long long ns) { return set_wait_limit_here(ns); }
+int score_status_meta(int* status, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_score_status, sizeof(int));
+  if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_score_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_device_status: %s", cudaGetErrorString(e));
+  }
+  return OC_OK;
+}
+}  // namespace oc
+
+#ifdef OC_TIMING
+extern "C" int oc_probe_read_score_stamps_meta(unsigned long long* host, int n) {
+  return (int)cudaMemcpyFromSymbol(host, oc::g_sstamp, sizeof(unsigned long long) * 24 * n);
+}
+#endif
+#endif  // OC_SCORE_META_TU
