@@ -303,7 +303,7 @@ __device__ __forceinline__ f32x2 fmul2(f32x2 a, f32x2 b) {
 
 constexpr int kVThreads = 512;
 constexpr int kVWarps = kVThreads / 32;
-constexpr int kVStages = 4;
+constexpr int kVStages = 5;
 constexpr int kVStageBytes = 32768;  // K + V of one item: 2 * CH * D * 2 with CH * D = 8192
 
 __device__ int g_attn_status = 0;
@@ -451,6 +451,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
   __shared__ int s_rel[kVStages];
   __shared__ volatile int s_abort;
   __shared__ int s_blk[kBlkCache];
+  __shared__ int s_sblk[kVStages];  // block index of the item in each stage (set when it is issued)
   __shared__ float s_wm[kVWarps][RT], s_wl[kVWarps][RT];
   __shared__ float s_wo[kVWarps][RT][D];
   __shared__ int s_pre[kMaxLists + 1];
@@ -482,6 +483,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     const int y = (blk < 0 || blk >= a.nblk) ? pos.b * a.kv_rows : pos.b * a.kv_rows + blk * a.bs + c * CH;
     uint8_t* dst = smem + (size_t)(k % kVStages) * kVStageBytes;
     uint64_t* bar = &full[k % kVStages];
+    s_sblk[k % kVStages] = blk;  // published to the consumers by the arrive below
     mbar_expect_tx(bar, 2 * KB);
     tma_load_2d(dst, &kmap, bar, pos.h * D, y);
     tma_load_2d(dst + KB, &vmap, bar, pos.h * D, y);
@@ -590,8 +592,7 @@ attn_stream_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
       s_abort = 1;
       if (lane == 0) atomicExch(&g_attn_status, 1);
     }
-    const int slot = item / a.chunks;
-    const int blk = a.idx[(size_t)b * a.idx_stride + (size_t)h * a.idx_hstride + slot];
+    const int blk = s_sblk[stage];
     const bool valid = !s_abort && blk >= 0 && blk < a.nblk;
     const uint8_t* ks = smem + (size_t)stage * kVStageBytes;
     const uint8_t* vs = ks + KB;
@@ -784,15 +785,28 @@ __device__ void lists_from_keep(AttnArgs& a, int* s_list, int* s_cnt, int* s_sca
   a.cnt_hstride = 0;
 }
 
+// Warps of the tensor-core stream kernel: (8192 / D) / 16 token groups of 16
+// tokens, times the output-channel slices of at most 128 channels (two at
+// D = 256: both warps of a token group compute its logits, each accumulates
+// half of the output channels).
+template <int D>
+constexpr int mma_threads() {
+  return 32 * ((8192 / D) / 16) * (D > 128 ? D / 128 : 1);
+}
+
 template <int D, int RT>
-__global__ void __launch_bounds__(32 * (8192 / D) / 16, 2)
+__global__ void __launch_bounds__(mma_threads<D>(), 2)
 attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a_in) {
   constexpr int CH = 8192 / D;           // tokens per item
-  constexpr int NW = CH / 16;            // warps: 16 tokens each
+  constexpr int NTG = CH / 16;           // token groups of 16
+  constexpr int CS = D > 128 ? D / 128 : 1;  // output-channel slices
+  constexpr int DO = D / CS;             // output channels per warp
+  constexpr int NW = NTG * CS;           // warps
   constexpr int NT = 32 * NW;
   constexpr int KS = D / 16;             // k-steps of S = Q K^T
-  constexpr int NO = D / 8;              // n-tiles of O
+  constexpr int NO = DO / 8;             // n-tiles of this warp's O
   constexpr int KB = CH * D * 2;         // bytes of the K (or V) half of a stage
+  static_assert(NT == mma_threads<D>(), "warp layout");
   static_assert(RT == 4 || RT == 8, "row tile");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -801,12 +815,13 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
   __shared__ volatile int s_abort;
   __shared__ int s_blk[kBlkCache];
   __shared__ float s_wm[NW][RT], s_wl[NW][RT];
-  __shared__ float s_wo[NW][RT][D];
+  __shared__ float s_wo[NW][RT][DO];
   __shared__ int s_pre[kMaxLists + 1];
   __shared__ int s_wsum[NW];
 
   OC_STAMP(0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tg = warp % NTG, cs = warp / NTG;  // token group, output-channel slice
   const int g = lane >> 2, c = lane & 3;  // MMA fragment coordinates
   if (tid == 0) {
     for (int i = 0; i < kMStages; ++i) { mbar_init(&full[i], 1); s_rel[i] = 0; }
@@ -898,15 +913,17 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     const size_t stride = (size_t)a.Hkv * a.R;
     const size_t p0 = ((size_t)cur_b * a.max_items * a.Hkv + cur_h) * a.R + r0;  // item 0, row r0
     for (int x = tid; x < nr * D; x += NT) {
-      const int r = x / D, d = x - r * D;
+      // channel d of row r: the token groups' states of its slice (the
+      // slices of a token group hold the same m and l)
+      const int r = x / D, d = x - r * D, w0 = (d / DO) * NTG, dl = d % DO;
       float M = -INFINITY;
-      for (int w = 0; w < NW; ++w) M = fmaxf(M, s_wm[w][r]);
+      for (int t = 0; t < NTG; ++t) M = fmaxf(M, s_wm[w0 + t][r]);
       float L = 0.f, O = 0.f;
       if (M != -INFINITY)
-        for (int w = 0; w < NW; ++w) {
-          const float f = exp2f(s_wm[w][r] - M);
-          L = fmaf(s_wl[w][r], f, L);
-          O = fmaf(s_wo[w][r][d], f, O);
+        for (int t = 0; t < NTG; ++t) {
+          const float f = exp2f(s_wm[w0 + t][r] - M);
+          L = fmaf(s_wl[w0 + t][r], f, L);
+          O = fmaf(s_wo[w0 + t][r][dl], f, O);
         }
       const size_t pr = p0 + (size_t)run_first * stride + r;
       a.ws_o[pr * D + d] = O;
@@ -959,34 +976,57 @@ attn_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     const bool valid = !s_abort && blk >= 0 && blk < a.nblk;
     const uint32_t ks_base = smem_u32(smem + (size_t)stage * kMStageBytes);
     const uint32_t vs_base = ks_base + KB;
-    // All fragments of this warp's 16 tokens, then the stage is released.
-    uint32_t kb[KS][4], vb[NO / 2][4];
-    {
-      const int mm = lane >> 3, rr = lane & 7;
+    float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int mm = lane >> 3, rr = lane & 7;
+    uint32_t vb[NO / 2][4];
+    if constexpr (CS == 1) {
+      // All fragments of this warp's 16 tokens, then the stage is released.
+      uint32_t kb[KS][4];
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks)  // matrices: (tokens 0-7 | 8-15) x (channels 16ks..+8 | +8..+16)
-        ldsm_x4(kb[ks], ks_base + swz<CH>(16 * warp + 8 * (mm >> 1) + rr, 2 * ks + (mm & 1)));
+        ldsm_x4(kb[ks], ks_base + swz<CH>(16 * tg + 8 * (mm >> 1) + rr, 2 * ks + (mm & 1)));
 #pragma unroll
       for (int np2 = 0; np2 < NO / 2; ++np2)  // matrices: (tokens 0-7 | 8-15) x (channel tiles 2np2 | 2np2+1)
-        ldsm_x4_t(vb[np2], vs_base + swz<CH>(16 * warp + 8 * (mm & 1) + rr, 2 * np2 + (mm >> 1)));
-    }
-    __syncwarp();
-    if (lane == 0 && atomicAdd(&s_rel[stage], 1) == NW - 1) {
-      s_rel[stage] = 0;
-      if (k + kMStages < n_mine && !s_abort) {
-        fence_proxy_async();
-        issue(k + kMStages, ahead);
+        ldsm_x4_t(vb[np2], vs_base + swz<CH>(16 * tg + 8 * (mm & 1) + rr, 2 * np2 + (mm >> 1)));
+      __syncwarp();
+      if (lane == 0 && atomicAdd(&s_rel[stage], 1) == NW - 1) {
+        s_rel[stage] = 0;
+        if (k + kMStages < n_mine && !s_abort) {
+          fence_proxy_async();
+          issue(k + kMStages, ahead);
+        }
       }
-    }
-    ahead.next(a);
-    if (!valid) continue;
-
-    // S = Q K^T for the two 8-token tiles (rows g, g+8; tokens 2c, 2c+1)
-    float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      ahead.next(a);
+      if (!valid) continue;
+      // S = Q K^T for the two 8-token tiles (rows g, g+8; tokens 2c, 2c+1)
 #pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {
-      mma_bf16_16816(sa[0], qa[ks], kb[ks][0], kb[ks][1]);
-      mma_bf16_16816(sa[1], qa[ks], kb[ks][2], kb[ks][3]);
+      for (int ks = 0; ks < KS; ++ks) {
+        mma_bf16_16816(sa[0], qa[ks], kb[ks][0], kb[ks][1]);
+        mma_bf16_16816(sa[1], qa[ks], kb[ks][2], kb[ks][3]);
+      }
+    } else {
+      // Wide heads: the logits k-step by k-step (K fragments are not all
+      // held at once), then this slice's V fragments, then the release.
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t kb[4];
+        ldsm_x4(kb, ks_base + swz<CH>(16 * tg + 8 * (mm >> 1) + rr, 2 * ks + (mm & 1)));
+        mma_bf16_16816(sa[0], qa[ks], kb[0], kb[1]);
+        mma_bf16_16816(sa[1], qa[ks], kb[2], kb[3]);
+      }
+#pragma unroll
+      for (int np2 = 0; np2 < NO / 2; ++np2)
+        ldsm_x4_t(vb[np2], vs_base + swz<CH>(16 * tg + 8 * (mm & 1) + rr, cs * NO + 2 * np2 + (mm >> 1)));
+      __syncwarp();
+      if (lane == 0 && atomicAdd(&s_rel[stage], 1) == NW - 1) {
+        s_rel[stage] = 0;
+        if (k + kMStages < n_mine && !s_abort) {
+          fence_proxy_async();
+          issue(k + kMStages, ahead);
+        }
+      }
+      ahead.next(a);
+      if (!valid) continue;
     }
     // online softmax in log2 units
 #pragma unroll
@@ -1039,7 +1079,7 @@ int keep_list_bytes(int B, int nb) { return ((B * nb + B) * 4 + 15) / 16 * 16; }
 template <int D>
 int launch_attn_mma(const AttnArgs& a, int rt, cudaStream_t st) {
   constexpr int CH = 8192 / D;
-  constexpr int NT = 32 * CH / 16;
+  constexpr int NT = mma_threads<D>();
   CUtensorMap km, vm;
   const uint64_t cols = (uint64_t)a.Hkv * D, rows = a.kv_rows ? (uint64_t)a.B * a.kv_rows : (uint64_t)a.nblk * a.bs;
   int rc = encode_map_2d(&km, a.k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, 64, CH, true);
@@ -1328,7 +1368,7 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
   a.nblk = pool_pages > 0 ? pool_pages : S / bs;
   a.R = Sq * a.G;
   const bool tma = use_tma_path(dtype, bs, D, (int64_t)B * Hkv);
-  const bool mma = tma && (D == 64 || D == 128);  // tensor-core stream kernel
+  const bool mma = tma && (D == 64 || D == 128 || D == 256);  // tensor-core stream kernel
   int rt = pick_rt(a.R, D);
   if (tma && rt * D > 512) rt = 512 / D;
   if (tma && rt > 4) rt = 4;
@@ -1358,7 +1398,9 @@ int run_attention(const void* q, const void* k, const void* v, int dtype, const 
 
   const bool stream_path = tma && max_blocks > 0;
   if (stream_path) {
-    rc = mma ? (D == 64 ? launch_attn_mma<64>(a, rt, st) : launch_attn_mma<128>(a, rt, st))
+    rc = mma ? (D == 64    ? launch_attn_mma<64>(a, rt, st)
+                : D == 128 ? launch_attn_mma<128>(a, rt, st)
+                           : launch_attn_mma<256>(a, rt, st))
              : launch_attn_stream<256>(a, rt, st);
     if (rc) return rc;
   } else if (max_blocks > 0) {
