@@ -1115,7 +1115,9 @@ def run_stack(args, rank, world, local_rank):
         "timed_region": "CUDA-graph replay of whole steps" if graph is not None else "eager steps",
         "cpu_baseline": None,
         "e2e": None,
-        "gpu_launches": K * (len(kinds) - n_glob + 3 * n_glob) * (1 if world == 1 else 2),
+        # per layer: attention (split-KV kernel + merge kernel), global layers
+        # also the scorer and the compaction; sharded, the cross-shard merge
+        "gpu_launches": K * ((len(kinds) - n_glob) * 2 + n_glob * 4 + (len(kinds) if world > 1 else 0)),
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
