@@ -12,6 +12,7 @@ E_AC (``spectral_energy.py:150-177``).  This module keeps the three, per
     cache = SpectralMetadataCache.from_keys(keys)        # one scorer pass
     cache.update_blocks(keys, first_block=j, num_blocks=1)   # block j rewritten
     keep, bound_max = cache.multiband_mask(q, tau, zeta_max)  # reads 0.5 MB, not |K|
+    out, keep, perm, count = cache.decode_step(q, keys, values, tau)  # gates + attention, one launch
 
 ``multiband_mask`` gives the same mask as ``compute_multiband_mask`` on the
 same keys (up to float32 summation order in the bound, as the fused scorer).
@@ -106,6 +107,42 @@ class SpectralMetadataCache:
             keep, bmax = keep[0], bmax[0]
             bounds = bounds[0] if bounds is not None else None
         return (keep, bmax, bounds) if want_bounds else (keep, bmax)
+
+    def decode_step(self, q, keys, values, tau, zeta_max=5.0, workspace=None):
+        """One decode step over the retained blocks with the gates from this
+        cache (``oc_decode_step_from_metadata``: one fused launch for bf16,
+        head_dim 128, <= 8 query rows per KV head; separate kernels
+        otherwise).  q (B, Sq, Hq, D); keys, values (B, S, H, D) of the same
+        dtype, S = num_blocks * 512.  ``workspace``: a uint8 device tensor
+        kept by the caller across steps (zero-filled once; allocated here when
+        None).  Returns out (B, Sq, Hq, D) bfloat16, keep (B, nb, H) bool,
+        perm (B, nb) and count (B) int32."""
+        k, v = _batched(keys), _batched(values)
+        qq = _lib.as_device(q, device=k.device)
+        if qq.dim() != 4:
+            raise ValueError(f"q must be (B, Sq, Hq, D), got {tuple(qq.shape)}")
+        qq = qq.to(k.dtype).contiguous()
+        B, Sq, Hq, D = qq.shape
+        _, S, H, _ = k.shape
+        if (B, H, D) != (self.batch, self.kv_heads, self.head_dim) or S != self.num_blocks * BLOCK or \
+                v.shape != k.shape or Hq % H:
+            raise ValueError(f"q {tuple(qq.shape)}, keys {tuple(k.shape)}, values {tuple(v.shape)} do not match "
+                             f"the cache")
+        nb = self.num_blocks
+        need = _lib.query("oc_decode_step_workspace_bytes", B, Sq, Hq, H, D, S)
+        if workspace is None:
+            workspace = torch.zeros((need,), dtype=torch.uint8, device=k.device)
+        elif workspace.numel() < need:
+            raise ValueError(f"workspace of {workspace.numel()} bytes, need {need}")
+        keep = torch.empty((B, nb, H), dtype=torch.uint8, device=k.device)
+        perm = torch.empty((B, nb), dtype=torch.int32, device=k.device)
+        count = torch.empty((B,), dtype=torch.int32, device=k.device)
+        out = torch.empty((B, Sq, Hq, D), dtype=torch.bfloat16, device=k.device)
+        _lib.call("oc_decode_step_from_metadata", _lib.ptr(qq), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(k),
+                  _lib.ptr(self.dc), _lib.ptr(self.e_ac), _lib.ptr(self.zeta), B, Sq, Hq, H, D, S, float(tau),
+                  float(zeta_max), _lib.ptr(keep), _lib.ptr(perm), _lib.ptr(count), _lib.ptr(out), 1,
+                  _lib.ptr(workspace), workspace.numel(), _lib.stream_ptr(k.device))
+        return out, keep.bool(), perm, count
 
 
 def _batched(keys):

@@ -106,3 +106,19 @@ def test_metadata_decode_separate_kernels_head_dim_64():
     assert int(count[0]) == rn and np.array_equal(host(perm[0]), rp)
     ref = O.indirect_attention(qf, kf, vf, rp, rn)
     np.testing.assert_allclose(host(out[0]).astype(np.float32), ref, rtol=ATT_RTOL, atol=ATT_ATOL)
+
+
+def test_metadata_cache_decode_step_python_api():
+    """SpectralMetadataCache.decode_step (the Python entry of the same
+    kernel) against the oracle, workspace reused across two steps."""
+    from orthocache_b200 import SpectralMetadataCache
+    B, nb, hq, hkv, sq = 2, 32, 32, 8, 1
+    q, k, v = make_batch(B, nb, hq, hkv, 128, sq, [0.75, 0.5], seed=900)
+    tau = tau_for(q[0], k[0], 0.75)
+    cache = SpectralMetadataCache.from_keys(k)
+    ws = workspace(B, sq, hq, hkv, 128, nb * 512)
+    for _ in range(2):
+        out, keep, perm, count = cache.decode_step(q, k, v, tau, ZMAX, workspace=ws)
+        torch.cuda.synchronize()
+        check_against_oracle(q, k, v, tau, keep, perm, count, out)
+    assert epoch(ws) == 2
