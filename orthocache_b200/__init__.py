@@ -27,6 +27,7 @@ from .indirect_attention import indirect_attention, compile_indirect_attention
 from .adaptive_attention import orthocache_attention, orthocache_attention_batched
 from .metadata_cache import SpectralMetadataCache
 from .paged import PagedKVCache
+from . import nvlink_model
 
 __all__ = [
     "fwht_512", "compute_block_energy_jax", "generate_threshold_mask", "compute_query_aware_bounds",
