@@ -28,8 +28,9 @@
 //     tcgen05.ld, keeps the running max and sum, writes P as bfloat16 pairs
 //     over the logits in tensor memory (tcgen05.st), and rescales O in tensor
 //     memory only when its row max grows by more than 2^8 (the stale max
-//     stays exact: the final o / l uses the same max for both); a quarter of
-//     the exponentials run as a polynomial on the FMA pipe to unload MUFU;
+//     stays exact: the final o / l uses the same max for both); one eighth
+//     of the exponentials run as a polynomial on the FMA pipe, the scaling,
+//     row sums and polynomial in paired (.f32x2) instructions;
 //   * the issue order per KV tile j is PV_0(j-1), S_0(j), PV_1(j-1), S_1(j):
 //     the commit that publishes S_t(j) also covers PV_t(j-1), so a softmax
 //     warpgroup that sees S_t(j) may rescale O_t and overwrite P_t, and
@@ -188,16 +189,63 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
       : "memory");
 }
 
-// 2^x on the FMA pipe, for the share of the exponentials taken off the MUFU
-// unit: x = n + f with n = floor(x), 2^f by the cubic through the four
-// Chebyshev nodes of [0, 1) (relative error < 1e-4, below the bfloat16
-// rounding that P gets), 2^n added to the exponent field.  x >= -127.
-__device__ __forceinline__ float poly_ex2(float x) {
-  x = fmaxf(x, -127.f);
-  const float n = floorf(x);
-  const float f = x - n;
-  const float p = fmaf(fmaf(fmaf(0.0789672570f, f, 0.2246931558f), f, 0.6963247711f), f, 0.9999002882f);
-  return __int_as_float(__float_as_int(p) + ((int)n << 23));
+// Paired fp32 arithmetic (sm_100a .f32x2 forms): one instruction for two
+// lanes of a float2, halving the issue slots of the softmax's FMA work.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// 2^x for a pair of values on the FMA pipe, for the share of the
+// exponentials taken off the MUFU unit.  x = n + f with n = floor(x) found
+// without a conversion instruction (those issue on the same narrow pipe as
+// MUFU): adding 1.5 * 2^23 with rounding toward -inf leaves floor(x) in the
+// low mantissa bits of t, and bits(t) << 23 is exactly n << 23 modulo 2^32.
+// 2^f on [0, 1) is the cubic through the four Chebyshev nodes of the
+// interval (relative error < 1e-4, below the bfloat16 rounding that P
+// gets); 2^n is added to the exponent field.  x is clamped to >= -126 so that
+// the exponent field never wraps (the result there is ~1e-38, i.e. zero).
+__device__ __forceinline__ void poly_ex2x2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t kMagic = f2_pack(12582912.f, 12582912.f);
+  const uint64_t x = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  uint64_t t, n, f;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(t) : "l"(x), "l"(kMagic));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(n) : "l"(t), "l"(kMagic));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(f) : "l"(x), "l"(n));
+  uint64_t p = f2_fma(f2_pack(0.0789672570f, 0.0789672570f), f, f2_pack(0.2246931558f, 0.2246931558f));
+  p = f2_fma(p, f, f2_pack(0.6963247711f, 0.6963247711f));
+  p = f2_fma(p, f, f2_pack(0.9999002882f, 0.9999002882f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __uint_as_float(__float_as_uint(t0) * (1u << 23) + __float_as_uint(p0));
+  y1 = __uint_as_float(__float_as_uint(t1) * (1u << 23) + __float_as_uint(p1));
+}
+
+// Chunks of 8 exponentials per 64 that run as poly_ex2x2: one in eight.
+// (Measured on config 2: shares of 0 and 1/8 are equally fast, 1/4 is 2 %
+// slower, 3/8 and 1/2 slower still, so MUFU is not what bounds the kernel.)
+__host__ __device__ constexpr bool poly_chunk(int c) { return c == 7; }
+
+// Three-input maximum (one instruction on sm_100a).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 __device__ __forceinline__ float fast_ex2(float x) {
@@ -312,20 +360,26 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
       s_ph ^= 1;
       tc_fence_after();
       // Row max over the 128 logits in two halves of 64 columns (the register
-      // budget is that of 3 warps per SM sub-partition); the first half stays
-      // in registers for its exponentials, the second is read again.
+      // budget is that of 3 warps per SM sub-partition, 168 registers); the
+      // first half (read second) stays in registers for its exponentials, the
+      // other is read again.
       float s[64];
       tmem_ld64_wait(t_s + 64, s);
       // Eight independent running maxima (a single chain of 128 dependent
       // max operations would sit on the critical path of every K/V tile).
       float m8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = s[i];
-#pragma unroll
-      for (int i = 8; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
+      for (int k = 0; k < 8; ++k) {
+        m8[k] = fmax3(s[k], s[8 + k], s[16 + k]);
+        m8[k] = fmax3(m8[k], s[24 + k], s[32 + k]);
+        m8[k] = fmax3(m8[k], s[40 + k], s[48 + k]);
+        m8[k] = fmaxf(m8[k], s[56 + k]);
+      }
       tmem_ld64_wait(t_s, s);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) m8[i & 7] = fmaxf(m8[i & 7], s[i]);
+      for (int i = 0; i < 64; i += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], s[i + k], s[i + 8 + k]);
       float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= a.scale_log2;
       const bool need = mx > m_used + 8.f;
@@ -349,29 +403,40 @@ __device__ void pf_softmax(PfSmem& sm, const PfArgs& a, int t, uint32_t tmem) {
       // memory (column c holds tokens 2c, 2c + 1), the A operand of P.V.
       // Tokens 0-63 go to columns 0-31, whose logits are already in
       // registers; tokens 64-127 to columns 32-63, after their logits (columns
-      // 64-127, untouched so far) have been read.  One chunk of 8 in 4 takes
-      // its exponentials on the FMA pipe.
-      float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums, as for the max
+      // 64-127, untouched so far) have been read.  One chunk of 8 in 8 takes
+      // its exponentials on the FMA pipe.  Independent partial sums (as for
+      // the max), four float2 pairs.
+      uint64_t r2[4] = {0, 0, 0, 0};
+      const uint64_t sc2 = f2_pack(a.scale_log2, a.scale_log2), nm2 = f2_pack(-m_used, -m_used);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         if (half == 1) tmem_ld64_wait(t_s + 64, s);
         uint32_t pk[32];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          float p[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float x = fmaf(s[8 * c + i], a.scale_log2, -m_used);
-            p[i] = (c & 3) == 3 ? poly_ex2(x) : fast_ex2(x);
-            r8[i] += p[i];
+          for (int i = 0; i < 4; ++i) {
+            float x0, x1, p0, p1;
+            f2_unpack(f2_fma(f2_pack(s[8 * c + 2 * i], s[8 * c + 2 * i + 1]), sc2, nm2), x0, x1);
+            if (poly_chunk(c)) {
+              poly_ex2x2(x0, x1, p0, p1);
+            } else {
+              p0 = fast_ex2(x0);
+              p1 = fast_ex2(x1);
+            }
+            r2[i] = f2_add(r2[i], f2_pack(p0, p1));
+            pk[4 * c + i] = pack_bf16x2(p0, p1);
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) pk[4 * c + i] = pack_bf16x2(p[2 * i], p[2 * i + 1]);
         }
         tmem_st32u(t_s + 32 * half, pk);
       }
       tc_wait_st();  // P and any rescaled O are in tensor memory
-      l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
+      {
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f2_unpack(r2[i], r[2 * i], r[2 * i + 1]);
+        l += ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+      }
       tc_fence_before();
       mbar_arrive(&sm.p_full[t]);
     }

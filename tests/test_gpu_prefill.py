@@ -146,6 +146,22 @@ def test_prefill_large_logits_rescale():
     np.testing.assert_allclose(out[0], ref, rtol=ATT_RTOL, atol=ATT_ATOL)
 
 
+def test_prefill_wide_logit_range():
+    """Logits spread over hundreds of log2 units below the row max: the
+    exponentials computed on the FMA pipe must flush to zero there, never
+    wrap the exponent field into a NaN or a large value."""
+    B, Sq, Hq, Hkv, nb, bs = 1, 256, 2, 1, 4, 512
+    q, k, v = _inputs(23, B, Sq, Hq, Hkv, nb * bs)
+    q = (q.float() * 64).bfloat16()
+    k = (k.float() * 8).bfloat16()
+    idx = torch.tensor([[2, 0, 3, 1]], dtype=torch.int32, device="cuda")
+    cnt = torch.tensor([4], dtype=torch.int32, device="cuda")
+    out = _run(q, k, v, idx, cnt, bs, nb).float().cpu().numpy()
+    assert np.isfinite(out).all()
+    ref = _oracle(q[0], k[0], v[0], [2, 0, 3, 1], 4, bs)
+    np.testing.assert_allclose(out[0], ref, rtol=ATT_RTOL, atol=ATT_ATOL)
+
+
 def test_prefill_config2_full_size():
     """Configuration 2 end to end at full size: keys of the 30/40/30 smooth /
     mid-band / noise mixture, the fused scorer's two-gate mask per batch row
