@@ -1,264 +1,32 @@
-"""Sequence-parallel exchange and attention over ``torch.distributed``.
+"""Sequence-parallel exchanges and attention through the C ABI over an NCCL
+communicator (``orthocache_b200.comm.NcclComm``), and the one-kernel sharded
+decode layer (``ShardedDecoder``).
 
-Drop-in counterparts of the reference's multi-device path (j-arndt/orthocache
-v0.3.0):
-
-  ``alltoallv.py``             stream_compact :44-75, count_sync :80-108,
-                               compute_offsets :113-145, pack_active_blocks
-                               :150-212, alltoallv_exchange :217-259,
-                               unpack_received_blocks :264-335,
-                               alltoallv_kv_exchange :340-440
-  ``distributed_attention.py`` distributed_orthocache_attention :131-195,
-                               ici_data_volume :198-223
-  ``benchmarks/phase_e_stratified.py``  build_stratified :164-273
-
-The reference's ``axis_name`` (a pmap axis) becomes a ``torch.distributed``
-process group: NCCL between GPUs (one process per GPU), gloo for host-side
-tests.  Block data moves only through the CUDA kernels of
-``liborthocache_b200.so`` (block gather, exchange index, attention, merge);
-the collectives are ``torch.distributed`` calls; the only host-side
-arithmetic is on the P per-device counts.
-
-Exchange semantics.  ``alltoallv_exchange`` returns every device's packed
-buffer concatenated in rank order (the (P * max_tokens, H, D) layout that
-``unpack_received_blocks`` and the reference's docstring describe), i.e. an
-all-gather of the packed buffers.
-
-Three ways to run attention across P sequence shards are provided:
-``distributed_orthocache_attention`` (the reference's replicated gather of
-the packed K/V), ``stratified_allgather_attention`` (``build_stratified``:
-the gather sized to the smallest capacity bucket that holds the largest
-count) and ``sequence_parallel_attention`` (no K/V movement: each rank
-attends to its own retained blocks and the per-row (m, l, o) partials are
-merged in log-sum-exp form after an all-gather of P * rows * (D + 2)
-floats).  All three give the attention of the query over the union of the
-retained blocks of all shards.
+The reference-named drop-ins live in their module twins and are re-exported
+here: :mod:`orthocache_b200.alltoallv` (``alltoallv.py``: count sync,
+offsets, pack, exchange, unpack) and :mod:`orthocache_b200.distributed_attention`
+(``distributed_attention.py``, ``benchmarks/phase_e_stratified.py``).  This
+module adds what the reference has no entry point for: the stratified
+exchange and the per-peer AllToAllv by KV head as single C-ABI calls
+(``oc_exchange_stratified``, ``oc_alltoallv_heads``), attention partitioned
+by KV head, and the sharded decode layer whose partials cross NVLink inside
+the kernel.
 """
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
+import torch.distributed as dist  # noqa: F401
 
 from . import _lib
 from . import _core
-
-BLOCK_SIZE = 512
-
-
-# ---------------------------------------------------------------------------
-# collectives (any device: NCCL for CUDA tensors, gloo for CPU tensors)
-# ---------------------------------------------------------------------------
-def _world(group):
-    return dist.get_world_size(group)
-
-
-def _all_gather_cat(t, group=None):
-    """Concatenate every rank's ``t`` along dim 0, in rank order."""
-    t = t.contiguous()
-    P = _world(group)
-    out = torch.empty((P * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-    if t.is_cuda:
-        dist.all_gather_into_tensor(out, t, group=group)
-    else:
-        dist.all_gather(list(out.chunk(P, dim=0)), t, group=group)
-    return out
-
-
-# ---------------------------------------------------------------------------
-# a9 (mask only), a15: compaction, count sync, offsets
-# ---------------------------------------------------------------------------
-def stream_compact(block_mask):
-    """(active_indices int32 (nb,), num_active int32 (1,)) of a (nb,) or
-    (nb, H) block mask (``alltoallv.py:44-75``; union over H)."""
-    perm, count = _core.compact(block_mask)
-    return perm[0], count
-
-
-def count_sync(local_num_active, group=None):
-    """Every rank's active-block count, int32 (P,) (``alltoallv.py:80-108``)."""
-    c = torch.as_tensor(local_num_active).reshape(1).to(torch.int32)
-    return _all_gather_cat(c, group)
-
-
-def compute_offsets(all_counts):
-    """(offsets (P,), total_active (1,)) int32: the exclusive prefix sum of the
-    counts and their sum (``alltoallv.py:113-145``).  Arithmetic on P integers."""
-    c = torch.as_tensor(all_counts).to(torch.int64).reshape(-1)
-    inc = torch.cumsum(c, 0)
-    offsets = (inc - c).to(torch.int32)
-    total = inc[-1:].to(torch.int32) if c.numel() else torch.zeros(1, dtype=torch.int32, device=c.device)
-    return offsets, total
-
-
-# ---------------------------------------------------------------------------
-# a14, a16: pack, exchange, unpack
-# ---------------------------------------------------------------------------
-def pack_active_blocks(kv_shard, active_indices, num_active, max_blocks: int, block_size: int = BLOCK_SIZE):
-    """Blocks active_indices[:num_active] of kv_shard (S, H, D) copied to the
-    front of a (max_blocks * block_size, H, D) buffer whose tail is zero
-    (``alltoallv.py:150-212``; ``distributed_attention.py:49-75``)."""
-    kv = _lib.as_device(kv_shard).contiguous()
-    idx = _lib.as_device(active_indices, device=kv.device, dtype=torch.int32).reshape(1, -1).contiguous()
-    cnt = _core.count_tensor(_lib.as_device(num_active, device=kv.device), kv.device)
-    out = _core.gather_blocks(kv.unsqueeze(0), idx, cnt, int(max_blocks), block_size, zero_tail=True)
-    return out[0]
-
-
-def alltoallv_exchange(k_packed, v_packed, group=None):
-    """Every rank's packed K and V, concatenated in rank order:
-    (P * max_tokens, H, D) each (``alltoallv.py:217-259``)."""
-    return _all_gather_cat(k_packed, group), _all_gather_cat(v_packed, group)
-
-
-def global_block_index(all_counts, slots_per_device: int):
-    """(order (P * slots,), total (1,)) int32 over a gathered buffer of P
-    chunks of ``slots_per_device`` blocks: valid slots (j % slots <
-    counts[j // slots]) first in ascending order, then the rest
-    (``distributed_attention.py:179-191``; ``phase_e_stratified.py:220-226``)."""
-    c = _lib.as_device(all_counts, dtype=torch.int32).reshape(-1).contiguous()
-    P = c.numel()
-    order = torch.empty((P * slots_per_device,), dtype=torch.int32, device=c.device)
-    total = torch.empty((1,), dtype=torch.int32, device=c.device)
-    offsets = torch.empty((P,), dtype=torch.int32, device=c.device)
-    _lib.call("oc_exchange_index", _lib.ptr(c), P, int(slots_per_device), _lib.ptr(order), _lib.ptr(total),
-              _lib.ptr(offsets), _lib.stream_ptr(c.device))
-    return order, total, offsets
-
-
-def unpack_received_blocks(kv_received, all_counts, num_devices: int, max_blocks: int,
-                           block_size: int = BLOCK_SIZE):
-    """(active_kv, device_offsets): the valid blocks of each device's chunk
-    moved to the front in device order, zero tail; token offsets of each
-    device's run (``alltoallv.py:264-335``).  Bit-exact block copies."""
-    kv = _lib.as_device(kv_received).contiguous()
-    order, total, offsets = global_block_index(_lib.as_device(all_counts, device=kv.device),
-                                               int(max_blocks))
-    nslots = int(num_devices) * int(max_blocks)
-    out = _core.gather_blocks(kv.unsqueeze(0), order.reshape(1, -1), total, nslots, block_size, zero_tail=True)
-    return out[0], offsets * block_size
-
-
-def alltoallv_kv_exchange(k_shard, v_shard, block_mask, group=None, block_size: int = BLOCK_SIZE):
-    """End-to-end exchange (``alltoallv.py:340-440``): returns
-    ``(k_active, v_active, all_counts, offsets, stats)``.  The first
-    total_active * block_size tokens of k_active / v_active are the retained
-    blocks of every rank in rank order; stats holds device tensors
-    (local_num_active, total_active, bytes_saved) and ints (dense_blocks,
-    bytes_dense) as the reference's dict does."""
-    k = _lib.as_device(k_shard).contiguous()
-    v = _lib.as_device(v_shard, device=k.device).contiguous()
-    nb = k.shape[0] // block_size
-    active_indices, num_active = stream_compact(block_mask)
-    all_counts = count_sync(num_active, group)
-    offsets, total_active = compute_offsets(all_counts)
-    kp = pack_active_blocks(k, active_indices, num_active, nb, block_size)
-    vp = pack_active_blocks(v, active_indices, num_active, nb, block_size)
-    kr, vr = alltoallv_exchange(kp, vp, group)
-    P = all_counts.numel()
-    k_active, _ = unpack_received_blocks(kr, all_counts, P, nb, block_size)
-    v_active, _ = unpack_received_blocks(vr, all_counts, P, nb, block_size)
-    H, D = k.shape[1], k.shape[2]
-    per_block = block_size * H * D * k.element_size() * 2  # K + V
-    dense_blocks = P * nb
-    bytes_dense = dense_blocks * per_block
-    stats = {
-        "local_num_active": num_active,
-        "total_active": total_active,
-        "dense_blocks": dense_blocks,
-        "bytes_saved": bytes_dense - total_active.to(torch.int64) * per_block,
-        "bytes_dense": bytes_dense,
-    }
-    return k_active, v_active, all_counts, offsets, stats
-
-
-# ---------------------------------------------------------------------------
-# a17, a18: attention across shards
-# ---------------------------------------------------------------------------
-def _attend_gathered(q, k_all, v_all, order, total, block_size):
-    q4, k4, v4, _ = _core.batched_qkv(q, k_all, v_all)
-    out = _core.attend(q4, k4, v4, order.reshape(1, -1), total, block_size, out_dtype=torch.bfloat16)
-    return out[0]
-
-
-def distributed_orthocache_attention(q_shard, k_shard, v_shard, block_mask, group=None,
-                                     block_size: int = BLOCK_SIZE):
-    """Attention of the (replicated) query over the retained blocks of every
-    rank (``distributed_attention.py:131-195``): local compaction and
-    packing, all-gather of the counts and of the packed K/V, the valid-slot
-    index over the gathered buffer, then indirect attention.  Returns
-    (Sq, Hq, D) bfloat16 on every rank."""
-    k = _lib.as_device(k_shard).contiguous()
-    v = _lib.as_device(v_shard, device=k.device).contiguous()
-    nb = k.shape[0] // block_size
-    active_indices, num_active = stream_compact(block_mask)
-    kp = pack_active_blocks(k, active_indices, num_active, nb, block_size)
-    vp = pack_active_blocks(v, active_indices, num_active, nb, block_size)
-    all_counts = count_sync(num_active, group)
-    k_all, v_all = alltoallv_exchange(kp, vp, group)
-    order, total, _ = global_block_index(all_counts, nb)
-    return _attend_gathered(q_shard, k_all, v_all, order, total, block_size)
-
-
-def stratified_buckets(nb_per_dev: int):
-    """The four capacities of ``build_stratified`` (``phase_e_stratified.py:182-197``):
-    max(1, nb/4), max(1, nb/2), max(1, 3nb/4), nb, duplicates removed, the
-    last repeated to four entries."""
-    out = []
-    for b in (max(1, nb_per_dev // 4), max(1, nb_per_dev // 2), max(1, (nb_per_dev * 3) // 4), nb_per_dev):
-        if b not in out:
-            out.append(b)
-    while len(out) < 4:
-        out.append(out[-1])
-    return tuple(out)
-
-
-def stratified_bucket(gmax: int, nb_per_dev: int) -> int:
-    """The smallest bucket that holds ``gmax`` blocks (``phase_e_stratified.py:262-265``)."""
-    return int(_lib.query("oc_stratified_bucket", int(nb_per_dev), int(gmax)))
-
-
-def stratified_allgather_attention(q, k_shard, v_shard, active_indices, num_active, group=None,
-                                   block_size: int = BLOCK_SIZE):
-    """``build_stratified`` (``phase_e_stratified.py:164-273``): the global max
-    count (all-reduce MAX, the reference's pmax) picks a capacity bucket;
-    every rank sends its first ``bucket`` retained blocks; the gathered
-    blocks at local position < count of their rank are attended to.
-    Returns ((Sq, Hq, D) bfloat16, bucket).  The bucket is read on the host
-    (one integer) because it sizes the collective."""
-    k = _lib.as_device(k_shard).contiguous()
-    v = _lib.as_device(v_shard, device=k.device).contiguous()
-    nb = k.shape[0] // block_size
-    na = _lib.as_device(num_active, device=k.device, dtype=torch.int32).reshape(1)
-    gmax = na.clone()
-    dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)
-    bucket = stratified_bucket(int(gmax.item()), nb)
-    kp = pack_active_blocks(k, active_indices, na, bucket, block_size)
-    vp = pack_active_blocks(v, active_indices, na, bucket, block_size)
-    all_counts = count_sync(na, group)
-    k_all, v_all = alltoallv_exchange(kp, vp, group)
-    order, total, _ = global_block_index(all_counts, bucket)
-    return _attend_gathered(q, k_all, v_all, order, total, block_size), bucket
-
-
-def sequence_parallel_attention(q, k_shard, v_shard, block_mask, group=None, block_size: int = BLOCK_SIZE):
-    """Attention over the union of all ranks' retained blocks with no K/V
-    movement: each rank attends to its own retained blocks, producing the
-    unnormalised (m, l, o) of every query row; an all-gather of those P
-    partials and a log-sum-exp merge give the result (the online-softmax
-    combine of ``distributed_attention.py:95-128`` across shards).  Returns
-    (Sq, Hq, D) bfloat16 on every rank."""
-    q4, k4, v4, _ = _core.batched_qkv(q, k_shard, v_shard)
-    active_indices, num_active = stream_compact(block_mask)
-    nb = k4.shape[1] // block_size
-    m, l, o = _core.partial_attend(q4, k4, v4, active_indices.reshape(1, -1), num_active, block_size,
-                                   max_blocks=nb)
-    P = _world(group)
-    gm = _all_gather_cat(m.unsqueeze(0), group)
-    gl = _all_gather_cat(l.unsqueeze(0), group)
-    go = _all_gather_cat(o.unsqueeze(0), group)
-    out = _core.merge_partials(gm.reshape(P, -1), gl.reshape(P, -1), go.reshape(P, -1, o.shape[-1]),
-                               tuple(q4.shape[1:]), torch.bfloat16)
-    return out
+from .alltoallv import (  # noqa: F401
+    BLOCK_SIZE, _world, _all_gather_cat, stream_compact, count_sync, compute_offsets, pack_active_blocks,
+    alltoallv_exchange, global_block_index, unpack_received_blocks, alltoallv_kv_exchange,
+)
+from .distributed_attention import (  # noqa: F401
+    _attend_gathered, distributed_orthocache_attention, stratified_buckets, stratified_bucket,
+    stratified_allgather_attention, sequence_parallel_attention, ici_data_volume,
+)
 
 
 # ---------------------------------------------------------------------------
@@ -390,20 +158,6 @@ class ShardedDecoder:
         if self.peer:
             _lib.load().oc_sharded_disconnect(_lib.ptr(self.ws))
             self.peer = False
-
-
-def ici_data_volume(num_blocks_per_device: int, num_devices: int, active_counts, num_heads: int,
-                    head_dim: int, dtype_bytes: int = 2):
-    """Exchange byte accounting (``distributed_attention.py:198-223``)."""
-    per_block = BLOCK_SIZE * num_heads * head_dim * dtype_bytes
-    dense = num_blocks_per_device * num_devices * per_block
-    sparse = sum(int(c) for c in active_counts) * per_block
-    return {
-        "dense_bytes": dense,
-        "sparse_bytes": sparse,
-        "savings_bytes": dense - sparse,
-        "savings_pct": (1 - sparse / dense) * 100 if dense > 0 else 0.0,
-    }
 
 
 __all__ = [
