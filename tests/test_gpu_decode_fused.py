@@ -91,6 +91,8 @@ def check_against_oracle(q, k, v, tau, keep, perm, count, out):
 
 @pytest.mark.parametrize("B,nb,hq,hkv,sq,evicts", [
     (1, 128, 32, 8, 1, [0.75]),           # config 1 at full size
+    (1, 128, 32, 8, 1, [0.5]),            # config 1's eviction sweep at full size
+    (1, 128, 32, 8, 1, [0.9]),
     (1, 16, 8, 8, 1, [0.5]),              # config 0
     (2, 40, 32, 8, 1, [0.5, 0.9]),        # two batch rows, different retained counts
     (3, 12, 16, 4, 2, [0.6, 0.0, 1.0]),   # R = 8 rows; nothing evicted; everything evicted
