@@ -37,8 +37,11 @@
 #include "oc_common.cuh"
 #include "oc_tma.cuh"
 #include "oc_mma.cuh"
+#include "oc_tcgen05.cuh"
 
 #include <math.h>
+#include <algorithm>
+#include <type_traits>
 
 namespace oc {
 namespace {
@@ -1982,6 +1985,390 @@ meta_bound_gemm_kernel(const float* __restrict__ dc, const float* __restrict__ e
   }
 }
 
+// The same bound GEMM on the tensor cores for bfloat16 queries:
+// mma.sync m16n8k8 with tf32 operands and float32 accumulation.  A bfloat16
+// query is exact in tf32 (8 of its 10 mantissa bits); each block mean is
+// split into a tf32 part and the tf32 of its remainder (two MMAs), so the
+// dot keeps about 21 bits of the mean, against 24 for the float32 FMA chain
+// of meta_bound_gemm_kernel — both differ from the float64 sum of the oracle
+// only by rounding.  CTA = 128 rows x 64 blocks of one (b, h), 8 warps of
+// 32 rows x 32 blocks; the K dimension is staged 32 at a time.
+constexpr int kMtLdq = kMbRows + 8, kMtLdb = kMbBlk + 8;  // row pitch = 8 mod 32 banks: conflict-free fragments
+
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(256)
+meta_bound_mma_kernel(const float* __restrict__ dc, const float* __restrict__ e_ac,
+                      const __nv_bfloat16* __restrict__ q, int nb, int H, int D, int Sq, int Hq, int G, int* key,
+                      float* bounds, MetaSrc ms) {
+  __shared__ float qs[kMbK][kMtLdq];
+  __shared__ uint32_t dh[kMbK][kMtLdb], dl[kMbK][kMtLdb];
+  __shared__ float s_nrm[kMbRows];
+  __shared__ float s_rs[kMbBlk];
+  __shared__ float s_max[4][kMbBlk];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c4 = lane & 3;
+  const int wr = (warp & 3) * 32, wc = (warp >> 2) * 32;  // warp tile origin: rows, blocks
+  const int bh = blockIdx.y, h = bh % H, b = bh / H;
+  const int r0 = blockIdx.x * kMbRows, j0 = blockIdx.z * kMbBlk;
+  const int rows = Sq * G;
+  // loaders: query row lr (two threads per row, 16 dims each as two 16-byte
+  // vectors); block lb (four threads per block, 8 dims each as two float4)
+  const int lr = tid >> 1, lhalf = tid & 1;
+  const __nv_bfloat16* qrow = nullptr;
+  if (r0 + lr < rows) {
+    const int s = (r0 + lr) / G, gq = (r0 + lr) - s * G;
+    qrow = q + (((size_t)b * Sq + s) * Hq + (size_t)h * G + gq) * D;
+  }
+  const int lb = tid >> 2, lq = tid & 3;
+  const int64_t dsrc = (j0 + lb < nb) ? meta_src(ms, b, j0 + lb, h, nb, H) : -1;
+  const float* dcrow = dsrc >= 0 ? dc + dsrc * D : nullptr;
+  if (tid < kMbBlk) {
+    const int64_t es = (j0 + tid < nb) ? meta_src(ms, b, j0 + tid, h, nb, H) : -1;
+    s_rs[tid] = es >= 0 ? sqrtf(e_ac[es]) : -1.f;  // -1: no block
+  }
+  float acc[2][4][4];
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[m][n][c] = 0.f;
+  float nrm = 0.f;
+  for (int k0 = 0; k0 < D; k0 += kMbK) {
+    {
+      uint4 v[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+      if (qrow) {
+        const uint4* src = reinterpret_cast<const uint4*>(qrow + k0 + lhalf * 16);
+        v[0] = src[0];
+        v[1] = src[1];
+      }
+      const __nv_bfloat16* e16 = reinterpret_cast<const __nv_bfloat16*>(v);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float x = __bfloat162float(e16[e]);
+        nrm = fmaf(x, x, nrm);
+        qs[lhalf * 16 + e][lr] = x;
+      }
+    }
+    {
+      float4 v[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+      if (dcrow) {
+        const float4* src = reinterpret_cast<const float4*>(dcrow + k0 + lq * 8);
+        v[0] = src[0];
+        v[1] = src[1];
+      }
+      const float* f = reinterpret_cast<const float*>(v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float mean = f[e] / kNorm;  // block mean = DC / sqrt(512), as in the FMA form
+        const uint32_t hi = tf32_rna(mean);
+        dh[lq * 8 + e][lb] = hi;
+        dl[lq * 8 + e][lb] = tf32_rna(mean - __uint_as_float(hi));
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kMbK; kk += 8) {
+      uint32_t a[2][4];
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const int rr = wr + m * 16 + g;
+        a[m][0] = __float_as_uint(qs[kk + c4][rr]);
+        a[m][1] = __float_as_uint(qs[kk + c4][rr + 8]);
+        a[m][2] = __float_as_uint(qs[kk + c4 + 4][rr]);
+        a[m][3] = __float_as_uint(qs[kk + c4 + 4][rr + 8]);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int cc = wc + n * 8 + g;
+        const uint32_t h0 = dh[kk + c4][cc], h1 = dh[kk + c4 + 4][cc];
+        const uint32_t l0 = dl[kk + c4][cc], l1 = dl[kk + c4 + 4][cc];
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          mma_tf32(acc[m][n], a[m], l0, l1);
+          mma_tf32(acc[m][n], a[m], h0, h1);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  nrm += __shfl_xor_sync(0xffffffffu, nrm, 1);
+  if (lhalf == 0) s_nrm[lr] = nrm;
+  __syncthreads();
+  const float sqrt_d = sqrtf((float)D);
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int jl = wc + n * 8 + 2 * c4 + c;  // block within the CTA tile
+      const float rs = s_rs[jl];
+      float bm = -INFINITY;
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int rl = wr + m * 16 + g + 8 * hf;
+          const int r = r0 + rl;
+          if (r < rows && rs >= 0.f) {
+            const float bound = acc[m][n][2 * hf + c] / sqrt_d + (sqrtf(s_nrm[rl]) * rs) / sqrt_d;
+            if (bounds) {
+              const int s = r / G, gq = r - s * G;
+              bounds[(((size_t)b * Sq + s) * nb + j0 + jl) * Hq + (size_t)h * G + gq] = bound;
+            }
+            bm = fmaxf(bm, bound);
+          }
+        }
+      // max over the 8 row groups g (lanes of equal c4)
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+      if (g == 0) s_max[warp & 3][jl] = bm;
+    }
+  }
+  __syncthreads();
+  if (tid < kMbBlk && j0 + tid < nb && s_rs[tid] >= 0.f) {
+    const float m = fmaxf(fmaxf(s_max[0][tid], s_max[1][tid]), fmaxf(s_max[2][tid], s_max[3][tid]));
+    atomicMax(&key[((size_t)b * nb + j0 + tid) * H + h], f2key(m));
+  }
+}
+
+// The bound GEMM on the 5th-generation tensor cores (tcgen05, accumulators
+// in tensor memory) for bfloat16 queries with head_dim 128.  A bfloat16
+// query is exact as an MMA operand; each block mean (DC / sqrt(512) in
+// float32, as in the FMA form) is split into three bfloat16 parts
+// m = p1 + p2 + p3 (24 significant bits, the float32 mean up to its last
+// bit), so one M128 N192 K16 kind::f16 MMA per 16 channels gives q . p1,
+// q . p2 and q . p3 in three column ranges of float32 accumulators, summed
+// in the epilogue (smallest first).  The bound is
+// (q . m + |q| sqrt(E_AC)) * (1 / sqrt(D)): the FMA form's terms, one
+// rounding apart.
+// CTA = one (b, h), 64 blocks, tpc row tiles of 128 query rows (gq adjacent
+// query heads x 128 / gq positions, so each position's rows are one
+// contiguous run).  16 warps: thread 0 issues the TMA loads of the row tiles
+// (double-buffered) and the MMAs; in the epilogue warp w reads tensor-memory
+// lanes 32 (w % 4) .. + 31 (rows) and block columns 16 (w / 4) .. + 15, and
+// every thread keeps a running max per block over its rows; the CTA ends with
+// one max per block (atomicMax of the ordered key, as in the FMA form).
+constexpr int kBtRows = 128, kBtBlk = 64, kBtN = 3 * kBtBlk, kBtThreads = 512;
+constexpr int kBtCols = kBtBlk / (kBtThreads / 128);  // block columns per thread: 16
+constexpr int kBtATile = kBtRows * 128 * 2;  // bf16 row tile: two 128B-swizzled boxes of 64 channels
+constexpr int kBtBBox = kBtN * 128;          // 192 rows x 64 channels of bf16
+struct BtSmem {
+  unsigned char a[2][kBtATile];
+  unsigned char bm[2][kBtBBox];
+  uint64_t a_full[2], mma_done;
+  uint32_t tmem;
+  float s_rs[kBtBlk];
+  float s_nrm[2][kBtThreads / 128][kBtRows];  // partial squared row norms by column group, per buffer
+  float s_max[4][kBtBlk];
+};
+constexpr size_t kBtSmemBytes = sizeof(BtSmem) + 1024;
+
+// 16 consecutive fp32 columns of this thread's lane, loaded and waited for in
+// one asm statement.
+__device__ __forceinline__ void tmem_ld16_wait(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(kBtThreads, 1)
+meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __restrict__ dc,
+                     const float* __restrict__ e_ac, int nb, int H, int Sq, int Hq, int G, int gq, int ntiles, int tpc,
+                     int* key, float* bounds, MetaSrc ms) {
+  constexpr int D = 128;
+  extern __shared__ unsigned char bt_raw[];
+  BtSmem& sm = *reinterpret_cast<BtSmem*>((reinterpret_cast<uintptr_t>(bt_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, cg = warp >> 2;  // tensor-memory lane quarter, column group
+  const int row = quarter * 32 + lane;           // row of the tile (tensor-memory lane)
+  const int bh = blockIdx.y, h = bh % H, b = bh / H;
+  const int j0 = blockIdx.z * kBtBlk;
+  const int t0 = blockIdx.x * tpc;
+  const int nt = min(tpc, ntiles - t0);
+  if (tid == 0) {
+    mbar_init(&sm.a_full[0], 1);
+    mbar_init(&sm.a_full[1], 1);
+    mbar_init(&sm.mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)),
+                 "r"(256)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid < kBtBlk) {
+    const int64_t es = (j0 + tid < nb) ? meta_src(ms, b, j0 + tid, h, nb, H) : -1;
+    sm.s_rs[tid] = es >= 0 ? sqrtf(e_ac[es]) : -1.f;  // -1: no block
+  }
+  {
+    // B operand: rows p * 64 + jj (part p of block jj's mean), K-major,
+    // 128-byte swizzle (16-byte chunk c of row n at chunk c ^ (n % 8)).
+    // Thread: block jj, channels 16 kq .. 16 kq + 15 (two 16-byte chunks).
+    const int jj = tid >> 3, kq = tid & 7;
+    const int kb = kq >> 2;  // box of 64 channels
+    const int64_t src = (j0 + jj < nb) ? meta_src(ms, b, j0 + jj, h, nb, H) : -1;
+    const float* rowp = src >= 0 ? dc + src * D + kq * 16 : nullptr;
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = (kq & 3) * 2 + cc;  // 16-byte chunk within the box's 128-byte row
+      float v[8];
+      if (rowp) {
+        const float4 x = reinterpret_cast<const float4*>(rowp)[2 * cc];
+        const float4 y = reinterpret_cast<const float4*>(rowp)[2 * cc + 1];
+        v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
+      uint32_t pk[3][4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float r0 = v[e] / kNorm, r1 = v[e + 1] / kNorm;
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          const __nv_bfloat16 h0 = __float2bfloat16_rn(r0), h1 = __float2bfloat16_rn(r1);
+          pk[p][e / 2] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+          r0 -= __bfloat162float(h0);
+          r1 -= __bfloat162float(h1);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        const int n = p * kBtBlk + jj;
+        *reinterpret_cast<uint4*>(sm.bm[kb] + n * 128 + ((c ^ (n & 7)) << 4)) =
+            make_uint4(pk[p][0], pk[p][1], pk[p][2], pk[p][3]);
+      }
+    }
+  }
+  fence_proxy_async();  // the B operand written by threads is read by the tensor cores
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem;
+  // A row tile: gq query heads (of this KV head's G) x 128 / gq positions,
+  // row r = position s0 + r / gq, head hq0 + r % gq
+  const int ng = G / gq, ppt = kBtRows / gq;
+  auto load_tile = [&](int t) {
+    const int T = t0 + t, hq = h * G + (T % ng) * gq, s0 = (T / ng) * ppt;
+    uint64_t* bar = &sm.a_full[t & 1];
+    mbar_expect_tx(bar, kBtATile);
+    tma_load_3d(sm.a[t & 1], &mq, bar, 0, hq, b * Sq + s0);
+    tma_load_3d(sm.a[t & 1] + kBtATile / 2, &mq, bar, 64, hq, b * Sq + s0);
+  };
+  if (tid == 0) {
+    load_tile(0);
+    if (nt > 1) load_tile(1);
+  }
+  float rmax[kBtCols], rs[kBtCols];
+#pragma unroll
+  for (int i = 0; i < kBtCols; ++i) {
+    rmax[i] = -INFINITY;
+    rs[i] = sm.s_rs[cg * kBtCols + i];
+  }
+  const float inv_sqrt_d = 1.f / sqrtf((float)D);
+  constexpr uint32_t kId = tc_idesc_bf16(kBtRows, kBtN, 0);
+  const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16) + cg * kBtCols;
+  bool ok = true;
+  for (int t = 0; t < nt; ++t) {
+    const int buf = t & 1;
+    const bool got = mbar_wait(&sm.a_full[buf], (t >> 1) & 1);
+    if (__syncthreads_or(!got)) { ok = false; break; }
+    {
+      // partial squared norm of row `row` over this column group's 32 channels
+      float nrm = 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const int c = cg * 4 + c4, kb = c >> 3, cl = c & 7;
+        const uint4 w = *reinterpret_cast<const uint4*>(sm.a[buf] + kb * (kBtATile / 2) + row * 128 +
+                                                        ((cl ^ (row & 7)) << 4));
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = __uint_as_float(u[e] << 16), hi = __uint_as_float(u[e] & 0xffff0000u);
+          nrm = fmaf(lo, lo, nrm);
+          nrm = fmaf(hi, hi, nrm);
+        }
+      }
+      sm.s_nrm[buf][cg][row] = nrm;
+    }
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ab = smem_u32(sm.a[buf]), bb = smem_u32(sm.bm[0]);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t ad = sdesc(ab + (kk >> 2) * (kBtATile / 2) + (kk & 3) * 32, 16, 1024);
+        const uint64_t bd = sdesc(bb + (kk >> 2) * kBtBBox + (kk & 3) * 32, 16, 1024);
+        umma_bf16(tmem, ad, bd, kId, kk > 0 ? 1 : 0);
+      }
+      umma_commit(&sm.mma_done);
+    }
+    const bool done = mbar_wait(&sm.mma_done, t & 1);
+    tc_fence_after();
+    // every thread has read this buffer and stored its partial norm: the
+    // buffer may be refilled
+    if (__syncthreads_or(!done)) { ok = false; break; }
+    if (tid == 0 && t + 2 < nt) load_tile(t + 2);
+    const int T = t0 + t, hq = h * G + (T % ng) * gq + row % gq, s = (T / ng) * ppt + row / gq;
+    const bool valid = s < Sq;
+    const float rn = sqrtf((sm.s_nrm[buf][0][row] + sm.s_nrm[buf][1][row]) +
+                           (sm.s_nrm[buf][2][row] + sm.s_nrm[buf][3][row]));
+    float x0[kBtCols], x1[kBtCols], x2[kBtCols];
+    tmem_ld16_wait(t_row, x0);
+    tmem_ld16_wait(t_row + kBtBlk, x1);
+    tmem_ld16_wait(t_row + 2 * kBtBlk, x2);
+#pragma unroll
+    for (int i = 0; i < kBtCols; ++i) {
+      if (valid && rs[i] >= 0.f) {
+        const float bound = fmaf(rn, rs[i], x2[i] + x1[i] + x0[i]) * inv_sqrt_d;
+        if (bounds) bounds[(((size_t)b * Sq + s) * nb + j0 + cg * kBtCols + i) * Hq + hq] = bound;
+        rmax[i] = fmaxf(rmax[i], bound);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // tensor memory read: the next tile's MMA may overwrite it
+  }
+  if (!ok && tid == 0) atomicExch(&g_score_status, 1);
+#pragma unroll
+  for (int i = 0; i < kBtCols; ++i) {
+    float m = rmax[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) sm.s_max[quarter][cg * kBtCols + i] = m;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ok && tid < kBtBlk && j0 + tid < nb && sm.s_rs[tid] >= 0.f) {
+    const float m = fmaxf(fmaxf(sm.s_max[0][tid], sm.s_max[1][tid]), fmaxf(sm.s_max[2][tid], sm.s_max[3][tid]));
+    atomicMax(&key[((size_t)b * nb + j0 + tid) * H + h], f2key(m));
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+  }
+}
+
 __global__ void meta_bound_gates_kernel(float* bound_max, const float* __restrict__ zeta, int64_t cells, float tau,
                                         float zeta_max, uint8_t* keep, int nb, int H, MetaSrc ms) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -2007,6 +2394,46 @@ int launch_meta_bound_gemm(const float* dc, const float* e_ac, const float* zeta
   int* key = reinterpret_cast<int*>(bound_max);
   meta_bound_init_kernel<<<g1, 256, 0, st>>>(key, cells);
   dim3 grid((unsigned)gx, (unsigned)(B * H), (unsigned)((nb + kMbBlk - 1) / kMbBlk));
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (D == 128 && aligned16(q) && aligned16(dc) && (int64_t)B * Sq < INT32_MAX) {
+      // tcgen05 form: q as a (B*Sq, Hq, 128) tensor map, row tiles of 128
+      // positions of one query head
+      // a box of gq adjacent query heads x 128 / gq positions: 128 rows of
+      // 128 bytes in runs of gq * 128 contiguous bytes
+      const int gq = (G <= kBtRows && kBtRows % G == 0) ? G : 1;
+      CUtensorMap mq;
+      const uint64_t mkey[4] = {5, (uint64_t)q, (uint64_t)Hq | ((uint64_t)gq << 32), (uint64_t)B * Sq};
+      if (!map_cache_get(mkey, &mq)) {
+        const uint64_t dims[3] = {128, (uint64_t)Hq, (uint64_t)B * Sq};
+        const uint64_t strides[2] = {256, (uint64_t)Hq * 256};
+        const uint32_t box[3] = {64, (uint32_t)gq, (uint32_t)(kBtRows / gq)};
+        const int r = encode_map_3d(&mq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dims, strides, box, true);
+        if (r) return set_error(OC_ERR_CUDA, "oc_score_from_metadata: tensor map for q failed (CUresult %d)", r);
+        map_cache_put(mkey, mq);
+      }
+      static std::atomic<uint64_t> s_setup{0};
+      if (first_on_device(s_setup)) {
+        cudaError_t e = cudaFuncSetAttribute(meta_bound_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kBtSmemBytes);
+        if (e != cudaSuccess) return set_error(OC_ERR_CUDA, "oc_score_from_metadata: %s", cudaGetErrorString(e));
+      }
+      // row tiles per CTA: one wave of at most one CTA per SM (one fits per SM)
+      const int ntiles = (G / gq) * ((Sq + kBtRows / gq - 1) / (kBtRows / gq));
+      const int64_t cols = (int64_t)B * H * ((nb + kBtBlk - 1) / kBtBlk);
+      const int64_t per_col = std::max<int64_t>(1, device_sm_count() / cols);
+      const int tpc = (int)((ntiles + per_col - 1) / per_col);
+      dim3 tgrid((unsigned)((ntiles + tpc - 1) / tpc), (unsigned)(B * H), (unsigned)((nb + kBtBlk - 1) / kBtBlk));
+      meta_bound_tc_kernel<<<tgrid, kBtThreads, kBtSmemBytes, st>>>(mq, dc, e_ac, nb, H, Sq, Hq, G, gq, ntiles, tpc, key,
+                                                                    bounds, ms);
+      meta_bound_gates_kernel<<<g1, 256, 0, st>>>(bound_max, zeta, cells, tau, zeta_max, keep, nb, H, ms);
+      return check_launch("meta_bound_tc_kernel");
+    }
+    if (aligned16(q) && aligned16(dc)) {
+      meta_bound_mma_kernel<<<grid, 256, 0, st>>>(dc, e_ac, q, nb, H, D, Sq, Hq, G, key, bounds, ms);
+      meta_bound_gates_kernel<<<g1, 256, 0, st>>>(bound_max, zeta, cells, tau, zeta_max, keep, nb, H, ms);
+      return check_launch("meta_bound_mma_kernel");
+    }
+  }
   meta_bound_gemm_kernel<T><<<grid, 256, 0, st>>>(dc, e_ac, q, nb, H, D, Sq, Hq, G, key, bounds, ms);
   meta_bound_gates_kernel<<<g1, 256, 0, st>>>(bound_max, zeta, cells, tau, zeta_max, keep, nb, H, ms);
   return check_launch("meta_bound_gemm_kernel");
