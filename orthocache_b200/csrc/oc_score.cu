@@ -2158,7 +2158,8 @@ meta_bound_mma_kernel(const float* __restrict__ dc, const float* __restrict__ e_
 // CTA = one (b, h), 64 blocks, tpc row tiles of 128 query rows (gq adjacent
 // query heads x 128 / gq positions, so each position's rows are one
 // contiguous run).  16 warps: thread 0 issues the TMA loads of the row tiles
-// (double-buffered) and the MMAs; in the epilogue warp w reads tensor-memory
+// (a ring of three) and the MMAs, into two tensor-memory accumulators so that
+// a tile's MMA overlaps the previous tile's epilogue; there warp w reads tensor-memory
 // lanes 32 (w % 4) .. + 31 (rows) and block columns 16 (w / 4) .. + 15, and
 // every thread keeps a running max per block over its rows; the CTA ends with
 // one max per block (atomicMax of the ordered key, as in the FMA form).
@@ -2166,13 +2167,14 @@ constexpr int kBtRows = 128, kBtBlk = 64, kBtN = 3 * kBtBlk, kBtThreads = 512;
 constexpr int kBtCols = kBtBlk / (kBtThreads / 128);  // block columns per thread: 16
 constexpr int kBtATile = kBtRows * 128 * 2;  // bf16 row tile: two 128B-swizzled boxes of 64 channels
 constexpr int kBtBBox = kBtN * 128;          // 192 rows x 64 channels of bf16
+constexpr int kBtABufs = 3;  // query row-tile ring
 struct BtSmem {
-  unsigned char a[2][kBtATile];
+  unsigned char a[kBtABufs][kBtATile];
   unsigned char bm[2][kBtBBox];
-  uint64_t a_full[2], mma_done;
+  uint64_t a_full[kBtABufs], mma_done[2];
   uint32_t tmem;
   float s_rs[kBtBlk];
-  float s_nrm[2][kBtThreads / 128][kBtRows];  // partial squared row norms by column group, per buffer
+  float s_nrm[2][kBtThreads / 128][kBtRows];  // partial squared row norms by column group, per accumulator
   float s_max[4][kBtBlk];
 };
 constexpr size_t kBtSmemBytes = sizeof(BtSmem) + 1024;
@@ -2207,14 +2209,14 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
   const int t0 = blockIdx.x * tpc;
   const int nt = min(tpc, ntiles - t0);
   if (tid == 0) {
-    mbar_init(&sm.a_full[0], 1);
-    mbar_init(&sm.a_full[1], 1);
-    mbar_init(&sm.mma_done, 1);
+    for (int i = 0; i < kBtABufs; ++i) mbar_init(&sm.a_full[i], 1);
+    mbar_init(&sm.mma_done[0], 1);
+    mbar_init(&sm.mma_done[1], 1);
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == 0) {  // two accumulators of 192 columns, at columns 0 and 256
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)),
-                 "r"(256)
+                 "r"(512)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -2272,15 +2274,13 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
   const int ng = G / gq, ppt = kBtRows / gq;
   auto load_tile = [&](int t) {
     const int T = t0 + t, hq = h * G + (T % ng) * gq, s0 = (T / ng) * ppt;
-    uint64_t* bar = &sm.a_full[t & 1];
+    uint64_t* bar = &sm.a_full[t % kBtABufs];
     mbar_expect_tx(bar, kBtATile);
-    tma_load_3d(sm.a[t & 1], &mq, bar, 0, hq, b * Sq + s0);
-    tma_load_3d(sm.a[t & 1] + kBtATile / 2, &mq, bar, 64, hq, b * Sq + s0);
+    tma_load_3d(sm.a[t % kBtABufs], &mq, bar, 0, hq, b * Sq + s0);
+    tma_load_3d(sm.a[t % kBtABufs] + kBtATile / 2, &mq, bar, 64, hq, b * Sq + s0);
   };
-  if (tid == 0) {
-    load_tile(0);
-    if (nt > 1) load_tile(1);
-  }
+  if (tid == 0)
+    for (int t = 0; t < kBtABufs && t < nt; ++t) load_tile(t);
   float rmax[kBtCols], rs[kBtCols];
 #pragma unroll
   for (int i = 0; i < kBtCols; ++i) {
@@ -2290,54 +2290,62 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
   const float inv_sqrt_d = 1.f / sqrtf((float)D);
   constexpr uint32_t kId = tc_idesc_bf16(kBtRows, kBtN, 0);
   const uint32_t t_row = tmem + ((uint32_t)(quarter * 32) << 16) + cg * kBtCols;
+  // Tile t: its MMA (accumulator t % 2) is issued in iteration t, its
+  // epilogue runs in iteration t + 1, overlapping the MMA of tile t + 1.
   bool ok = true;
-  for (int t = 0; t < nt; ++t) {
-    const int buf = t & 1;
-    const bool got = mbar_wait(&sm.a_full[buf], (t >> 1) & 1);
-    if (__syncthreads_or(!got)) { ok = false; break; }
-    {
-      // partial squared norm of row `row` over this column group's 32 channels
-      float nrm = 0.f;
+  for (int t = 0; t <= nt; ++t) {
+    if (t < nt) {
+      const int buf = t % kBtABufs;
+      const bool got = mbar_wait(&sm.a_full[buf], (t / kBtABufs) & 1);
+      if (__syncthreads_or(!got)) { ok = false; break; }
+      {
+        // partial squared norm of row `row` over this column group's 32 channels
+        float nrm = 0.f;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        const int c = cg * 4 + c4, kb = c >> 3, cl = c & 7;
-        const uint4 w = *reinterpret_cast<const uint4*>(sm.a[buf] + kb * (kBtATile / 2) + row * 128 +
-                                                        ((cl ^ (row & 7)) << 4));
-        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const int c = cg * 4 + c4, kb = c >> 3, cl = c & 7;
+          const uint4 w = *reinterpret_cast<const uint4*>(sm.a[buf] + kb * (kBtATile / 2) + row * 128 +
+                                                          ((cl ^ (row & 7)) << 4));
+          const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float lo = __uint_as_float(u[e] << 16), hi = __uint_as_float(u[e] & 0xffff0000u);
-          nrm = fmaf(lo, lo, nrm);
-          nrm = fmaf(hi, hi, nrm);
+          for (int e = 0; e < 4; ++e) {
+            const float lo = __uint_as_float(u[e] << 16), hi = __uint_as_float(u[e] & 0xffff0000u);
+            nrm = fmaf(lo, lo, nrm);
+            nrm = fmaf(hi, hi, nrm);
+          }
         }
+        sm.s_nrm[t & 1][cg][row] = nrm;
       }
-      sm.s_nrm[buf][cg][row] = nrm;
-    }
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t ab = smem_u32(sm.a[buf]), bb = smem_u32(sm.bm[0]);
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t ab = smem_u32(sm.a[buf]), bb = smem_u32(sm.bm[0]);
+        const uint32_t acc = tmem + (uint32_t)(t & 1) * 256;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t ad = sdesc(ab + (kk >> 2) * (kBtATile / 2) + (kk & 3) * 32, 16, 1024);
-        const uint64_t bd = sdesc(bb + (kk >> 2) * kBtBBox + (kk & 3) * 32, 16, 1024);
-        umma_bf16(tmem, ad, bd, kId, kk > 0 ? 1 : 0);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = sdesc(ab + (kk >> 2) * (kBtATile / 2) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc(bb + (kk >> 2) * kBtBBox + (kk & 3) * 32, 16, 1024);
+          umma_bf16(acc, ad, bd, kId, kk > 0 ? 1 : 0);
+        }
+        umma_commit(&sm.mma_done[t & 1]);
       }
-      umma_commit(&sm.mma_done);
     }
-    const bool done = mbar_wait(&sm.mma_done, t & 1);
+    if (t == 0) continue;
+    const int e = t - 1;  // the tile whose epilogue runs now
+    const bool done = mbar_wait(&sm.mma_done[e & 1], (e >> 1) & 1);
     tc_fence_after();
-    // every thread has read this buffer and stored its partial norm: the
-    // buffer may be refilled
     if (__syncthreads_or(!done)) { ok = false; break; }
-    if (tid == 0 && t + 2 < nt) load_tile(t + 2);
-    const int T = t0 + t, hq = h * G + (T % ng) * gq + row % gq, s = (T / ng) * ppt + row / gq;
+    // tile e's MMA is complete and every thread read its buffer (before the
+    // barrier of iteration e): the buffer takes tile e + 3
+    if (tid == 0 && e + kBtABufs < nt) load_tile(e + kBtABufs);
+    const int T = t0 + e, hq = h * G + (T % ng) * gq + row % gq, s = (T / ng) * ppt + row / gq;
     const bool valid = s < Sq;
-    const float rn = sqrtf((sm.s_nrm[buf][0][row] + sm.s_nrm[buf][1][row]) +
-                           (sm.s_nrm[buf][2][row] + sm.s_nrm[buf][3][row]));
+    const float rn = sqrtf((sm.s_nrm[e & 1][0][row] + sm.s_nrm[e & 1][1][row]) +
+                           (sm.s_nrm[e & 1][2][row] + sm.s_nrm[e & 1][3][row]));
+    const uint32_t t_acc = t_row + (uint32_t)(e & 1) * 256;
     float x0[kBtCols], x1[kBtCols], x2[kBtCols];
-    tmem_ld16_wait(t_row, x0);
-    tmem_ld16_wait(t_row + kBtBlk, x1);
-    tmem_ld16_wait(t_row + 2 * kBtBlk, x2);
+    tmem_ld16_wait(t_acc, x0);
+    tmem_ld16_wait(t_acc + kBtBlk, x1);
+    tmem_ld16_wait(t_acc + 2 * kBtBlk, x2);
 #pragma unroll
     for (int i = 0; i < kBtCols; ++i) {
       if (valid && rs[i] >= 0.f) {
@@ -2347,7 +2355,7 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
       }
     }
     tc_fence_before();
-    __syncthreads();  // tensor memory read: the next tile's MMA may overwrite it
+    __syncthreads();  // accumulator e % 2 and norms e % 2 read: tile e + 2 may reuse them
   }
   if (!ok && tid == 0) atomicExch(&g_score_status, 1);
 #pragma unroll
@@ -2365,7 +2373,7 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
   }
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
   }
 }
 
