@@ -689,6 +689,9 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   __shared__ float s_dcw[NBUF][D];           // DC coefficients of the tile in buffer tb
   __shared__ float s_qn[kQCacheBytes / (2 * 64)];  // squared norms of the staged query rows
   __shared__ volatile int s_abort;
+  constexpr int kMetaPre = 32 * NE;          // META: tiles whose decisions the compute warps make
+  __shared__ int s_kpre[META ? kMetaPre : 1];
+  __shared__ __align__(8) uint64_t kpbar;    // META: s_kpre is filled
 #ifdef OC_TIMING
   __shared__ unsigned long long s_tarr[kStages];
   __shared__ unsigned long long s_trel;
@@ -731,6 +734,7 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
     for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); s_rel[i] = 0; }
     for (int i = 0; i < NBUF; ++i) { mbar_init(&tfull[i], kW); mbar_init(&tempty[i], 1); }
     mbar_init(&setbar, 1);
+    if constexpr (META) mbar_init(&kpbar, kW);
     fence_mbar_init();
     s_abort = 0;
     s_merge = 0;
@@ -782,15 +786,17 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
       asm volatile("bar.sync 1, %0;" ::"r"(NE * 32) : "memory");
     }
     // This warp's tiles are e, e + NE, ...; with META the decisions of the
-    // first 32 are made before the wait for the previous kernel (the
-    // metadata and the queries are inputs), lane i holding tile i's.
+    // first 32 (tiles < kMetaPre) are made by the compute warps before the
+    // wait for the previous kernel (the metadata and the queries are
+    // inputs), one warp per tile; lane i picks up tile e + i NE's.
     int meta_kp = 0;
     if constexpr (META) {
       const int n_mine_tiles = e < my_tiles ? (my_tiles - 1 - e) / NE + 1 : 0;
-      for (int i = 0; i < min(n_mine_tiles, 32); ++i) {
-        const int kp = meta_keep<D>(a, e + i * NE, q_cached, s_q, s_qn, lane);
-        if (lane == i) meta_kp = kp;
+      if (!mbar_wait(&kpbar, 0)) {
+        s_abort = 1;
+        if (lane == 0) atomicExch(&g_score_status, 1);
       }
+      if (lane < min(n_mine_tiles, 32)) meta_kp = s_kpre[e + lane * NE];
     }
     // Outputs and the workspace are written from here on.
     pdl_wait();
@@ -1084,6 +1090,18 @@ score_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
   // bank groups.  Lane (matrix lane / 8, row lane % 8) addresses:
   const uint32_t lane_off = (uint32_t)hb * (kSlabB / 2) + (uint32_t)((lane >> 3) * 8 + (lane & 7)) * 128 +
                             (uint32_t)((ch ^ (lane & 7)) << 4);
+  if constexpr (META) {
+    // Keep decisions of this CTA's tiles < kMetaPre, one warp per tile (the
+    // compute warps are otherwise idle until the attention phase), handed to
+    // the epilogue warps through s_kpre; the queries are read from global
+    // memory (their shared-memory copy is being staged meanwhile).
+    for (int t = warp; t < min(my_tiles, kMetaPre); t += kW) {
+      const int kp = meta_keep<D>(a, t, false, nullptr, nullptr, lane);
+      if (lane == 0) s_kpre[t] = kp;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&kpbar);
+  }
   for (int tile = 0; tile < (META ? 0 : my_tiles); ++tile) {
     const int tb = tile % NBUF;
     if (tile >= NBUF && !__all_sync(0xffffffffu, mbar_wait(&tempty[tb], (tile / NBUF - 1) & 1))) {
