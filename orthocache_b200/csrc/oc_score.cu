@@ -624,9 +624,9 @@ __device__ __forceinline__ int meta_keep(const ScoreArgs& a, int tile, bool q_ca
   const float resid_scale = sqrtf(__ldg(a.e_ac + cell));
   const float z = __ldg(a.zeta + cell);
   const float* dcp = a.dc + cell * D;
-  float dv[8];
+  float dv[8], nv[8];
 #pragma unroll
-  for (int r = 0; r < 8; ++r) dv[r] = 0.f;
+  for (int r = 0; r < 8; ++r) dv[r] = nv[r] = 0.f;
 #pragma unroll
   for (int c = lane; c < D; c += 32) {
     const float mean = __ldg(dcp + c) / kNorm;
@@ -635,24 +635,20 @@ __device__ __forceinline__ int meta_keep(const ScoreArgs& a, int tile, bool q_ca
       if (r < rows) {
         const int s = r / a.G, gq = r - s * a.G;
         const size_t qrow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + gq;
-        dv[r] = fmaf(__bfloat162float(qb[qrow * D + c]), mean, dv[r]);
+        const float qv = __bfloat162float(qb[qrow * D + c]);
+        dv[r] = fmaf(qv, mean, dv[r]);
+        nv[r] = fmaf(qv, qv, nv[r]);  // squared norms on the same loads (uncached queries)
       }
   }
   const float dot = transpose_sum8(dv, lane);
+  const float nrm_lanes = q_cached ? 0.f : transpose_sum8(nv, lane);
   const int r = lane >> 2;
   float bound = -INFINITY;
   if (r < rows) {
     const int s = r / a.G, gq = r - s * a.G;
     const size_t qrow = ((size_t)b * a.Sq + s) * a.Hq + (size_t)h * a.G + gq;
     float nrm = 0.f;
-    if (q_cached) {
-      nrm = s_qn[qrow];
-    } else {
-      for (int c = 0; c < D; ++c) {
-        const float qv = __bfloat162float(qb[qrow * D + c]);
-        nrm = fmaf(qv, qv, nrm);
-      }
-    }
+    nrm = q_cached ? s_qn[qrow] : nrm_lanes;
     const float sqrt_d = sqrtf((float)D);
     bound = dot / sqrt_d + (sqrtf(nrm) * resid_scale) / sqrt_d;
   }
