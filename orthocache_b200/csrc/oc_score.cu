@@ -2193,19 +2193,25 @@ struct BtSmem {
 };
 constexpr size_t kBtSmemBytes = sizeof(BtSmem) + 1024;
 
-// 16 consecutive fp32 columns of this thread's lane, loaded and waited for in
-// one asm statement.
-__device__ __forceinline__ void tmem_ld16_wait(uint32_t taddr, float* v) {
-  uint32_t r[16];
+// 16 consecutive fp32 columns of this thread's lane, loaded without waiting:
+// the registers are valid only after tmem_ld_wait().
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
+}
+
+// Waits for this thread's outstanding tensor-memory loads, then passes each of
+// the n loaded registers through an empty volatile statement after the wait,
+// so that no use of them can be scheduled before it.
+template <int n>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < n; ++i) asm volatile("" : "+r"(r[i]));
 }
 
 __global__ void __launch_bounds__(kBtThreads, 1)
@@ -2314,7 +2320,7 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
       if (__syncthreads_or(!got)) { ok = false; break; }
       {
         // partial squared norm of row `row` over this column group's 32 channels
-        float nrm = 0.f;
+        float nrm4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           const int c = cg * 4 + c4, kb = c >> 3, cl = c & 7;
@@ -2324,11 +2330,11 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float lo = __uint_as_float(u[e] << 16), hi = __uint_as_float(u[e] & 0xffff0000u);
-            nrm = fmaf(lo, lo, nrm);
-            nrm = fmaf(hi, hi, nrm);
+            nrm4[e] = fmaf(lo, lo, nrm4[e]);
+            nrm4[e] = fmaf(hi, hi, nrm4[e]);
           }
         }
-        sm.s_nrm[t & 1][cg][row] = nrm;
+        sm.s_nrm[t & 1][cg][row] = (nrm4[0] + nrm4[1]) + (nrm4[2] + nrm4[3]);
       }
       if (tid == 0) {
         tc_fence_after();
@@ -2356,14 +2362,19 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
     const float rn = sqrtf((sm.s_nrm[e & 1][0][row] + sm.s_nrm[e & 1][1][row]) +
                            (sm.s_nrm[e & 1][2][row] + sm.s_nrm[e & 1][3][row]));
     const uint32_t t_acc = t_row + (uint32_t)(e & 1) * 256;
-    float x0[kBtCols], x1[kBtCols], x2[kBtCols];
-    tmem_ld16_wait(t_acc, x0);
-    tmem_ld16_wait(t_acc + kBtBlk, x1);
-    tmem_ld16_wait(t_acc + 2 * kBtBlk, x2);
+    // the three partial-dot column ranges of this row: three loads in
+    // flight, one wait
+    uint32_t xr[3 * kBtCols];
+    tmem_ld16(t_acc, xr);
+    tmem_ld16(t_acc + kBtBlk, xr + kBtCols);
+    tmem_ld16(t_acc + 2 * kBtBlk, xr + 2 * kBtCols);
+    tmem_ld_wait<3 * kBtCols>(xr);
 #pragma unroll
     for (int i = 0; i < kBtCols; ++i) {
       if (valid && rs[i] >= 0.f) {
-        const float bound = fmaf(rn, rs[i], x2[i] + x1[i] + x0[i]) * inv_sqrt_d;
+        const float x0 = __uint_as_float(xr[i]), x1 = __uint_as_float(xr[kBtCols + i]),
+                    x2 = __uint_as_float(xr[2 * kBtCols + i]);
+        const float bound = fmaf(rn, rs[i], x2 + x1 + x0) * inv_sqrt_d;
         if (bounds) bounds[(((size_t)b * Sq + s) * nb + j0 + cg * kBtCols + i) * Hq + hq] = bound;
         rmax[i] = fmaxf(rmax[i], bound);
       }
