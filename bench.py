@@ -435,6 +435,58 @@ def e2e_pipelined(eng, layers, q_host, Ke):
     return e0.elapsed_time(e1) / Ke
 
 
+def e2e_prefill_pipelined(step_fn, q_host, out, n):
+    """End to end with host buffers for the chunked prefill: step s reads its
+    queries from q_host[s % len(q_host)] (pinned) and its output is copied
+    back to pinned host memory.  The up-copies run on one stream and the
+    down-copies on another (PCIe carries both directions at once), both
+    double-buffered against the compute stream.  Returns ms per step (CUDA
+    events on the compute stream, after every copy of the timed steps)."""
+    import torch
+    cs = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    q_dev = [torch.empty(tuple(q_host[0].shape), dtype=q_host[0].dtype, device=out.device) for _ in range(2)]
+    o_dev = [torch.empty_like(out) for _ in range(2)]
+    o_host = [torch.empty(tuple(out.shape), dtype=out.dtype).pin_memory() for _ in range(2)]
+    ev = lambda: torch.cuda.Event()
+    ev_q, ev_k, ev_o = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+    nh = len(q_host)
+
+    def run(n):
+        with torch.cuda.stream(up):
+            up.wait_stream(cs)
+            q_dev[0].copy_(q_host[0], non_blocking=True)
+            ev_q[0].record(up)
+        for s in range(n):
+            b = s & 1
+            cs.wait_event(ev_q[b])
+            if s >= 2:
+                cs.wait_event(ev_o[b])  # step s-2's output has left o_dev[b]
+            step_fn(s, q_dev[b], o_dev[b])
+            ev_k[b].record(cs)
+            if s + 1 < n:
+                with torch.cuda.stream(up):
+                    if s >= 1:
+                        up.wait_event(ev_k[b ^ 1])  # step s-1 has read q_dev[b ^ 1]
+                    q_dev[b ^ 1].copy_(q_host[(s + 1) % nh], non_blocking=True)
+                    ev_q[b ^ 1].record(up)
+            with torch.cuda.stream(down):
+                down.wait_event(ev_k[b])
+                o_host[b].copy_(o_dev[b], non_blocking=True)
+                ev_o[b].record(down)
+        cs.wait_stream(up)
+        cs.wait_stream(down)
+
+    run(4)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cs)
+    run(n)
+    e1.record(cs)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n, o_host[(n - 1) & 1]
+
+
 def metadata_decode_time(eng, layers, K):
     """Decode layers over write-time metadata: the average layer time in a
     CUDA-graph replay of LAYERS layers and its roofline."""
@@ -865,7 +917,7 @@ def run_prefill(args, rank, world, local_rank):
     e_ac, zeta, bmax = (torch.empty((P_B, nb, HKV), **f32) for _ in range(3))
     cells = nb * HKV
 
-    def score(L):
+    def score(L, q=None):
         # one pass over all keys for the query-independent block metadata
         # (DC, E_AC, zeta), the bounds of all 8192 query rows per KV head as a
         # tiled GEMM, then the two gates with each batch row's own τ (the
@@ -873,7 +925,8 @@ def run_prefill(args, rank, world, local_rank):
         # one by one)
         _lib.call("oc_block_metadata", L.k.data_ptr(), 1, P_B, P_S, HKV, D, dc.data_ptr(), e_ac.data_ptr(),
                   zeta.data_ptr(), st())
-        _lib.call("oc_score_from_metadata", dc.data_ptr(), e_ac.data_ptr(), zeta.data_ptr(), L.q.data_ptr(), 1, P_B,
+        q = L.q if q is None else q
+        _lib.call("oc_score_from_metadata", dc.data_ptr(), e_ac.data_ptr(), zeta.data_ptr(), q.data_ptr(), 1, P_B,
                   nb, HKV, D, P_SQ, HQ, -math.inf, ZETA_MAX, bmax.data_ptr(), None, None, st())
         for b in range(P_B):
             _lib.call("oc_apply_gates", bmax.data_ptr() + 4 * b * cells, zeta.data_ptr() + 4 * b * cells, cells,
@@ -882,10 +935,11 @@ def run_prefill(args, rank, world, local_rank):
     def compact():
         _lib.call("oc_stream_compact", keep.data_ptr(), P_B, nb, HKV, perm.data_ptr(), count.data_ptr(), st())
 
-    def attend(L, q=None):
+    def attend(L, q=None, o=None):
         q = L.q if q is None else q
+        o = out if o is None else o
         _lib.call("oc_prefill_attention", q.data_ptr(), L.k.data_ptr(), L.v.data_ptr(), 1, perm.data_ptr(), nb, 0,
-                  count.data_ptr(), 1, 0, P_B, P_SQ, HQ, HKV, D, P_S, 512, nb, out.data_ptr(), 1, st())
+                  count.data_ptr(), 1, 0, P_B, P_SQ, HQ, HKV, D, P_S, 512, nb, o.data_ptr(), 1, st())
 
     def step(L, q=None):
         score(L)
@@ -924,22 +978,26 @@ def run_prefill(args, rank, world, local_rank):
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    # end to end: the chunk's queries from pinned host memory, the output back
+    # end to end: the chunk's queries from pinned host memory, the output
+    # back, through the same C-ABI calls; copies on two streams (up, down),
+    # double-buffered, so that step i+1's queries go up and step i's output
+    # comes down while step i+1 computes (a chunked-prefill serving loop)
     q_host = [L.q.cpu().pin_memory() for L in layers]
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_dev = torch.empty_like(layers[0].q)
     Ke = max(4, min(K, 50))
 
-    def e2e_step(i):
-        q_dev.copy_(q_host[i % P_LAYERS], non_blocking=True)
+    def e2e_step(i, q_dev, o_dev):
         L = layers[i % P_LAYERS]
-        score(L)
+        score(L, q_dev)
         compact()
-        attend(L, q_dev)
-        out_host.copy_(out, non_blocking=True)
+        attend(L, q_dev, o_dev)
 
-    e2e_step(0)
-    e2e_ms = timed(e2e_step, Ke)
+    e2e_ms, o_last = e2e_prefill_pipelined(e2e_step, q_host, out, Ke)
+    # the last step's output as it reached the host equals the same layer run
+    # directly on the device (no buffer was overwritten while in flight)
+    step(layers[(Ke - 1) % P_LAYERS])
+    torch.cuda.synchronize()
+    if not torch.allclose(o_last.float(), out.cpu().float(), rtol=1e-2, atol=2e-2):
+        raise RuntimeError("config 2: pipelined end-to-end output differs from the direct run")
     if rank != 0:
         return
     kept = statistics.mean(statistics.mean(L.kept) for L in layers)
@@ -976,7 +1034,10 @@ def run_prefill(args, rank, world, local_rank):
         "cpu_baseline": None,
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms/layer", "h2d_bytes_per_step": P_B * rows_b,
                 "d2h_bytes_per_step": P_B * rows_b,
-                "note": "queries of the chunk from pinned host memory, attention output back; KV cache resident"},
+                "note": "public C-ABI calls per step; queries of the chunk from pinned host memory, attention "
+                        "output back to pinned host memory; copies on an up and a down stream, double-buffered "
+                        "(step i+1's queries go up and step i's output comes down while step i+1 computes); "
+                        "KV cache resident"},
         "gpu_launches": K * (1 + 3 + P_B + 1 + 1),
         "clocks": clk.summary(),
         "retained_blocks": kept,
