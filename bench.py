@@ -48,8 +48,9 @@ FALLBACK_HBM = 6650.0
 # this workload (75 % eviction): not measured by this script but taken from the
 # ncu capture summarised in profiles/decode_fused_config1.md (reported with
 # that source in the JSON line; null at other evictions).
-FUSED_TRAFFIC = 194310144
-FUSED_TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/decode_fused_config1.md"
+FUSED_TRAFFIC = 195485700
+FUSED_TRAFFIC_SOURCE = ("ncu dram__bytes.sum.per_second x gpu__time_duration.sum of one launch (3.693427 TB/s x "
+                        "52.928 us), profiles/decode_fused_config1.md")
 
 
 def parse():
