@@ -1608,9 +1608,14 @@ extern "C" int oc_decode_step_from_metadata(const void* q, const void* k, const 
                                             void* workspace, size_t workspace_bytes, oc_stream_t stream) {
   OC_REQUIRE(keep && perm && count && out, OC_ERR_NULL, "oc_decode_step_from_metadata: null output pointer");
   OC_REQUIRE(dc && e_ac && zeta, OC_ERR_NULL, "oc_decode_step_from_metadata: null metadata pointer");
-  OC_REQUIRE(seq_len % 512 == 0, OC_ERR_SHAPE, "oc_decode_step_from_metadata: seq_len %d not a multiple of 512",
-             seq_len);
+  OC_REQUIRE(seq_len >= 0 && seq_len % 512 == 0, OC_ERR_SHAPE,
+             "oc_decode_step_from_metadata: seq_len %d not a non-negative multiple of 512", seq_len);
   OC_REQUIRE(batch >= 1 && kv_heads >= 1, OC_ERR_SHAPE, "oc_decode_step_from_metadata: batch/kv_heads < 1");
+  OC_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, OC_ERR_SHAPE,
+             "oc_decode_step_from_metadata: head_dim %d not in {64,128,256}", head_dim);
+  OC_REQUIRE(q_len >= 1 && q_heads >= kv_heads && q_heads % kv_heads == 0, OC_ERR_SHAPE,
+             "oc_decode_step_from_metadata: q_heads %d must be a positive multiple of kv_heads %d (q_len %d)",
+             q_heads, kv_heads, q_len);
   const int nb = seq_len / 512;
   const size_t fused_bytes = oc::decode_fused_bytes(batch, seq_len, kv_heads);
   OC_REQUIRE(workspace && workspace_bytes >= fused_bytes, OC_ERR_CAPACITY,

@@ -62,3 +62,24 @@ def test_host_side_validation_without_gpu():
     rc = lib.oc_indirect_attention_noalloc(None, None, None, 1, None, 4, 0, None, 1, 0, 1, 1, 32, 8, 0,
                                            2048, 512, 4, ctypes.c_void_p(16), 1, None)
     assert rc == -2 and b"head_dim" in lib.oc_last_error()
+
+
+@pytest.mark.parametrize("seq_len,head_dim,q_heads,kv_heads,needle", [
+    (-512, 128, 32, 8, b"seq_len"),
+    (512, 0, 32, 8, b"head_dim"),
+    (512, 7, 32, 8, b"head_dim"),
+    (512, 128, 30, 8, b"q_heads"),
+    (512, 128, 32, 0, b"kv_heads"),
+])
+def test_decode_step_shape_errors_without_gpu(seq_len, head_dim, q_heads, kv_heads, needle):
+    """Both one-launch decode entry points reject a bad shape on the host with
+    OC_ERR_SHAPE before any launch (the pointers are never dereferenced)."""
+    from orthocache_b200 import _lib
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    rc = lib.oc_decode_step_from_metadata(p, p, p, 1, p, p, p, 1, 1, q_heads, kv_heads, head_dim, seq_len, 0.0, 5.0,
+                                          p, p, p, p, 1, p, 1 << 30, None)
+    assert rc == -2 and needle in lib.oc_last_error()
+    rc = lib.oc_decode_step(p, p, p, 1, 1, 1, q_heads, kv_heads, head_dim, seq_len, 0.0, 5.0, p, p, p, p, 1,
+                            p, 1 << 30, None)
+    assert rc == -2 and needle in lib.oc_last_error()
