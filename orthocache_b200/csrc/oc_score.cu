@@ -2369,14 +2369,25 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
     tmem_ld16(t_acc + kBtBlk, xr + kBtCols);
     tmem_ld16(t_acc + 2 * kBtBlk, xr + 2 * kBtCols);
     tmem_ld_wait<3 * kBtCols>(xr);
+    // rmax keeps the unscaled maximum; the 1/sqrt(D) scale is applied once
+    // per block at the end (rounding is monotonic, so the scaled maximum is
+    // the same float).  Columns of absent blocks (rs < 0) are never read.
+    if (valid) {
+      if (bounds) {
 #pragma unroll
-    for (int i = 0; i < kBtCols; ++i) {
-      if (valid && rs[i] >= 0.f) {
-        const float x0 = __uint_as_float(xr[i]), x1 = __uint_as_float(xr[kBtCols + i]),
-                    x2 = __uint_as_float(xr[2 * kBtCols + i]);
-        const float bound = fmaf(rn, rs[i], x2 + x1 + x0) * inv_sqrt_d;
-        if (bounds) bounds[(((size_t)b * Sq + s) * nb + j0 + cg * kBtCols + i) * Hq + hq] = bound;
-        rmax[i] = fmaxf(rmax[i], bound);
+        for (int i = 0; i < kBtCols; ++i) {
+          if (rs[i] >= 0.f) {
+            const float u = fmaf(rn, rs[i], __uint_as_float(xr[2 * kBtCols + i]) + __uint_as_float(xr[kBtCols + i]) +
+                                                __uint_as_float(xr[i]));
+            bounds[(((size_t)b * Sq + s) * nb + j0 + cg * kBtCols + i) * Hq + hq] = u * inv_sqrt_d;
+            rmax[i] = fmaxf(rmax[i], u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kBtCols; ++i)
+          rmax[i] = fmaxf(rmax[i], fmaf(rn, rs[i], __uint_as_float(xr[2 * kBtCols + i]) +
+                                                       __uint_as_float(xr[kBtCols + i]) + __uint_as_float(xr[i])));
       }
     }
     tc_fence_before();
@@ -2394,7 +2405,7 @@ meta_bound_tc_kernel(const __grid_constant__ CUtensorMap mq, const float* __rest
   __syncthreads();
   if (ok && tid < kBtBlk && j0 + tid < nb && sm.s_rs[tid] >= 0.f) {
     const float m = fmaxf(fmaxf(sm.s_max[0][tid], sm.s_max[1][tid]), fmaxf(sm.s_max[2][tid], sm.s_max[3][tid]));
-    atomicMax(&key[((size_t)b * nb + j0 + tid) * H + h], f2key(m));
+    atomicMax(&key[((size_t)b * nb + j0 + tid) * H + h], f2key(m * inv_sqrt_d));
   }
   if (warp == 0) {
     tc_fence_after();
