@@ -42,6 +42,10 @@ def test_metadata_cache_vs_oracle(nb, hq, hkv, d, sq, dtype):
     np.testing.assert_allclose(host(bmax), r0["bound_max"], rtol=1e-5, atol=1e-5)
     want = (r0["bound_max"] >= np.float32(tau)) & (r0["zeta"] <= np.float32(5.0))
     assert_mask_parity(host(keep), want, r0["zeta"], r0["bound_max"], tau, 5.0)
+    # without per-row bounds the maxima come from a separate fast path (scale
+    # applied once per block): the same floats and the same mask
+    keep2, bmax2 = cache.multiband_mask(q, tau, 5.0)
+    assert torch.equal(bmax2, bmax) and torch.equal(keep2, keep)
     # the same mask as the key-reading scorer
     sc = oc.score_blocks(k, q, tau=tau, zeta_max=5.0, want=("keep",))
     assert_mask_parity(host(keep), host(sc["keep"]), r0["zeta"], r0["bound_max"], tau, 5.0)
