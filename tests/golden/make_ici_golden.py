@@ -10,7 +10,7 @@ import json
 import os
 import sys
 
-ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ORTHOCACHE_REFERENCE", ".")
 spec = importlib.util.spec_from_file_location("ici", os.path.join(ref, "src/orthocache/ici_bandwidth_model.py"))
 R = importlib.util.module_from_spec(spec)
 spec.loader.exec_module(R)
